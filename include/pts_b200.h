@@ -1,0 +1,153 @@
+/*
+ * pts_b200.h -- C ABI of the B200 tree-verification library (libpts_b200.so).
+ *
+ * Plain pointers and sizes only.  Every device pointer must point to memory
+ * of the current CUDA device; every function enqueues its work on `stream`
+ * and returns without synchronising.  The library never allocates: buffers
+ * and workspaces belong to the caller.  Return value: PTS_OK (0) or one of
+ * the PTS_ERR_* codes below; pts_last_error() gives a message for the
+ * calling thread's last failure.
+ *
+ * Layouts (the reference's, parallel_tree_spec/src/parallel_tree_spec):
+ *   paged KV layer   [max_pages, 2, page_len, Hkv, D]   (NHD, K = 0, V = 1)
+ *                    flashinfer/cache_manager.py:55-72
+ *   KV pool          [L, max_pages, 2, page_len, Hkv, D]
+ *   queries / keys   [tokens, heads, D] contiguous      flashinfer/attention_wrapper.py:176-182
+ *   logits           [rows, V] bf16, row stride given   verification.py:139
+ *   trees            back-to-back per request, row_indptr[B+1]; parents are
+ *                    local indices (root = row 0 of its request, parent -1),
+ *                    BFS order (parent < child)         tree.py:145-159
+ */
+#ifndef PTS_B200_H
+#define PTS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* pts_stream_t; /* cudaStream_t */
+
+#define PTS_OK 0
+#define PTS_ERR_INVALID 1     /* bad argument (maps to ValueError)                      */
+#define PTS_ERR_CAPACITY 2    /* workspace too small or size above a stated maximum     */
+#define PTS_ERR_CUDA 3        /* a CUDA runtime call or launch failed                    */
+#define PTS_ERR_UNSUPPORTED 4 /* shape or option this build does not implement           */
+#define PTS_ERR_INDEX 5       /* index out of range (maps to IndexError)                */
+
+/* Largest tree (rows per request) the acceptance and attention kernels take. */
+#define PTS_MAX_TREE_NODES 1024
+
+const char* pts_last_error(void);
+int pts_version(void);
+
+/* ------------------------------------------------------------------ acceptance
+ * Fused acceptance: one pass over the bf16 logits computes, per row, the max,
+ * the fp32 sum of exp(x - max), and the argmax of the bf16-rounded softmax
+ * (first index on ties), then walks each request's tree on the device.
+ *
+ * Outputs per request b (out_stride = max entries per request >= its depth+1):
+ *   out_tokens[b*out_stride + i], out_hidden[b*out_stride + i]   i < n_out
+ *   out_counts[b*4 + {0,1,2,3}] = {n_out, total_len, accept_len, accepted_node}
+ * eos_token_id < 0 means "no EOS".
+ */
+size_t pts_accept_workspace_size(int num_rows, int vocab);
+
+/* Replaces verify_tree_exact + _verify_step_greedy + _sample_probs
+ * (verification.py:185-268, 58-77, 46-55). */
+int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                      const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                      int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
+                      int32_t* out_hidden, int32_t* out_counts, int out_stride, void* workspace,
+                      size_t workspace_bytes, pts_stream_t stream);
+
+/* Replaces verify_tree_traversal (verification.py:275-524) with the
+ * per-iteration torch.rand(1) draw (verification.py:396) taken from the
+ * Philox4x32-10 stream u(b, k) = (philox(key = seed, ctr = (k>>2, b,
+ * offset_lo, offset_hi))[k&3] >> 8) * 2^-24.  draft_probs[r] is node r's
+ * cumulative_probability (tree.py:30).  top_p < 1 restricts the target
+ * distribution to its nucleus (no counterpart in the reference);
+ * do_sample != 0 draws the bonus token from the accepted row's distribution
+ * with draw index 2*PTS_MAX_TREE_NODES instead of taking its argmax
+ * (verification.py:508-511). */
+int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                         const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                         int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                         float temperature, float top_p, int do_sample, uint64_t philox_seed,
+                         uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                         int32_t* out_counts, int out_stride, void* workspace,
+                         size_t workspace_bytes, pts_stream_t stream);
+
+/* ------------------------------------------------------------------ paged KV
+ * Per appended token t: batch_indices[t] = b and positions[t] = seq_lens[b] -
+ * (append_indptr[b+1] - append_indptr[b]) + (t - append_indptr[b]).
+ * Replaces flashinfer.get_batch_indices_positions as called by
+ * getKvCacheBatchPosition(mode="tree") (flashinfer/cache_manager.py:263-271),
+ * one append segment per request. */
+int pts_batch_positions(const int32_t* append_indptr, const int32_t* seq_lens, int batch,
+                        int num_tokens, int32_t* batch_indices, int32_t* positions,
+                        pts_stream_t stream);
+
+/* Scatter new K/V rows ([T, Hkv, D], token stride in elements) into one
+ * layer's pages.  Replaces flashinfer.append_paged_kv_cache
+ * (flashinfer/attention_wrapper.py:201-212).  elem_bytes = 2 (bf16/fp16) or 4. */
+int pts_kv_append(const void* k, const void* v, int64_t k_token_stride, int64_t v_token_stride,
+                  void* kv_layer, const int32_t* batch_indices, const int32_t* positions,
+                  const int32_t* page_indptr, const int32_t* page_indices, int num_tokens,
+                  int num_kv_heads, int head_dim, int page_len, int max_pages, int elem_bytes,
+                  pts_stream_t stream);
+
+/* KV compaction: for request b, slot offsets[b] + accepted[i] is copied to
+ * slot offsets[b] + i (i < accepted_indptr[b+1] - accepted_indptr[b]) in every
+ * layer, K and V, all reads before any write, slots mapped through the
+ * request's page table.  Replaces KvCachePool.reorder_cache_with_offset and
+ * RequestKvCache.reorder_cache_with_offset (flashinfer/cache_manager.py:103-140,
+ * 196-213); with page_indices = 0..max_pages-1 for every request it is the
+ * pool-level flat-slot form.  new_kv_len / new_last_page_len (nullable)
+ * receive offsets[b] + count and its last-page fill. */
+int pts_kv_compact(void* kv_pool, int num_layers, int max_pages, int page_len, int num_kv_heads,
+                   int head_dim, int elem_bytes, const int32_t* page_indptr,
+                   const int32_t* page_indices, const int32_t* accepted_indptr,
+                   const int32_t* accepted, const int32_t* offsets, int batch, int max_accepted,
+                   int32_t* new_kv_len, int32_t* new_last_page_len, pts_stream_t stream);
+
+/* ------------------------------------------------------------------ attention
+ * Ancestor bitmask of every tree row: bit j of row i's mask_words-word mask is
+ * set when node j of the same request is i itself or one of its ancestors.
+ * Replaces Tree.create_attention_mask (tree.py:167-194) for the tree block. */
+int pts_tree_mask_from_parents(const int32_t* parents, const int32_t* qo_indptr, int batch,
+                               int total_q, int mask_words, uint64_t* mask_bits,
+                               pts_stream_t stream);
+
+/* Pack a boolean custom mask [sum_b N_b * kv_len_b] (FlashInfer's flattened
+ * custom_mask, flashinfer/attention_wrapper.py:141) into tree bitmasks.
+ * Columns before kv_len_b - N_b must all be true; *bad_rows (device int,
+ * nullable) counts rows where they are not. */
+int pts_tree_mask_from_bool(const uint8_t* mask, const int32_t* qo_indptr, const int32_t* mask_indptr,
+                            const int32_t* kv_lens, int batch, int total_q, int mask_words,
+                            uint64_t* mask_bits, int32_t* bad_rows, pts_stream_t stream);
+
+/* Tree-masked paged attention, bf16 in / bf16 out, fp32 accumulation on the
+ * tcgen05 tensor cores.  Query row i of request b sees the request's KV slots
+ * [0, kv_len_b - N_b) (the prefix) and the tree slots kv_len_b - N_b + j whose
+ * bit j is set in its mask.  kv_len_b = (page_indptr[b+1]-page_indptr[b]-1) *
+ * page_len + last_page_len[b].  Replaces BatchPrefillWithPagedKVCacheWrapper
+ * plan/run with custom_mask, causal=False (flashinfer/attention_wrapper.py:
+ * 131-144, 250-252).  head_dim 128, page_len 16, Hq/Hkv = 4 in this build. */
+size_t pts_tree_attn_workspace_size(int batch, int total_q, int num_qo_heads, int head_dim,
+                                    int max_kv_len);
+int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                      const int32_t* page_indptr, const int32_t* page_indices,
+                      const int32_t* last_page_len, const uint64_t* mask_bits, int mask_words,
+                      void* out, int batch, int total_q, int max_qo_len, int max_kv_len,
+                      int num_qo_heads, int num_kv_heads, int head_dim, int page_len,
+                      int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
+                      pts_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PTS_B200_H */

@@ -1,0 +1,230 @@
+"""Device operations: torch tensors in, C-ABI calls out.
+
+Every function here validates shapes and dtypes, takes raw device pointers
+from CUDA tensors and launches on the current torch stream.  Nothing falls
+back to another implementation: a missing library or a non-CUDA tensor
+raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_WS: Dict[Tuple[int, str], torch.Tensor] = {}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if t.device.type != "cuda":
+            raise ValueError("tensors must be on a CUDA device (this path has no CPU implementation)")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        t = t.to(torch.int32)
+    if not t.is_contiguous():
+        t = t.contiguous()
+    return t
+
+
+def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
+    """A per-device, per-kind scratch buffer (256-byte aligned), grown on demand."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+# ------------------------------------------------------------------ acceptance
+def _accept_common(logits, row_indptr, parents, tokens):
+    if logits.dtype != torch.bfloat16 or logits.dim() != 2:
+        raise ValueError("logits must be a 2-D bf16 tensor [rows, vocab]")
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    dev = _need_cuda(logits, row_indptr, parents, tokens)
+    return dev, _i32(row_indptr, "row_indptr"), _i32(parents, "parents"), _i32(tokens, "tokens")
+
+
+def accept_greedy(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch.Tensor, tokens: torch.Tensor,
+                  eos_token_id: Optional[int] = None, max_nodes: Optional[int] = None,
+                  out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+    """Greedy acceptance (``verify_tree_exact``) for a batch of trees.
+
+    Returns (tokens [B, S] int32, hidden [B, S] int32, counts [B, 4] int32)
+    with counts = (n_out, total_len, accept_len, accepted_node).
+    """
+    dev, row_indptr, parents, tokens = _accept_common(logits, row_indptr, parents, tokens)
+    B = row_indptr.numel() - 1
+    R, V = logits.shape
+    mn = int(max_nodes) if max_nodes is not None else R
+    mn = min(mn, _lib.PTS_MAX_TREE_NODES)
+    if out is None:
+        ot = torch.empty(B, mn, dtype=torch.int32, device=dev)
+        oh = torch.empty(B, mn, dtype=torch.int32, device=dev)
+        oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    else:
+        ot, oh, oc = out
+    wsz = _lib.lib().pts_accept_workspace_size(R, V)
+    ws = workspace(dev, "accept", wsz)
+    _lib.call("pts_accept_greedy", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(), parents.data_ptr(),
+              tokens.data_ptr(), B, R, V, mn, -1 if eos_token_id is None else int(eos_token_id), ot.data_ptr(),
+              oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
+    return ot, oh, oc
+
+
+def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch.Tensor, tokens: torch.Tensor,
+                     draft_probs: torch.Tensor, eos_token_id: Optional[int] = None, temperature: float = 1.0,
+                     top_p: float = 1.0, do_sample: bool = False, seed: int = 0, offset: int = 0,
+                     max_nodes: Optional[int] = None,
+                     out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+    """Traversal verification (``verify_tree_traversal``) for a batch of trees;
+    the per-iteration uniform of request b is Philox stream (seed, offset, b)."""
+    dev, row_indptr, parents, tokens = _accept_common(logits, row_indptr, parents, tokens)
+    if draft_probs.dtype != torch.float32:
+        draft_probs = draft_probs.to(torch.float32)
+    draft_probs = draft_probs.contiguous()
+    _need_cuda(logits, draft_probs)
+    B = row_indptr.numel() - 1
+    R, V = logits.shape
+    mn = int(max_nodes) if max_nodes is not None else R
+    mn = min(mn, _lib.PTS_MAX_TREE_NODES)
+    if out is None:
+        ot = torch.empty(B, mn, dtype=torch.int32, device=dev)
+        oh = torch.empty(B, mn, dtype=torch.int32, device=dev)
+        oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    else:
+        ot, oh, oc = out
+    wsz = _lib.lib().pts_accept_workspace_size(R, V)
+    ws = workspace(dev, "accept", wsz)
+    _lib.call("pts_accept_traversal", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
+              parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr(), B, R, V, mn,
+              -1 if eos_token_id is None else int(eos_token_id), float(temperature), float(top_p),
+              1 if do_sample else 0, int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), ot.data_ptr(),
+              oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
+    return ot, oh, oc
+
+
+# ------------------------------------------------------------------ paged KV
+def batch_positions(append_indptr: torch.Tensor, seq_lens: torch.Tensor, num_tokens: int):
+    dev = _need_cuda(append_indptr, seq_lens)
+    append_indptr, seq_lens = _i32(append_indptr, "append_indptr"), _i32(seq_lens, "seq_lens")
+    bi = torch.empty(num_tokens, dtype=torch.int32, device=dev)
+    pos = torch.empty(num_tokens, dtype=torch.int32, device=dev)
+    _lib.call("pts_batch_positions", append_indptr.data_ptr(), seq_lens.data_ptr(), append_indptr.numel() - 1,
+              num_tokens, bi.data_ptr(), pos.data_ptr(), _stream(dev))
+    return bi, pos
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, kv_layer: torch.Tensor, batch_indices: torch.Tensor,
+              positions: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor) -> None:
+    """Scatter k/v [T, Hkv, D] into one layer [max_pages, 2, page_len, Hkv, D]."""
+    dev = _need_cuda(k, v, kv_layer, batch_indices, positions, page_indptr, page_indices)
+    if kv_layer.dim() != 5 or kv_layer.shape[1] != 2:
+        raise ValueError("kv_layer must be [max_pages, 2, page_len, Hkv, D]")
+    if not kv_layer.is_contiguous():
+        raise ValueError("kv_layer must be contiguous")
+    P, _, pl, H, D = kv_layer.shape
+    if k.dtype != kv_layer.dtype or v.dtype != kv_layer.dtype:
+        raise ValueError("k/v dtype must match the cache dtype")
+    k = k.reshape(k.shape[0], H * D) if k.stride(-1) == 1 and k[0].is_contiguous() else k.contiguous().reshape(-1, H * D)
+    v = v.reshape(v.shape[0], H * D) if v.stride(-1) == 1 and v[0].is_contiguous() else v.contiguous().reshape(-1, H * D)
+    _lib.call("pts_kv_append", k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), kv_layer.data_ptr(),
+              _i32(batch_indices, "bi").data_ptr(), _i32(positions, "pos").data_ptr(),
+              _i32(page_indptr, "indptr").data_ptr(), _i32(page_indices, "indices").data_ptr(), k.shape[0], H, D, pl,
+              P, kv_layer.element_size(), _stream(dev))
+
+
+def kv_compact(pool: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor,
+               accepted_indptr: torch.Tensor, accepted: torch.Tensor, offsets: torch.Tensor, max_accepted: int,
+               new_kv_len: Optional[torch.Tensor] = None, new_last_page_len: Optional[torch.Tensor] = None) -> None:
+    """Copy slot offsets[b]+accepted[i] -> offsets[b]+i in every layer of
+    ``pool`` [L, max_pages, 2, page_len, Hkv, D]."""
+    dev = _need_cuda(pool, page_indptr, page_indices, accepted_indptr, accepted, offsets)
+    if pool.dim() != 6 or pool.shape[2] != 2 or not pool.is_contiguous():
+        raise ValueError("pool must be a contiguous [L, max_pages, 2, page_len, Hkv, D] tensor")
+    L, P, _, pl, H, D = pool.shape
+    B = accepted_indptr.numel() - 1
+    _lib.call("pts_kv_compact", pool.data_ptr(), L, P, pl, H, D, pool.element_size(),
+              _i32(page_indptr, "a").data_ptr(), _i32(page_indices, "b").data_ptr(),
+              _i32(accepted_indptr, "c").data_ptr(), _i32(accepted, "d").data_ptr(), _i32(offsets, "e").data_ptr(),
+              B, int(max_accepted), new_kv_len.data_ptr() if new_kv_len is not None else None,
+              new_last_page_len.data_ptr() if new_last_page_len is not None else None, _stream(dev))
+
+
+# ------------------------------------------------------------------ attention
+def mask_words_for(max_nodes: int) -> int:
+    return max(1, math.ceil(max_nodes / 64))
+
+
+def tree_mask_from_parents(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_words: int) -> torch.Tensor:
+    dev = _need_cuda(parents, qo_indptr)
+    parents, qo_indptr = _i32(parents, "parents"), _i32(qo_indptr, "qo_indptr")
+    T = parents.numel()
+    bits = torch.empty(T, mask_words, dtype=torch.int64, device=dev)
+    _lib.call("pts_tree_mask_from_parents", parents.data_ptr(), qo_indptr.data_ptr(), qo_indptr.numel() - 1, T,
+              mask_words, bits.data_ptr(), _stream(dev))
+    return bits
+
+
+def tree_mask_from_bool(mask: torch.Tensor, qo_indptr: torch.Tensor, mask_indptr: torch.Tensor,
+                        kv_lens: torch.Tensor, mask_words: int, bad_rows: Optional[torch.Tensor] = None):
+    dev = _need_cuda(mask, qo_indptr, mask_indptr, kv_lens)
+    if mask.dtype != torch.bool:
+        mask = mask.to(torch.bool)
+    mask = mask.contiguous()
+    qo_indptr = _i32(qo_indptr, "qo")
+    T = int(qo_indptr[-1].item()) if bad_rows is None else None
+    raise_if_bad = bad_rows is None
+    if bad_rows is None:
+        bad_rows = torch.zeros(1, dtype=torch.int32, device=dev)
+    total_q = T if T is not None else None
+    if total_q is None:
+        total_q = int(qo_indptr[-1].item())
+    bits = torch.empty(total_q, mask_words, dtype=torch.int64, device=dev)
+    _lib.call("pts_tree_mask_from_bool", mask.data_ptr(), qo_indptr.data_ptr(), _i32(mask_indptr, "mi").data_ptr(),
+              _i32(kv_lens, "kl").data_ptr(), qo_indptr.numel() - 1, total_q, mask_words, bits.data_ptr(),
+              bad_rows.data_ptr(), _stream(dev))
+    if raise_if_bad and int(bad_rows.item()) != 0:
+        raise ValueError("custom mask is not a tree mask: a prefix column is masked out")
+    return bits
+
+
+def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Tensor, page_indptr: torch.Tensor,
+                   page_indices: torch.Tensor, last_page_len: torch.Tensor, mask_bits: torch.Tensor,
+                   max_qo_len: int, max_kv_len: int, sm_scale: Optional[float] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Tree-masked paged attention: q [T, Hq, D] bf16, kv_layer [P, 2, 16, Hkv, D] bf16."""
+    dev = _need_cuda(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len, mask_bits)
+    if q.dtype != torch.bfloat16 or kv_layer.dtype != torch.bfloat16:
+        raise ValueError("tree attention takes bf16 queries and cache")
+    if not q.is_contiguous() or not kv_layer.is_contiguous():
+        raise ValueError("q and kv_layer must be contiguous")
+    T, Hq, D = q.shape
+    P, _, pl, Hkv, D2 = kv_layer.shape
+    if D2 != D:
+        raise ValueError("head_dim mismatch between q and cache")
+    B = qo_indptr.numel() - 1
+    if out is None:
+        out = torch.empty_like(q)
+    scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(D)
+    wsz = _lib.lib().pts_tree_attn_workspace_size(B, T, Hq, D, int(max_kv_len))
+    ws = workspace(dev, "attn", max(wsz, 256))
+    _lib.call("pts_tree_attn_run", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
+              _i32(page_indptr, "pi").data_ptr(), _i32(page_indices, "px").data_ptr(),
+              _i32(last_page_len, "lp").data_ptr(), mask_bits.data_ptr(), mask_bits.shape[1], out.data_ptr(), B, T,
+              int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
+    return out

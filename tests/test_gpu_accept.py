@@ -1,0 +1,150 @@
+"""GPU parity: fused acceptance kernel vs the reference's golden outputs and
+the oracle.  Accepted tokens, hidden indices and counts must be bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import accept as acc
+from oracle.philox import UniformStream
+from parallel_tree_spec_b200 import kernels as K
+from parallel_tree_spec_b200 import workload as wl
+from tests.golden_inputs import checked_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def bf16(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+def run_batch(trees, logits_bits, method, eos=None, T=1.0, seed=0, offset=0):
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    x = bf16(np.concatenate(logits_bits, 0)).to(DEV)
+    args = (x, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV), torch.from_numpy(tok).to(DEV))
+    if method == "exact":
+        ot, oh, oc = K.accept_greedy(*args, eos_token_id=eos)
+    else:
+        ot, oh, oc = K.accept_traversal(*args, torch.from_numpy(dp).to(DEV), eos_token_id=eos, temperature=T,
+                                        seed=seed, offset=offset)
+    ot, oh, oc = ot.cpu().numpy(), oh.cpu().numpy(), oc.cpu().numpy()
+    res = []
+    for b in range(len(trees)):
+        n = int(oc[b, 0])
+        res.append(dict(tokens=ot[b, :n].tolist(), hidden=oh[b, :n].tolist(), total_len=int(oc[b, 1]),
+                        accept_len=int(oc[b, 2]), node=int(oc[b, 3])))
+    return res
+
+
+def filler(vocab, rng):
+    t = wl.make_tree(rng, 0, 0, vocab)
+    return t, wl.make_logits(rng, t, vocab)
+
+
+def test_golden_acceptance_cases(accept_golden):
+    """Every golden case, placed at its Philox request index in a batch padded
+    with root-only trees."""
+    rng = np.random.default_rng(0)
+    for rec in accept_golden:
+        c = rec["case"]
+        t, x = checked_inputs(rec)
+        req = c.get("request", 0) if c["method"] == "traversal" else 0
+        trees, logits = [], []
+        for _ in range(req):
+            ft, fx = filler(c["vocab"], rng)
+            trees.append(ft)
+            logits.append(fx)
+        trees.append(t)
+        logits.append(x)
+        out = run_batch(trees, logits, c["method"], eos=c.get("eos_value"), T=c.get("temperature", 1.0),
+                        seed=c.get("philox_seed", 0), offset=c.get("philox_offset", 0))[req]
+        assert out["tokens"] == rec["tokens"], c
+        assert out["hidden"] == rec["hidden"], c
+        assert (out["total_len"], out["accept_len"]) == (rec["total_len"], rec["accept_len"]), c
+
+
+@pytest.mark.parametrize("method,T,plant", [("exact", 1.0, 0.7), ("exact", 1.0, 0.0), ("traversal", 1.0, 1.0),
+                                            ("traversal", 0.8, 1.0), ("traversal", 1.0, 0.0)])
+def test_batched_full_vocab_vs_oracle(method, T, plant):
+    """Benchmark shape: 16 trees of 65 rows over a 128256 vocabulary."""
+    rng = np.random.default_rng(11 + int(plant * 10) + int(T * 100))
+    V = 128256
+    trees = [wl.make_tree(rng, 8, 8, V) for _ in range(16)]
+    logits = [wl.make_logits(rng, t, V, plant=plant, soft=(method == "traversal")) for t in trees]
+    seed, offset = 1234, 77
+    out = run_batch(trees, logits, method, T=T, seed=seed, offset=offset)
+    accepted = 0
+    for b, (t, x) in enumerate(zip(trees, logits)):
+        am, p = acc.row_stats(x, T if method == "traversal" else 1.0)
+        if method == "exact":
+            s, h, tl, al = acc.greedy_walk(t.parents, t.tokens, am)
+        else:
+            mb = acc.mb_from_probs(t.parents, t.tokens, p)
+            s, h, tl, al, _ = acc.traversal_walk(t.parents, t.tokens, t.draft_probs, mb, am,
+                                                 UniformStream(seed, offset, b))
+        assert out[b]["tokens"] == s and out[b]["hidden"] == h, (b, out[b], s, h)
+        assert (out[b]["total_len"], out[b]["accept_len"]) == (tl, al)
+        accepted += al
+    if plant > 0:
+        assert accepted > 0
+
+
+def test_near_tie_rows_vs_oracle():
+    """Tiny logits: many distinct values round to the same bf16 probability,
+    so the argmax must come from the rounded probabilities (the rescan path)."""
+    rng = np.random.default_rng(5)
+    V = 50000
+    trees = [wl.make_tree(rng, 4, 3, V) for _ in range(6)]
+    logits = [wl.make_logits(rng, t, V, sigma=0.01) for t in trees]
+    out = run_batch(trees, logits, "exact")
+    n_tie_rows = 0
+    for b, (t, x) in enumerate(zip(trees, logits)):
+        am, p = acc.row_stats(x)
+        raw = np.argmax(acc.bf16_bits_to_f32(x), axis=-1)
+        n_tie_rows += int(np.count_nonzero(raw != am))
+        s, h, tl, al = acc.greedy_walk(t.parents, t.tokens, am)
+        assert out[b]["tokens"] == s and out[b]["hidden"] == h
+    assert n_tie_rows > 0          # the case really exercises rounded-probability ties
+
+
+def test_unaligned_vocab_and_stride():
+    """Odd vocabulary (scalar load path) and a padded row stride."""
+    rng = np.random.default_rng(9)
+    V = 1001
+    trees = [wl.make_tree(rng, 3, 3, V) for _ in range(3)]
+    logits = [wl.make_logits(rng, t, V, plant=0.8) for t in trees]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    x = np.concatenate(logits, 0)
+    padded = np.zeros((x.shape[0], 1040), np.uint16)
+    padded[:, :V] = x
+    xt = bf16(padded).to(DEV)[:, :V]
+    ot, oh, oc = K.accept_greedy(xt, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV),
+                                 torch.from_numpy(tok).to(DEV))
+    oc = oc.cpu().numpy()
+    for b, (t, xb) in enumerate(zip(trees, logits)):
+        am, _ = acc.row_stats(xb)
+        s, h, tl, al = acc.greedy_walk(t.parents, t.tokens, am)
+        n = int(oc[b, 0])
+        assert ot[b, :n].cpu().tolist() == s and oh[b, :n].cpu().tolist() == h
+
+
+def test_repeated_calls_reuse_workspace():
+    """Counters in the shared workspace are reset on every call."""
+    rng = np.random.default_rng(2)
+    V = 4096
+    trees = [wl.make_tree(rng, 4, 4, V) for _ in range(4)]
+    logits = [wl.make_logits(rng, t, V, plant=0.9) for t in trees]
+    a = run_batch(trees, logits, "exact")
+    for _ in range(3):
+        assert run_batch(trees, logits, "exact") == a
+
+
+def test_bad_arguments_raise():
+    x = torch.zeros(4, 16, dtype=torch.bfloat16, device=DEV)
+    ind = torch.tensor([0, 4], dtype=torch.int32, device=DEV)
+    par = torch.tensor([-1, 0, 0, 1], dtype=torch.int32, device=DEV)
+    tok = torch.tensor([0, 1, 2, 3], dtype=torch.int32, device=DEV)
+    with pytest.raises(ValueError):
+        K.accept_traversal(x, ind, par, tok, torch.ones(4, device=DEV), temperature=0.0)
+    with pytest.raises(ValueError):
+        K.accept_greedy(x.cpu(), ind, par, tok)

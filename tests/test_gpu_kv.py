@@ -1,0 +1,143 @@
+"""GPU parity: paged-KV append, batch positions, compaction and mask packing."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as att
+from oracle import kv as okv
+from parallel_tree_spec_b200 import kernels as K
+from parallel_tree_spec_b200 import workload as wl
+from tests.conftest import GOLDEN
+from tests.golden_inputs import sha1
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def to_dev_bits(a: np.ndarray) -> torch.Tensor:
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16).copy()).to(DEV)
+    return torch.from_numpy(a.view(np.int32).copy()).to(DEV)
+
+
+def from_dev_bits(t: torch.Tensor, dtype) -> np.ndarray:
+    return t.cpu().numpy().view(dtype)
+
+
+@pytest.mark.parametrize("flat", [False, True])
+def test_compaction_matches_reference_reorder(reorder_golden, flat):
+    for i, rec in enumerate(reorder_golden):
+        before = np.load(os.path.join(GOLDEN, f"reorder_{i}_before.npy"))
+        pool = to_dev_bits(before)
+        L, P, _, pl, H, D = before.shape
+        if flat:      # pool-level form: flat physical slots (identity page table)
+            pages = list(range(P))
+        else:         # request-level form: the request's page table
+            pages = rec["pages_before"]
+        path = rec["path"]
+        K.kv_compact(pool, torch.tensor([0, len(pages)], dtype=torch.int32, device=DEV),
+                     torch.tensor(pages, dtype=torch.int32, device=DEV),
+                     torch.tensor([0, len(path)], dtype=torch.int32, device=DEV),
+                     torch.tensor(path, dtype=torch.int32, device=DEV),
+                     torch.tensor([rec["offset"] - 1], dtype=torch.int32, device=DEV), len(path))
+        assert sha1(from_dev_bits(pool, before.dtype)) == rec["sha1_after"], i
+
+
+def test_compaction_batched_page_tables_vs_oracle():
+    rng = np.random.default_rng(4)
+    L, P, pl, H, D = 3, 64, 16, 8, 128
+    pool = rng.integers(0, 2 ** 16, size=(L, P, 2, pl, H, D), dtype=np.uint16)
+    perm = rng.permutation(P).tolist()
+    tables, paths, offs, lens = [], [], [], []
+    cur = 0
+    for b in range(5):
+        kvl = int(rng.integers(40, 120))
+        npg = (kvl + pl - 1) // pl
+        tables.append(perm[cur:cur + npg])
+        cur += npg
+        n_tree = 20
+        off = kvl - n_tree
+        path = [0] + sorted(rng.choice(np.arange(1, n_tree), size=int(rng.integers(0, 6)), replace=False).tolist())
+        if b % 2:
+            path = path + [path[-1]]
+        paths.append(path)
+        offs.append(off)
+        lens.append(kvl)
+    exp = pool.copy()
+    for tb, pth, off, kvl in zip(tables, paths, offs, lens):
+        okv.request_reorder(exp, tb, kvl, pth, off + 1)
+    dpool = to_dev_bits(pool)
+    pind = np.cumsum([0] + [len(t) for t in tables]).astype(np.int32)
+    aind = np.cumsum([0] + [len(p) for p in paths]).astype(np.int32)
+    nkv = torch.empty(5, dtype=torch.int32, device=DEV)
+    nlast = torch.empty(5, dtype=torch.int32, device=DEV)
+    K.kv_compact(dpool, torch.from_numpy(pind).to(DEV), torch.tensor(sum(tables, []), dtype=torch.int32, device=DEV),
+                 torch.from_numpy(aind).to(DEV), torch.tensor(sum(paths, []), dtype=torch.int32, device=DEV),
+                 torch.tensor(offs, dtype=torch.int32, device=DEV), max(len(p) for p in paths), nkv, nlast)
+    assert np.array_equal(from_dev_bits(dpool, np.uint16), exp)
+    assert nkv.cpu().tolist() == [o + len(p) for o, p in zip(offs, paths)]
+    assert nlast.cpu().tolist() == [(o + len(p) - 1) % pl + 1 for o, p in zip(offs, paths)]
+
+
+def test_append_and_positions_vs_oracle():
+    rng = np.random.default_rng(8)
+    P, pl, H, D = 40, 16, 8, 128
+    layer = rng.integers(0, 2 ** 16, size=(P, 2, pl, H, D), dtype=np.uint16)
+    perm = rng.permutation(P).tolist()
+    kv_lens, n_app, tables = [], [], []
+    cur = 0
+    for b in range(4):
+        n = int(rng.integers(1, 30))
+        kvl = int(rng.integers(n, 100))
+        npg = (kvl + pl - 1) // pl
+        tables.append(perm[cur:cur + npg])
+        cur += npg
+        kv_lens.append(kvl)
+        n_app.append(n)
+    T = sum(n_app)
+    k = rng.integers(0, 2 ** 16, size=(T, H, D), dtype=np.uint16)
+    v = rng.integers(0, 2 ** 16, size=(T, H, D), dtype=np.uint16)
+    bi, pos = okv.batch_positions(kv_lens, n_app)
+    exp = layer.copy()
+    okv.append(exp, k, v, tables, bi, pos)
+    app_ind = torch.tensor(np.cumsum([0] + n_app), dtype=torch.int32, device=DEV)
+    dbi, dpos = K.batch_positions(app_ind, torch.tensor(kv_lens, dtype=torch.int32, device=DEV), T)
+    assert dbi.cpu().numpy().tolist() == bi.tolist() and dpos.cpu().numpy().tolist() == pos.tolist()
+    dl = to_dev_bits(layer).view(torch.bfloat16)
+    K.kv_append(to_dev_bits(k).view(torch.bfloat16), to_dev_bits(v).view(torch.bfloat16), dl, dbi, dpos,
+                torch.tensor(np.cumsum([0] + [len(t) for t in tables]), dtype=torch.int32, device=DEV),
+                torch.tensor(sum(tables, []), dtype=torch.int32, device=DEV))
+    assert np.array_equal(from_dev_bits(dl.view(torch.int16), np.uint16), exp)
+
+
+def test_tree_masks_vs_oracle():
+    rng = np.random.default_rng(1)
+    trees = [wl.make_tree(rng, w, d, 500) for (w, d) in [(8, 8), (3, 2), (0, 0), (16, 8), (1, 70)]]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    words = K.mask_words_for(max(t.size for t in trees))
+    bits = K.tree_mask_from_parents(torch.from_numpy(par).to(DEV), torch.from_numpy(indptr).to(DEV), words)
+    bits = bits.cpu().numpy().view(np.uint64)
+    prefixes = [5, 0, 3, 17, 1]
+    flat, mind, kvl = [], [0], []
+    for b, t in enumerate(trees):
+        a = att.ancestor_mask(t.parents)
+        rows = bits[indptr[b]:indptr[b + 1]]
+        got = np.array([[(rows[i, j // 64] >> np.uint64(j % 64)) & np.uint64(1) for j in range(t.size)]
+                        for i in range(t.size)], dtype=bool)
+        assert np.array_equal(got, a), b
+        m = att.tree_mask(t.parents, prefixes[b])
+        flat.append(m.reshape(-1))
+        mind.append(mind[-1] + m.size)
+        kvl.append(m.shape[1])
+    bits2 = K.tree_mask_from_bool(torch.from_numpy(np.concatenate(flat)).to(DEV), torch.from_numpy(indptr).to(DEV),
+                                  torch.tensor(mind, dtype=torch.int32, device=DEV),
+                                  torch.tensor(kvl, dtype=torch.int32, device=DEV), words)
+    assert np.array_equal(bits2.cpu().numpy().view(np.uint64), bits)
+    bad = np.concatenate(flat).copy()
+    bad[0] = False
+    with pytest.raises(ValueError):
+        K.tree_mask_from_bool(torch.from_numpy(bad).to(DEV), torch.from_numpy(indptr).to(DEV),
+                              torch.tensor(mind, dtype=torch.int32, device=DEV),
+                              torch.tensor(kvl, dtype=torch.int32, device=DEV), words)
