@@ -1,0 +1,503 @@
+#!/usr/bin/env python
+"""Tree-verification step benchmark (B200).
+
+One step = the verification of one batch of draft trees against the target's
+paged KV cache, for one attention layer, on one GPU:
+
+  1. tree-mask packing from the parent arrays          (pts_tree_mask_from_parents)
+  2. append positions of the tree tokens                (pts_batch_positions)
+  3. append of the tree tokens' K/V into the pages      (pts_kv_append)
+  4. tree-masked paged attention                        (pts_tree_attn_run)
+  5. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
+  6. compaction of each accepted path's KV              (pts_kv_compact)
+
+Workload (default): 16 requests, 4096-token prefix, 65-row trees (root + 8
+levels of 8), 32 query / 8 KV heads, head_dim 128, 16-token pages, logits
+[16*65, 128256] bf16 N(0, 3) with planted child tokens, traversal
+verification at temperature 1.0.  Seeded synthetic inputs; per step the KV
+(273 MB) and logits (267 MB) are each larger than L2.
+
+`--impl reference` times the CPU restatement of the same path (the reference
+is Python; its tree-verification path runs as the NumPy oracle on the host
+cores) on a bounded sample of the workload.
+
+For N > 1 the driver launches this under torchrun: every rank verifies its own
+batch (weak scaling, no collective on the data path); timing is the max over
+ranks of the device-timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "tree-verify steps/s and verified tree tokens/s per GPU at bs=16, 4k prefix"
+UNIT = "steps/s"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--mode", choices=["traversal", "greedy"], default="traversal")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--prefix", type=int, default=4096)
+    ap.add_argument("--width", type=int, default=8)
+    ap.add_argument("--depth", type=int, default=8)
+    ap.add_argument("--vocab", type=int, default=128256)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-sample-requests", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args(argv)
+
+
+def workload_name(a):
+    mode = f"traversal T={a.temperature}" if a.mode == "traversal" else "greedy"
+    n = 1 + a.width * a.depth
+    return (f"tree-verify step: B={a.batch} requests, prefix={a.prefix}, tree rows={n} (width {a.width}, depth "
+            f"{a.depth}), Hq={a.hq}, Hkv={a.hkv}, D=128, page=16, vocab={a.vocab}, {mode}")
+
+
+def algorithmic_bytes(a):
+    n = 1 + a.width * a.depth
+    kv_len = a.prefix + n
+    kv_read = a.batch * a.hkv * kv_len * 128 * 2 * 2
+    q_o = 2 * a.batch * n * a.hq * 128 * 2
+    append = a.batch * n * a.hkv * 128 * 2 * 2
+    logits = a.batch * n * a.vocab * 2
+    compact = 2 * a.batch * (a.depth + 1) * a.hkv * 128 * 2 * 2
+    return dict(attention=kv_read + q_o, kv_read=kv_read, q_o=q_o, append=append, accept=logits,
+                compact=compact, step=kv_read + q_o + append + logits + compact)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_table():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML in a thread."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int, period: float = 0.005):
+        self.index, self.period = index, period
+        self.samples = []
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self._ok:
+            self._t.join(timeout=1)
+
+    def summary(self, t0=None, t1=None):
+        s = [x for x in self.samples if (t0 is None or x[0] >= t0) and (t1 is None or x[0] <= t1)]
+        window = "timed region"
+        if not s:
+            s, window = self.samples, "around timed region"
+        if not s:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mask = 0
+        for x in s:
+            mask |= int(x[2])
+        reasons = [n for b, n in self.REASONS.items() if mask & b]
+        return {"sm_mhz": statistics.median([x[1] for x in s]), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(s), "window": window}
+
+
+# ---------------------------------------------------------------- workload
+def build_workload(a, device, seed):
+    import torch
+    from parallel_tree_spec_b200 import kernels as K
+    from parallel_tree_spec_b200 import workload as wl
+
+    rng = np.random.default_rng(seed + 2)
+    trees = [wl.make_tree(rng, a.width, a.depth, a.vocab) for _ in range(a.batch)]
+    n = trees[0].size
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    B, P, Hq, Hkv, D, pl = a.batch, a.prefix, a.hq, a.hkv, 128, 16
+    kv_len = P + n
+    pages_per = (kv_len + pl - 1) // pl
+    max_pages = B * pages_per + 16
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    layer = torch.empty(max_pages, 2, pl, Hkv, D, dtype=torch.bfloat16, device=device)
+    layer.normal_(0.0, 1.0 / math.sqrt(D), generator=g)
+    perm = torch.randperm(max_pages, generator=g, device=device)[: B * pages_per].to(torch.int32)
+    g.manual_seed(seed)
+    q = torch.randn(B * n, Hq, D, generator=g, device=device).to(torch.bfloat16)
+    k_new = (torch.randn(B * n, Hkv, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)
+    v_new = (torch.randn(B * n, Hkv, D, generator=g, device=device) / math.sqrt(D)).to(torch.bfloat16)
+    g.manual_seed(seed + 3)
+    logits = (torch.randn(B * n, a.vocab, generator=g, device=device) * 3.0).to(torch.bfloat16)
+    # plant: each row's children get logits near the row max (long accepted paths)
+    par_t = torch.from_numpy(par.astype(np.int64))
+    rows = torch.arange(B * n)
+    child = rows[par_t >= 0]
+    parent_row = (torch.from_numpy(indptr[:-1].astype(np.int64)).repeat_interleave(n))[par_t >= 0] + par_t[par_t >= 0]
+    ctok = torch.from_numpy(tok.astype(np.int64))[child]
+    rmax = logits.float().amax(dim=1)
+    boost = torch.rand(child.numel(), generator=torch.Generator().manual_seed(seed + 4)) * 3.0 - 0.5
+    logits[parent_row.to(device), ctok.to(device)] = (rmax[parent_row.to(device)] + boost.to(device)).to(torch.bfloat16)
+
+    dev_i32 = lambda x: torch.as_tensor(np.ascontiguousarray(x), dtype=torch.int32, device=device)
+    W = dict(
+        trees=trees, n=n, kv_len=kv_len, layer=layer, pool=layer.view(1, *layer.shape), q=q, k_new=k_new,
+        v_new=v_new, logits=logits,
+        qo_indptr=dev_i32(indptr), parents=dev_i32(par), tokens=dev_i32(tok),
+        draft_probs=torch.as_tensor(dp, dtype=torch.float32, device=device),
+        page_indptr=dev_i32(np.arange(B + 1) * pages_per), page_indices=perm.contiguous(),
+        last_page_len=dev_i32(np.full(B, (kv_len - 1) % pl + 1)), seq_lens=dev_i32(np.full(B, kv_len)),
+        offsets=dev_i32(np.full(B, P)), mask_words=K.mask_words_for(n),
+        host=dict(parents=par, tokens=tok, draft_probs=dp, indptr=indptr),
+    )
+    W["out"] = torch.empty_like(q)
+    W["ot"] = torch.empty(B, n, dtype=torch.int32, device=device)
+    W["oh"] = torch.empty(B, n, dtype=torch.int32, device=device)
+    W["oc"] = torch.empty(B, 4, dtype=torch.int32, device=device)
+    W["bits"] = torch.empty(B * n, W["mask_words"], dtype=torch.int64, device=device)
+    W["bi"] = torch.empty(B * n, dtype=torch.int32, device=device)
+    W["pos"] = torch.empty(B * n, dtype=torch.int32, device=device)
+    return W
+
+
+class Step:
+    """The verification step as raw C-ABI launches on the current stream."""
+
+    def __init__(self, a, W, device, philox_seed=5):
+        import torch
+        from parallel_tree_spec_b200 import _lib, kernels as K
+        self.a, self.W, self.K, self.L = a, W, K, _lib.lib()
+        self.dev = device
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        B, n = a.batch, W["n"]
+        self.acc_ws = K.workspace(device, "accept", self.L.pts_accept_workspace_size(B * n, a.vocab))
+        self.attn_ws = K.workspace(device, "attn", max(256, self.L.pts_tree_attn_workspace_size(
+            B, B * n, a.hq, 128, W["kv_len"])))
+        self.philox_seed = philox_seed
+        self.step_index = 0
+        self.launches_per_step = 6
+
+    def run(self, ev=None):
+        from parallel_tree_spec_b200._lib import check
+        a, W, L, s = self.a, self.W, self.L, self.stream
+        B, n = a.batch, W["n"]
+        P = W["page_indptr"]
+        check(L.pts_tree_mask_from_parents(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), B, B * n,
+                                           W["mask_words"], W["bits"].data_ptr(), s), "mask")
+        check(L.pts_batch_positions(W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(), B, B * n,
+                                    W["bi"].data_ptr(), W["pos"].data_ptr(), s), "positions")
+        lay = W["layer"]
+        check(L.pts_kv_append(W["k_new"].data_ptr(), W["v_new"].data_ptr(), a.hkv * 128, a.hkv * 128, lay.data_ptr(),
+                              W["bi"].data_ptr(), W["pos"].data_ptr(), P.data_ptr(), W["page_indices"].data_ptr(),
+                              B * n, a.hkv, 128, 16, lay.shape[0], 2, s), "append")
+        if ev is not None:
+            ev[0].record()
+        check(L.pts_tree_attn_run(W["q"].data_ptr(), lay.data_ptr(), W["qo_indptr"].data_ptr(), P.data_ptr(),
+                                  W["page_indices"].data_ptr(), W["last_page_len"].data_ptr(), W["bits"].data_ptr(),
+                                  W["mask_words"], W["out"].data_ptr(), B, B * n, n, W["kv_len"], a.hq, a.hkv, 128,
+                                  16, lay.shape[0], 1.0 / math.sqrt(128), self.attn_ws.data_ptr(),
+                                  self.attn_ws.numel(), s), "attention")
+        if ev is not None:
+            ev[1].record()
+        x = W["logits"]
+        if a.mode == "traversal":
+            check(L.pts_accept_traversal(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
+                                         W["tokens"].data_ptr(), W["draft_probs"].data_ptr(), B, B * n, a.vocab, n,
+                                         -1, a.temperature, 1.0, 0, self.philox_seed, self.step_index,
+                                         W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
+                                         self.acc_ws.data_ptr(), self.acc_ws.numel(), s), "accept")
+        else:
+            check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
+                                      W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(),
+                                      W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
+                                      self.acc_ws.numel(), s), "accept")
+        if ev is not None:
+            ev[2].record()
+        pool = W["pool"]
+        check(L.pts_kv_compact(pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
+                               W["page_indices"].data_ptr(), W["oh"].data_ptr(), n, W["oc"].data_ptr(), 4,
+                               W["offsets"].data_ptr(), B, n, None, None, s), "compact")
+        if ev is not None:
+            ev[3].record()
+        self.step_index += 1
+
+
+# ---------------------------------------------------------------- CPU (oracle port)
+def cpu_sample_time(a, seed, n_req):
+    """Seconds the NumPy restatement of the path takes per request, measured on
+    ``n_req`` requests of the same workload (attention over the request's
+    4k-prefix KV for all query heads, acceptance over its [N, V] logits and
+    the walk, compaction of the accepted path)."""
+    from oracle import accept as oacc
+    from oracle import attention as oatt
+    from oracle import kv as okv
+    from oracle.philox import UniformStream
+    from parallel_tree_spec_b200 import workload as wl
+
+    rng = np.random.default_rng(seed + 100)
+    n = 1 + a.width * a.depth
+    kv_len = a.prefix + n
+    pl = 16
+    npg = (kv_len + pl - 1) // pl
+    t_total = 0.0
+    for r in range(n_req):
+        t = wl.make_tree(rng, a.width, a.depth, a.vocab)
+        x = wl.make_logits(rng, t, a.vocab, plant=1.0, soft=True)
+        layer = (rng.standard_normal((npg, 2, pl, a.hkv, 128), dtype=np.float32) / np.sqrt(128)).astype(np.float32)
+        q = rng.standard_normal((n, a.hq, 128), dtype=np.float32)
+        mask = oatt.tree_mask(t.parents, a.prefix)
+        t0 = time.perf_counter()
+        oatt.tree_attention(q, layer, [list(range(npg))], [kv_len], [0, n], [mask], 1 / math.sqrt(128))
+        am, p = oacc.row_stats(x, a.temperature if a.mode == "traversal" else 1.0)
+        if a.mode == "traversal":
+            mb = oacc.mb_from_probs(t.parents, t.tokens, p)
+            s, h, tl, al, _ = oacc.traversal_walk(t.parents, t.tokens, t.draft_probs, mb, am, UniformStream(5, 0, r))
+        else:
+            s, h, tl, al = oacc.greedy_walk(t.parents, t.tokens, am)
+            h = list(h)
+        pool = layer[None]
+        okv.request_reorder(pool, list(range(npg)), kv_len, h, a.prefix + 1)
+        t_total += time.perf_counter() - t0
+    return t_total / n_req
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        info = threadpool_info()
+        return max([d.get("num_threads", 1) for d in info] or [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n = 1 + a.width * a.depth
+    t_req = cpu_sample_time(a, a.seed, a.cpu_sample_requests)       # warm (first call pays imports)
+    times = []
+    for _ in range(max(1, a.warmup)):
+        cpu_sample_time(a, a.seed, a.cpu_sample_requests)
+    for _ in range(max(1, a.steps)):
+        times.append(cpu_sample_time(a, a.seed, a.cpu_sample_requests) * a.batch)
+    step_s = statistics.mean(times)
+    value = 1.0 / step_s
+    rec = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": workload_name(a), "global_batch": a.batch, "prefix": a.prefix, "tree_rows": n,
+                   "vocab": a.vocab, "mode": a.mode},
+        "tokens_per_s": value * a.batch * n,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{a.cpu_sample_requests} request(s) of the {a.batch}-request step per timed "
+                                   f"step, scaled by {a.batch}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(rec), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_b200(a):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from parallel_tree_spec_b200 import _lib
+    _lib.lib()
+    W = build_workload(a, device, a.seed + 1000 * rank)
+    step = Step(a, W, device)
+    for _ in range(max(3, a.warmup)):
+        step.run()
+    torch.cuda.synchronize()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local).start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_host0 = time.perf_counter()
+    start.record()
+    for i in range(a.steps):
+        step.run(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    t_host1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    acc_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    cmp_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / a.steps
+    value = world * a.steps / (elapsed_ms / 1e3)
+
+    # e2e: tree inputs from pinned host memory, results back to the host every step
+    e2e = run_e2e(a, W, step, device)
+    if world > 1:
+        t = torch.tensor([e2e["value"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        e2e["value"] = float(t.item()) * world
+
+    ab = algorithmic_bytes(a)
+    peak, peak_kind = measured_peaks()
+    k_attn = statistics.mean(attn_ms) * 1e-3
+    k_acc = statistics.mean(acc_ms) * 1e-3
+    dom = "tree_attn_kernel" if k_attn >= k_acc else "accept_kernel"
+    dom_bytes = ab["attention"] if dom == "tree_attn_kernel" else ab["accept"]
+    dom_s = max(k_attn, k_acc)
+    achieved = dom_bytes / dom_s / 1e9
+    traffic = traffic_table().get(dom)
+    n = W["n"]
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        t_req = cpu_sample_time(a, a.seed, a.cpu_sample_requests)
+        cpu = {"value": 1.0 / (t_req * a.batch), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+               "sample": f"{a.cpu_sample_requests} request(s) of the {a.batch}-request step (attention for all "
+                         f"heads, acceptance over [{n}, {a.vocab}], compaction), scaled by {a.batch}"}
+    rec = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": workload_name(a), "global_batch": a.batch * world, "prefix": a.prefix,
+                   "tree_rows": n, "vocab": a.vocab, "mode": a.mode, "parallelism": f"batch-sharded x{world}",
+                   "l2": "inputs larger than L2 every step (KV 273 MB, logits 267 MB)"},
+        "tokens_per_s": value * a.batch * n,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes},
+        "step_roofline": {"algorithmic_bytes": ab["step"], "achieved_gbs": ab["step"] / (ms_per_step * 1e-3) / 1e9,
+                          "frac": ab["step"] / (ms_per_step * 1e-3) / 1e9 / peak},
+        "kernels_us": {"tree_attn": k_attn * 1e6, "accept": k_acc * 1e6, "compact": statistics.mean(cmp_ms) * 1e3},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": step.launches_per_step * a.steps,
+        "clocks": sampler.summary(t_host0, t_host1),
+        "accept_len_mean": float(W["oc"][:, 2].float().mean().item()),
+    }
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(a, W, step, device):
+    """Same step through host buffers: the tree inputs (parents, tokens, draft
+    probabilities) are copied from pinned host memory and the accepted
+    tokens / hidden indices / counts are read back every step."""
+    import torch
+    h = W["host"]
+    hp = torch.from_numpy(h["parents"]).pin_memory()
+    ht = torch.from_numpy(h["tokens"]).pin_memory()
+    hd = torch.from_numpy(h["draft_probs"]).pin_memory()
+    ot = torch.empty_like(W["ot"], device="cpu").pin_memory()
+    oh = torch.empty_like(W["oh"], device="cpu").pin_memory()
+    oc = torch.empty_like(W["oc"], device="cpu").pin_memory()
+    h2d = hp.numel() * 4 + ht.numel() * 4 + hd.numel() * 4
+    d2h = ot.numel() * 4 + oh.numel() * 4 + oc.numel() * 4
+
+    def one():
+        W["parents"].copy_(hp, non_blocking=True)
+        W["tokens"].copy_(ht, non_blocking=True)
+        W["draft_probs"].copy_(hd, non_blocking=True)
+        step.run()
+        ot.copy_(W["ot"], non_blocking=True)
+        oh.copy_(W["oh"], non_blocking=True)
+        oc.copy_(W["oc"], non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    for _ in range(3):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(a.e2e_steps):
+        one()
+    dt = time.perf_counter() - t0
+    return {"value": a.e2e_steps / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+def main(argv=None):
+    a = parse_args(argv)
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_b200(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -99,19 +99,23 @@ int pts_kv_append(const void* k, const void* v, int64_t k_token_stride, int64_t 
                   int num_kv_heads, int head_dim, int page_len, int max_pages, int elem_bytes,
                   pts_stream_t stream);
 
-/* KV compaction: for request b, slot offsets[b] + accepted[i] is copied to
- * slot offsets[b] + i (i < accepted_indptr[b+1] - accepted_indptr[b]) in every
- * layer, K and V, all reads before any write, slots mapped through the
- * request's page table.  Replaces KvCachePool.reorder_cache_with_offset and
+/* KV compaction: request b's accepted list is accepted[b*accepted_stride + i],
+ * i < accepted_counts[b*counts_stride]; slot offsets[b] + accepted[..i] is
+ * copied to slot offsets[b] + i in every layer, K and V, all reads before any
+ * write, slots mapped through the request's page table.  The acceptance
+ * kernels' out_hidden / out_counts (counts_stride 4) plug in directly.
+ * Replaces KvCachePool.reorder_cache_with_offset and
  * RequestKvCache.reorder_cache_with_offset (flashinfer/cache_manager.py:103-140,
- * 196-213); with page_indices = 0..max_pages-1 for every request it is the
- * pool-level flat-slot form.  new_kv_len / new_last_page_len (nullable)
- * receive offsets[b] + count and its last-page fill. */
+ * 196-213): the request-level call's offset is offsets[b] + 1; with
+ * page_indices = 0..max_pages-1 it is the pool-level flat-slot form.
+ * new_kv_len / new_last_page_len (nullable) receive offsets[b] + count and
+ * its last-page fill (cache_manager.py:203-207). */
 int pts_kv_compact(void* kv_pool, int num_layers, int max_pages, int page_len, int num_kv_heads,
                    int head_dim, int elem_bytes, const int32_t* page_indptr,
-                   const int32_t* page_indices, const int32_t* accepted_indptr,
-                   const int32_t* accepted, const int32_t* offsets, int batch, int max_accepted,
-                   int32_t* new_kv_len, int32_t* new_last_page_len, pts_stream_t stream);
+                   const int32_t* page_indices, const int32_t* accepted, int accepted_stride,
+                   const int32_t* accepted_counts, int counts_stride, const int32_t* offsets,
+                   int batch, int max_accepted, int32_t* new_kv_len, int32_t* new_last_page_len,
+                   pts_stream_t stream);
 
 /* ------------------------------------------------------------------ attention
  * Ancestor bitmask of every tree row: bit j of row i's mask_words-word mask is

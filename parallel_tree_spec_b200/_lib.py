@@ -37,8 +37,8 @@ SIGNATURES = {
     "pts_batch_positions": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_kv_append": (C.c_int, [vp, vp, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, vp]),
-    "pts_kv_compact": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
-                                 C.c_int, C.c_int, vp, vp, vp]),
+    "pts_kv_compact": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, C.c_int,
+                                 vp, C.c_int, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_tree_mask_from_parents": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "pts_tree_mask_from_bool": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
     "pts_tree_attn_workspace_size": (sz, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),

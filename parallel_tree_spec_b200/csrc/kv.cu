@@ -58,14 +58,16 @@ __global__ void kv_append_kernel(const char* __restrict__ k, const char* __restr
 // (cache_manager.py:133-134).
 __global__ void kv_compact_kernel(char* __restrict__ pool, int64_t layer_bytes, int max_pages, int page_len,
                                   int heads, int head_bytes, const int32_t* __restrict__ page_indptr,
-                                  const int32_t* __restrict__ page_indices, const int32_t* __restrict__ acc_indptr,
-                                  const int32_t* __restrict__ accepted, const int32_t* __restrict__ offsets) {
+                                  const int32_t* __restrict__ page_indices, const int32_t* __restrict__ accepted,
+                                  int acc_stride, const int32_t* __restrict__ acc_counts, int counts_stride,
+                                  int max_accepted, const int32_t* __restrict__ offsets) {
   extern __shared__ uint4 stage[];
   const int b = blockIdx.z;
   const int lkv = blockIdx.y;           // layer * 2 + kv
   const int h = blockIdx.x;
   const int layer = lkv >> 1, kv = lkv & 1;
-  const int a0 = acc_indptr[b], na = acc_indptr[b + 1] - a0;
+  const int32_t* acc = accepted + (int64_t)b * acc_stride;
+  const int na = min(max(acc_counts[(int64_t)b * counts_stride], 0), max_accepted);
   const int p0 = page_indptr[b], np = page_indptr[b + 1] - p0;
   const int off = offsets[b];
   const int vec = head_bytes / 16;
@@ -80,14 +82,14 @@ __global__ void kv_compact_kernel(char* __restrict__ pool, int64_t layer_bytes, 
   };
   for (int e = threadIdx.x; e < na * vec; e += blockDim.x) {
     const int i = e / vec, j = e % vec;
-    const int src = accepted[a0 + i];
+    const int src = acc[i];
     const char* sp = (src == i) ? nullptr : slot_ptr(off + src);
     if (sp) stage[e] = ((const uint4*)sp)[j];
   }
   __syncthreads();
   for (int e = threadIdx.x; e < na * vec; e += blockDim.x) {
     const int i = e / vec, j = e % vec;
-    const int src = accepted[a0 + i];
+    const int src = acc[i];
     if (src == i) continue;
     char* sp = slot_ptr(off + src);
     char* dp = slot_ptr(off + i);
@@ -95,11 +97,12 @@ __global__ void kv_compact_kernel(char* __restrict__ pool, int64_t layer_bytes, 
   }
 }
 
-__global__ void kv_compact_lengths_kernel(const int32_t* __restrict__ acc_indptr, const int32_t* __restrict__ offsets,
-                                          int batch, int page_len, int32_t* new_kv_len, int32_t* new_last) {
+__global__ void kv_compact_lengths_kernel(const int32_t* __restrict__ acc_counts, int counts_stride, int max_accepted,
+                                          const int32_t* __restrict__ offsets, int batch, int page_len,
+                                          int32_t* new_kv_len, int32_t* new_last) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
-  const int len = offsets[b] + acc_indptr[b + 1] - acc_indptr[b];
+  const int len = offsets[b] + min(max(acc_counts[(int64_t)b * counts_stride], 0), max_accepted);
   if (new_kv_len) new_kv_len[b] = len;
   if (new_last) new_last[b] = len == 0 ? 0 : (len - 1) % page_len + 1;
 }
@@ -203,10 +206,12 @@ extern "C" int pts_kv_append(const void* k, const void* v, int64_t k_token_strid
 
 extern "C" int pts_kv_compact(void* kv_pool, int num_layers, int max_pages, int page_len, int num_kv_heads,
                               int head_dim, int elem_bytes, const int32_t* page_indptr,
-                              const int32_t* page_indices, const int32_t* accepted_indptr,
-                              const int32_t* accepted, const int32_t* offsets, int batch, int max_accepted,
-                              int32_t* new_kv_len, int32_t* new_last_page_len, pts_stream_t stream) {
-  PTS_CHECK_ARG(kv_pool && page_indptr && page_indices && accepted_indptr && accepted && offsets, "null pointer");
+                              const int32_t* page_indices, const int32_t* accepted, int accepted_stride,
+                              const int32_t* accepted_counts, int counts_stride, const int32_t* offsets, int batch,
+                              int max_accepted, int32_t* new_kv_len, int32_t* new_last_page_len,
+                              pts_stream_t stream) {
+  PTS_CHECK_ARG(kv_pool && page_indptr && page_indices && accepted && accepted_counts && offsets, "null pointer");
+  PTS_CHECK_ARG(accepted_stride >= max_accepted && counts_stride >= 1, "bad accepted/counts strides");
   PTS_CHECK_ARG(elem_bytes == 2 || elem_bytes == 4, "elem_bytes must be 2 or 4");
   PTS_CHECK_ARG(num_layers > 0 && max_pages > 0 && page_len > 0 && num_kv_heads > 0 && head_dim > 0, "bad shape");
   PTS_CHECK_ARG(batch > 0 && max_accepted >= 0, "bad batch/max_accepted");
@@ -223,14 +228,15 @@ extern "C" int pts_kv_compact(void* kv_pool, int num_layers, int max_pages, int 
     const int64_t layer_bytes = (int64_t)max_pages * 2 * page_len * num_kv_heads * head_bytes;
     dim3 grid(num_kv_heads, 2 * num_layers, batch);
     kv_compact_kernel<<<grid, 128, smem, st>>>((char*)kv_pool, layer_bytes, max_pages, page_len, num_kv_heads,
-                                               head_bytes, page_indptr, page_indices, accepted_indptr, accepted,
-                                               offsets);
+                                               head_bytes, page_indptr, page_indices, accepted, accepted_stride,
+                                               accepted_counts, counts_stride, max_accepted, offsets);
     int rc = launch_status("kv_compact_kernel");
     if (rc) return rc;
   }
   if (new_kv_len || new_last_page_len) {
-    kv_compact_lengths_kernel<<<(batch + 127) / 128, 128, 0, st>>>(accepted_indptr, offsets, batch, page_len,
-                                                                   new_kv_len, new_last_page_len);
+    kv_compact_lengths_kernel<<<(batch + 127) / 128, 128, 0, st>>>(accepted_counts, counts_stride, max_accepted,
+                                                                   offsets, batch, page_len, new_kv_len,
+                                                                   new_last_page_len);
     return launch_status("kv_compact_lengths_kernel");
   }
   return PTS_OK;

@@ -149,19 +149,27 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, kv_layer: torch.Tensor, batch_in
 
 
 def kv_compact(pool: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor,
-               accepted_indptr: torch.Tensor, accepted: torch.Tensor, offsets: torch.Tensor, max_accepted: int,
+               accepted: torch.Tensor, accepted_counts: torch.Tensor, offsets: torch.Tensor,
                new_kv_len: Optional[torch.Tensor] = None, new_last_page_len: Optional[torch.Tensor] = None) -> None:
-    """Copy slot offsets[b]+accepted[i] -> offsets[b]+i in every layer of
-    ``pool`` [L, max_pages, 2, page_len, Hkv, D]."""
-    dev = _need_cuda(pool, page_indptr, page_indices, accepted_indptr, accepted, offsets)
+    """For request b copy slot offsets[b] + accepted[b, i] -> offsets[b] + i,
+    i < accepted_counts[b, 0], in every layer of ``pool``
+    [L, max_pages, 2, page_len, Hkv, D].  ``accepted`` is [B, S] int32 and
+    ``accepted_counts`` [B] or [B, C] (first column used), which is what the
+    acceptance kernels return."""
+    dev = _need_cuda(pool, page_indptr, page_indices, accepted, accepted_counts, offsets)
     if pool.dim() != 6 or pool.shape[2] != 2 or not pool.is_contiguous():
         raise ValueError("pool must be a contiguous [L, max_pages, 2, page_len, Hkv, D] tensor")
     L, P, _, pl, H, D = pool.shape
-    B = accepted_indptr.numel() - 1
+    accepted = _i32(accepted, "accepted")
+    if accepted.dim() != 2:
+        raise ValueError("accepted must be [B, S]")
+    counts = _i32(accepted_counts, "counts")
+    cstride = 1 if counts.dim() == 1 else counts.stride(0)
+    B, S = accepted.shape
     _lib.call("pts_kv_compact", pool.data_ptr(), L, P, pl, H, D, pool.element_size(),
-              _i32(page_indptr, "a").data_ptr(), _i32(page_indices, "b").data_ptr(),
-              _i32(accepted_indptr, "c").data_ptr(), _i32(accepted, "d").data_ptr(), _i32(offsets, "e").data_ptr(),
-              B, int(max_accepted), new_kv_len.data_ptr() if new_kv_len is not None else None,
+              _i32(page_indptr, "a").data_ptr(), _i32(page_indices, "b").data_ptr(), accepted.data_ptr(),
+              accepted.stride(0), counts.data_ptr(), cstride, _i32(offsets, "e").data_ptr(), B, S,
+              new_kv_len.data_ptr() if new_kv_len is not None else None,
               new_last_page_len.data_ptr() if new_last_page_len is not None else None, _stream(dev))
 
 

@@ -39,9 +39,9 @@ def test_compaction_matches_reference_reorder(reorder_golden, flat):
         path = rec["path"]
         K.kv_compact(pool, torch.tensor([0, len(pages)], dtype=torch.int32, device=DEV),
                      torch.tensor(pages, dtype=torch.int32, device=DEV),
-                     torch.tensor([0, len(path)], dtype=torch.int32, device=DEV),
-                     torch.tensor(path, dtype=torch.int32, device=DEV),
-                     torch.tensor([rec["offset"] - 1], dtype=torch.int32, device=DEV), len(path))
+                     torch.tensor([path], dtype=torch.int32, device=DEV),
+                     torch.tensor([len(path)], dtype=torch.int32, device=DEV),
+                     torch.tensor([rec["offset"] - 1], dtype=torch.int32, device=DEV))
         assert sha1(from_dev_bits(pool, before.dtype)) == rec["sha1_after"], i
 
 
@@ -70,12 +70,17 @@ def test_compaction_batched_page_tables_vs_oracle():
         okv.request_reorder(exp, tb, kvl, pth, off + 1)
     dpool = to_dev_bits(pool)
     pind = np.cumsum([0] + [len(t) for t in tables]).astype(np.int32)
-    aind = np.cumsum([0] + [len(p) for p in paths]).astype(np.int32)
+    S = max(len(p) for p in paths) + 3
+    acc = np.full((5, S), -7, np.int32)          # padding past each count is never read
+    for b, pth in enumerate(paths):
+        acc[b, :len(pth)] = pth
+    counts = np.zeros((5, 4), np.int32)
+    counts[:, 0] = [len(p) for p in paths]
     nkv = torch.empty(5, dtype=torch.int32, device=DEV)
     nlast = torch.empty(5, dtype=torch.int32, device=DEV)
     K.kv_compact(dpool, torch.from_numpy(pind).to(DEV), torch.tensor(sum(tables, []), dtype=torch.int32, device=DEV),
-                 torch.from_numpy(aind).to(DEV), torch.tensor(sum(paths, []), dtype=torch.int32, device=DEV),
-                 torch.tensor(offs, dtype=torch.int32, device=DEV), max(len(p) for p in paths), nkv, nlast)
+                 torch.from_numpy(acc).to(DEV), torch.from_numpy(counts).to(DEV),
+                 torch.tensor(offs, dtype=torch.int32, device=DEV), nkv, nlast)
     assert np.array_equal(from_dev_bits(dpool, np.uint16), exp)
     assert nkv.cpu().tolist() == [o + len(p) for o, p in zip(offs, paths)]
     assert nlast.cpu().tolist() == [(o + len(p) - 1) % pl + 1 for o, p in zip(offs, paths)]
