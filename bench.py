@@ -62,6 +62,8 @@ def parse_args(argv=None):
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-sample-requests", type=int, default=1)
+    ap.add_argument("--cpu-time-budget", type=float, default=90.0,
+                    help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
@@ -334,14 +336,17 @@ def run_reference(a):
     n = 1 + a.width * a.depth
     t_req = cpu_sample_time(a, a.seed, a.cpu_sample_requests)       # warm (first call pays imports)
     times = []
-    for _ in range(max(1, a.warmup)):
+    t_start = time.perf_counter()
+    for _ in range(max(1, min(a.warmup, 3))):
         cpu_sample_time(a, a.seed, a.cpu_sample_requests)
     for _ in range(max(1, a.steps)):
         times.append(cpu_sample_time(a, a.seed, a.cpu_sample_requests) * a.batch)
+        if time.perf_counter() - t_start > a.cpu_time_budget:
+            break
     step_s = statistics.mean(times)
     value = 1.0 / step_s
     rec = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": len(times),
         "warmup": a.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
         "config": {"workload": workload_name(a), "global_batch": a.batch, "prefix": a.prefix, "tree_rows": n,
@@ -349,7 +354,7 @@ def run_reference(a):
         "tokens_per_s": value * a.batch * n,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                          "sample": f"{a.cpu_sample_requests} request(s) of the {a.batch}-request step per timed "
-                                   f"step, scaled by {a.batch}"},
+                                   f"step, scaled by {a.batch}; {len(times)} timed steps"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(rec), flush=True)
