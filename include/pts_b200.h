@@ -136,7 +136,8 @@ int pts_tree_mask_from_bool(const uint8_t* mask, const int32_t* qo_indptr, const
 /* Tree-masked paged attention, bf16 in / bf16 out, fp32 accumulation on the
  * tcgen05 tensor cores.  Query row i of request b sees the request's KV slots
  * [0, kv_len_b - N_b) (the prefix) and the tree slots kv_len_b - N_b + j whose
- * bit j is set in its mask.  kv_len_b = (page_indptr[b+1]-page_indptr[b]-1) *
+ * bit j is set in its mask; mask_bits == NULL makes the rows causal (row i
+ * sees slots up to kv_len_b - N_b + i: prefill and decode).  kv_len_b = (page_indptr[b+1]-page_indptr[b]-1) *
  * page_len + last_page_len[b].  Replaces BatchPrefillWithPagedKVCacheWrapper
  * plan/run with custom_mask, causal=False (flashinfer/attention_wrapper.py:
  * 131-144, 250-252).  head_dim 128, page_len 16, Hq/Hkv = 4 in this build. */

@@ -10,16 +10,21 @@
 //                     (128-byte swizzle, two 64-column halves of D each);
 //   warp 1 (MMA)      issues S_t = Q_t K^T (M=128, N=32, K=128) into TMEM for
 //                     each tile t, then O_t += P_t V (M=128, N=128, K=32);
-//   warps 2-5         (one warpgroup; warp w owns TMEM lanes 32*(w%4)..) read
-//                     S_t, apply the scale and the tree mask, keep a running
-//                     max and sum per row, write P_t (bf16) to shared memory,
-//                     and rescale O_t in TMEM when the row max grows by more
-//                     than 2^8 (lazy rescaling keeps exp2 arguments <= 8).
-// After the last block the same warpgroup normalises O_t by the row sum and
-// stores bf16 rows.  TMEM: O_t at columns 128*t, S_t at 384 + 32*t.
+//   warps 2-5, 6-9    (two softmax warpgroups: the first owns tiles 0 and 2,
+//                     the second tile 1; warp w reads TMEM lanes 32*(w%4)..)
+//                     read S_t, apply the scale and the tree mask, keep a
+//                     running max and sum per row, write P_t (bf16) to shared
+//                     memory, and rescale O_t in TMEM when the row max grows by
+//                     more than 2^8 (lazy rescaling keeps exp2 arguments <= 8).
+// The MMA warp issues S_t for block j+1 right after O_t's update for block j,
+// so the tensor pipe works on the next block while the softmax warps finish
+// the current one.  After the last block each warpgroup normalises its O_t by
+// the row sum and stores bf16 rows.  TMEM: O_t at columns 128*t, S_t at
+// 384 + 32*t.  The request's page table is staged in shared memory.
 //
 // The tree mask: KV slots below kv_len - N are the prefix (always visible);
 // slot kv_len - N + j is visible to row i when bit j of i's mask is set.
+// Without a mask the rows are causal: row i sees slots up to kv_len - N + i.
 // Every barrier wait is bounded; on timeout the CTA records an error, drains
 // its own tensor-core work and TMA copies, frees TMEM and returns.
 #include <cuda.h>
@@ -37,7 +42,8 @@ constexpr int kBlockN = 32;           // KV tokens per block
 constexpr int kTilesPerCta = 3;
 constexpr int kPage = 16;
 constexpr int kD = 128;
-constexpr int kThreads = 192;         // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kThreads = 320;         // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int kMaxSmemPages = 2048;   // page-table entries staged in shared memory
 constexpr uint32_t kTileBytes = 128 * kD * 2;                 // one Q tile (both halves)
 constexpr uint32_t kHalfBytes = 128 * 128;                    // [128 rows x 64 cols] bf16
 constexpr uint32_t kStageBytes = 4 * kBlockN * 128;           // K(2 halves) + V(2 halves)
@@ -60,7 +66,8 @@ struct __align__(8) Bars {
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffKV = kOffQ + kTilesPerCta * kTileBytes;
 constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffBars = kOffP + kTilesPerCta * kPBytes;
+constexpr uint32_t kOffPages = kOffP + kTilesPerCta * kPBytes;
+constexpr uint32_t kOffBars = kOffPages + kMaxSmemPages * 4;
 constexpr uint32_t kSmemBytes = kOffBars + 1024 + 1024;       // bars + alignment slack
 
 struct AttnParams {
@@ -120,8 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kTilesPerCta; ++t) {
       mbar_init(&bars.s_full[t], 1);
-      mbar_init(&bars.s_free[t], 128);
-      mbar_init(&bars.p_full[t], 128);
+      mbar_init(&bars.s_free[t], 4);      // one arrival per softmax warp
+      mbar_init(&bars.p_full[t], 4);
     }
     mbar_init(&bars.o_full, 1);
     mbar_init(&bars.drain, 1);
@@ -134,10 +141,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&bars.tmem, 512);
     tmem_relinquish();
   }
+  int32_t* spages = (int32_t*)(smem + kOffPages);
+  if (warp == 0) {
+    for (int i = lane; i < min(n_pages, kMaxSmemPages); i += 32) spages[i] = p.page_indices[p0 + i];
+  }
   if (warp >= 2) {
     // rows of P that no softmax thread writes must read as zero
     uint4* pz = (uint4*)(smem + kOffP);
-    for (int i = threadIdx.x - 64; i < (int)(kTilesPerCta * kPBytes / 16); i += 128) pz[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x - 64; i < (int)(kTilesPerCta * kPBytes / 16); i += kThreads - 64)
+      pz[i] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
   }
   tc_fence_before();
@@ -167,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* st = smem + kOffKV + s * kStageBytes;
         for (int pg = 0; pg < 2; ++pg) {
           const int slot = 2 * j + pg;
-          const int phys = slot < n_pages ? p.page_indices[p0 + slot] : p.max_pages;   // OOB -> zero fill
+          const int phys = slot >= n_pages ? p.max_pages                                // OOB -> zero fill
+                           : (slot < kMaxSmemPages ? spages[slot] : p.page_indices[p0 + slot]);
           const int page = (phys >= 0 && phys < p.max_pages) ? phys : p.max_pages;
           for (int half = 0; half < 2; ++half) {
             tma_load_4d(st + half * (kBlockN * 128) + pg * (kPage * 128), &kv_map, &bars.kv_full[s], half * 64, h,
@@ -184,66 +197,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t id_qk = idesc_bf16_f32(128, kBlockN, 0, 0);
-      const uint32_t id_pv = idesc_bf16_f32(128, kD, 0, 1);
-      bool ok = mbar_wait(&bars.q_full, 0);
-      if (!ok) record_abort(bars, p, 21);
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&bars.kv_full[s], (j / kStages) & 1)) {
-          record_abort(bars, p, 22);
-          break;
-        }
-        if (aborted(bars)) break;
-        tc_fence_after();
-        const uint32_t st = smem_u32(smem + kOffKV + s * kStageBytes);
-        for (int t = 0; t < n_tiles && ok; ++t) {
-          if (j > 0 && !mbar_wait(&bars.s_free[t], (j - 1) & 1)) {
-            record_abort(bars, p, 23);
+    // The whole warp walks the loop; one elected lane issues.  Every operand
+    // descriptor is a base descriptor plus a compile-time offset (the block
+    // loop is unrolled by the stage count), which keeps the issue rate at the
+    // tensor pipe's rate.
+    const uint32_t id_qk = idesc_bf16_f32(128, kBlockN, 0, 0);
+    const uint32_t id_pv = idesc_bf16_f32(128, kD, 0, 1);
+    const uint64_t qd0 = smem_desc(smem_u32(smem + kOffQ), 16, 1024, kSwizzle128B);
+    const uint64_t kd0 = smem_desc(smem_u32(smem + kOffKV), 16, 1024, kSwizzle128B);
+    const uint64_t vd0 = smem_desc(smem_u32(smem + kOffKV + 2 * kBlockN * 128), kBlockN * 128, 1024, kSwizzle128B);
+    const uint64_t pd0 = smem_desc(smem_u32(smem + kOffP), 16, 1024, kSwizzle128B);
+    const bool leader = elect_one();
+#define PTS_QK(T, S)                                                                                          \
+  do {                                                                                                        \
+    if (leader) {                                                                                             \
+      _Pragma("unroll") for (int k = 0; k < kD / 16; ++k) {                                                   \
+        const uint64_t a = qd0 + (uint64_t)(((T) * kTileBytes + (k / 4) * kHalfBytes + (k % 4) * 32) >> 4);    \
+        const uint64_t bd = kd0 + (uint64_t)(((S) * kStageBytes + (k / 4) * (kBlockN * 128) + (k % 4) * 32) >> 4); \
+        mma_bf16_ss(tmem + 384 + 32 * (T), a, bd, id_qk, k > 0);                                              \
+      }                                                                                                       \
+      mma_commit(&bars.s_full[T]);                                                                            \
+    }                                                                                                         \
+    __syncwarp();                                                                                             \
+  } while (0)
+    bool ok = mbar_wait(&bars.q_full, 0) && mbar_wait(&bars.kv_full[0], 0);
+    if (!ok && lane == 0) record_abort(bars, p, 21);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll
+      for (int t = 0; t < kTilesPerCta; ++t)
+        if (t < n_tiles) PTS_QK(t, 0);
+    }
+    for (int j0 = 0; ok && j0 < n_blocks; j0 += kStages) {
+#pragma unroll
+      for (int ss = 0; ss < kStages; ++ss) {
+        const int j = j0 + ss;
+        if (j >= n_blocks || !ok) break;
+        const int s1 = (ss + 1) % kStages;
+        const bool more = j + 1 < n_blocks;
+#pragma unroll
+        for (int t = 0; t < kTilesPerCta; ++t) {
+          if (t >= n_tiles || !ok) break;
+          bool w_ok = mbar_wait(&bars.p_full[t], j & 1) && !aborted(bars);
+          if (!__all_sync(0xffffffffu, w_ok)) {
+            if (lane == 0) record_abort(bars, p, 24);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t qa = smem_u32(smem + kOffQ + t * kTileBytes);
+          if (leader) {
 #pragma unroll
-          for (int k = 0; k < kD / 16; ++k) {
-            const uint64_t a = smem_desc(qa + (k / 4) * kHalfBytes + (k % 4) * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bd = smem_desc(st + (k / 4) * (kBlockN * 128) + (k % 4) * 32, 16, 1024, kSwizzle128B);
-            mma_bf16_ss(tmem + 384 + 32 * t, a, bd, id_qk, k > 0);
+            for (int k = 0; k < kBlockN / 16; ++k) {
+              const uint64_t a = pd0 + (uint64_t)((t * kPBytes + k * 32) >> 4);
+              const uint64_t bd = vd0 + (uint64_t)((ss * kStageBytes + k * 2048) >> 4);
+              mma_bf16_ss(tmem + 128 * t, a, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+            }
+            if (t == n_tiles - 1) mma_commit(&bars.kv_empty[ss]);
           }
-          mma_commit(&bars.s_full[t]);
-        }
-        for (int t = 0; t < n_tiles && ok; ++t) {
-          if (!mbar_wait(&bars.p_full[t], j & 1)) {
-            record_abort(bars, p, 24);
-            ok = false;
-            break;
-          }
-          if (aborted(bars)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t pa = smem_u32(smem + kOffP + t * kPBytes);
-          const uint32_t vb = st + 2 * (kBlockN * 128);
-#pragma unroll
-          for (int k = 0; k < kBlockN / 16; ++k) {
-            const uint64_t a = smem_desc(pa + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bd = smem_desc(vb + k * 2048, kBlockN * 128, 1024, kSwizzle128B);
-            mma_bf16_ss(tmem + 128 * t, a, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          __syncwarp();
+          if (more) {
+            // S_t for the next block: its K stage must have landed and the
+            // softmax must have read S_t of this block
+            w_ok = (t != 0 || mbar_wait(&bars.kv_full[s1], ((j + 1) / kStages) & 1)) &&
+                   mbar_wait(&bars.s_free[t], j & 1);
+            if (!__all_sync(0xffffffffu, w_ok)) {
+              if (lane == 0) record_abort(bars, p, 23);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            PTS_QK(t, s1);
           }
         }
-        mma_commit(&bars.kv_empty[s]);
       }
+    }
+#undef PTS_QK
+    if (leader) {
       mma_commit(&bars.o_full);
       mma_commit(&bars.drain);
-      mbar_wait(&bars.drain, 0);
     }
+    __syncwarp();
+    mbar_wait(&bars.drain, 0);
   } else {
     // ------------------------------------------------------------ softmax warpgroup
     const int quarter = warp & 3;
     const int r_local = quarter * 32 + lane;
+    const int wg = (warp - 2) >> 2;                 // 0: tiles 0 and 2, 1: tile 1
+    auto owns = [&](int t) { return wg == 0 ? (t != 1) : (t == 1); };
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     float m_used[kTilesPerCta], l_sum[kTilesPerCta];
     bool valid[kTilesPerCta];
@@ -263,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int t = 0; t < kTilesPerCta; ++t) {
         if (t >= n_tiles) break;
+        if (!owns(t)) continue;
         if (!mbar_wait(&bars.s_full[t], j & 1)) {
           record_abort(bars, p, 31);
           ok = false;
@@ -273,7 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_base + 384 + 32 * t, sr);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&bars.s_free[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.s_free[t]);
         float x[32];
         float mblk = -INFINITY;
         if (valid[t]) {
@@ -284,14 +327,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               mblk = fmaxf(mblk, x[c]);
             }
           } else {
-            const uint64_t* mrow = p.mask_bits + (int64_t)(q0 + node[t]) * p.mask_words;
+            const uint64_t* mrow = p.mask_bits ? p.mask_bits + (int64_t)(q0 + node[t]) * p.mask_words : nullptr;
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
               const int kv = kv0 + c;
               bool vis = kv < kv_len;
               if (vis && kv >= prefix) {
                 const int tn = kv - prefix;
-                vis = (tn / 64 < p.mask_words) && ((__ldg(mrow + tn / 64) >> (tn % 64)) & 1ull);
+                vis = p.mask_bits == nullptr
+                          ? (tn <= node[t])
+                          : (tn / 64 < p.mask_words) && ((__ldg(mrow + tn / 64) >> (tn % 64)) & 1ull);
               }
               x[c] = vis ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
               mblk = fmaxf(mblk, x[c]);
@@ -339,7 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars.p_full[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.p_full[t]);
       }
       if (aborted(bars)) ok = false;
     }
@@ -347,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && mbar_wait(&bars.o_full, 0)) {
       tc_fence_after();
       for (int t = 0; t < n_tiles; ++t) {
+        if (!owns(t)) continue;
         const float inv = (valid[t] && l_sum[t] > 0.0f) ? 1.0f / l_sum[t] : 0.0f;
         const int R = (tile0 + t) * 128 + r_local;
         const int hh = R % p.g;
@@ -421,17 +468,19 @@ extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int3
                                  int max_qo_len, int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
                                  int page_len, int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
                                  pts_stream_t stream) {
-  PTS_CHECK_ARG(q && kv_layer && qo_indptr && page_indptr && page_indices && last_page_len && mask_bits && out,
-                "null pointer");
+  PTS_CHECK_ARG(q && kv_layer && qo_indptr && page_indptr && page_indices && last_page_len && out, "null pointer");
   PTS_CHECK_ARG(batch > 0 && total_q > 0 && max_qo_len > 0 && max_kv_len > 0, "bad sizes");
   PTS_CHECK_ARG(num_qo_heads > 0 && num_kv_heads > 0 && num_qo_heads % num_kv_heads == 0, "bad head counts");
   if (head_dim != kD) return set_error(PTS_ERR_UNSUPPORTED, "head_dim %d (this build: 128)", head_dim);
   if (page_len != kPage) return set_error(PTS_ERR_UNSUPPORTED, "page_len %d (this build: 16)", page_len);
   const int g = num_qo_heads / num_kv_heads;
   if (g > 128 || 128 % g != 0) return set_error(PTS_ERR_UNSUPPORTED, "GQA group %d must divide 128", g);
-  if (max_qo_len > PTS_MAX_TREE_NODES)
-    return set_error(PTS_ERR_CAPACITY, "tree of %d rows above %d", max_qo_len, PTS_MAX_TREE_NODES);
-  PTS_CHECK_ARG(mask_words >= (max_qo_len + 63) / 64, "mask_words %d too small for %d rows", mask_words, max_qo_len);
+  if (mask_bits) {
+    if (max_qo_len > PTS_MAX_TREE_NODES)
+      return set_error(PTS_ERR_CAPACITY, "tree of %d rows above %d", max_qo_len, PTS_MAX_TREE_NODES);
+    PTS_CHECK_ARG(mask_words >= (max_qo_len + 63) / 64, "mask_words %d too small for %d rows", mask_words,
+                  max_qo_len);
+  }
   PTS_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)kv_layer & 15) == 0 && ((uintptr_t)out & 15) == 0,
                 "q, kv_layer and out must be 16-byte aligned");
   if (!workspace || workspace_bytes < 256) return set_error(PTS_ERR_CAPACITY, "workspace of at least 256 bytes");
@@ -474,6 +523,7 @@ extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int3
     attr_set = true;
   }
   const int groups = ((max_qo_len * g + 127) / 128 + kTilesPerCta - 1) / kTilesPerCta;
+  if (groups > 65535) return set_error(PTS_ERR_CAPACITY, "%d query rows per request is too many", max_qo_len);
   dim3 grid(num_kv_heads, batch, groups);
   tree_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(p, q_map, kv_map);
   return launch_status("tree_attn_kernel");

@@ -189,34 +189,36 @@ def tree_mask_from_parents(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_
 
 
 def tree_mask_from_bool(mask: torch.Tensor, qo_indptr: torch.Tensor, mask_indptr: torch.Tensor,
-                        kv_lens: torch.Tensor, mask_words: int, bad_rows: Optional[torch.Tensor] = None):
+                        kv_lens: torch.Tensor, mask_words: int, total_q: Optional[int] = None,
+                        check: bool = True) -> torch.Tensor:
+    """Pack a flattened boolean tree mask into per-row ancestor bitmasks.
+    With ``check`` the prefix columns are verified on the device and a
+    non-tree mask raises ValueError (one device-to-host read)."""
     dev = _need_cuda(mask, qo_indptr, mask_indptr, kv_lens)
     if mask.dtype != torch.bool:
         mask = mask.to(torch.bool)
     mask = mask.contiguous()
     qo_indptr = _i32(qo_indptr, "qo")
-    T = int(qo_indptr[-1].item()) if bad_rows is None else None
-    raise_if_bad = bad_rows is None
-    if bad_rows is None:
-        bad_rows = torch.zeros(1, dtype=torch.int32, device=dev)
-    total_q = T if T is not None else None
     if total_q is None:
         total_q = int(qo_indptr[-1].item())
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
     bits = torch.empty(total_q, mask_words, dtype=torch.int64, device=dev)
     _lib.call("pts_tree_mask_from_bool", mask.data_ptr(), qo_indptr.data_ptr(), _i32(mask_indptr, "mi").data_ptr(),
               _i32(kv_lens, "kl").data_ptr(), qo_indptr.numel() - 1, total_q, mask_words, bits.data_ptr(),
-              bad_rows.data_ptr(), _stream(dev))
-    if raise_if_bad and int(bad_rows.item()) != 0:
+              bad.data_ptr(), _stream(dev))
+    if check and int(bad.item()) != 0:
         raise ValueError("custom mask is not a tree mask: a prefix column is masked out")
     return bits
 
 
 def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Tensor, page_indptr: torch.Tensor,
-                   page_indices: torch.Tensor, last_page_len: torch.Tensor, mask_bits: torch.Tensor,
+                   page_indices: torch.Tensor, last_page_len: torch.Tensor, mask_bits: Optional[torch.Tensor],
                    max_qo_len: int, max_kv_len: int, sm_scale: Optional[float] = None,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Tree-masked paged attention: q [T, Hq, D] bf16, kv_layer [P, 2, 16, Hkv, D] bf16."""
-    dev = _need_cuda(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len, mask_bits)
+    """Tree-masked paged attention: q [T, Hq, D] bf16, kv_layer [P, 2, 16, Hkv, D]
+    bf16; ``mask_bits`` None means causal rows."""
+    dev = _need_cuda(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len,
+                     *([mask_bits] if mask_bits is not None else []))
     if q.dtype != torch.bfloat16 or kv_layer.dtype != torch.bfloat16:
         raise ValueError("tree attention takes bf16 queries and cache")
     if not q.is_contiguous() or not kv_layer.is_contiguous():
@@ -233,6 +235,7 @@ def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Ten
     ws = workspace(dev, "attn", max(wsz, 256))
     _lib.call("pts_tree_attn_run", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
               _i32(page_indptr, "pi").data_ptr(), _i32(page_indices, "px").data_ptr(),
-              _i32(last_page_len, "lp").data_ptr(), mask_bits.data_ptr(), mask_bits.shape[1], out.data_ptr(), B, T,
+              _i32(last_page_len, "lp").data_ptr(), mask_bits.data_ptr() if mask_bits is not None else None,
+              mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T,
               int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
     return out
