@@ -1,23 +1,23 @@
 // Fused tree acceptance over bf16 logits (greedy and traversal verification).
 //
-// One launch does everything.  Each logits row is owned by a thread-block
-// cluster of C = ceil(V / 16384) CTAs (256 threads x 64 elements each, the
-// whole chunk held in registers after one 128-bit streaming load per vector;
-// four CTAs per SM so loads of one CTA overlap the reductions of others):
+// One launch does everything.  Each logits row is split into C = ceil(V/16384)
+// chunks, one CTA each (256 threads x 64 elements, the chunk held in
+// registers after one 128-bit streaming load per vector; four CTAs per SM so
+// the loads of one CTA overlap the reductions of others):
 //   1. every thread reduces its 64 values to (max m_t, sum_t exp(x - m_t),
 //      first index of m_t) in one pass (packed bf16x2 max, ex2.approx);
-//   2. warp, CTA and cluster merges combine the partials: m = max, s = sum of
-//      s_t * exp(m_t - m) (CUDA expf factors, double above the warp level),
-//      argmax = first index of m; every cluster rank pushes its partial into
-//      rank 0 through distributed shared memory and a remote mbarrier arrive;
-//   3. rank 0 takes the argmax of the bf16-rounded probabilities
+//   2. warp and CTA merges combine the partials: m = max, s = sum of
+//      s_t * exp(m_t - m) (CUDA expf factors, double accumulation),
+//      argmax = first index of m; the CTA's partial goes to the workspace and
+//      the last chunk of the row to finish (acquire/release counter) merges
+//      the row's partials in chunk order;
+//   3. that CTA takes the argmax of the bf16-rounded probabilities
 //      bf16(exp(x - m) / s): the first index of m, unless a value just below m
 //      can round to the same probability (only possible for small m), in
 //      which case the row is rescanned with the exact rounding rule;
-//   4. the last row of a request to finish (acquire/release counter) walks the
-//      tree on the device: the greedy walk of verify_tree_exact
-//      (verification.py:185-268) or the traversal loop of
-//      verify_tree_traversal (verification.py:275-524).
+//   4. the last row of a request to finish walks the tree on the device: the
+//      greedy walk of verify_tree_exact (verification.py:185-268) or the
+//      traversal loop of verify_tree_traversal (verification.py:275-524).
 // The probabilities that decide anything (per-node target probabilities,
 // argmax ties) are computed like torch's softmax epilogue: expf(x - m) / s.
 //
@@ -35,15 +35,12 @@
 // its parent.  Fp32 tensor arithmetic and fp64 scalar arithmetic are replayed
 // with explicitly rounded operations in the reference's order.
 //
-// Workspace (caller-owned): row stats and a per-request counter array that
-// is cleared at the start of every call.
-#include <cooperative_groups.h>
+// Workspace (caller-owned): chunk partials, row stats, and per-row and
+// per-request counters that are cleared at the start of every call.
 #include <float.h>
 #include <limits.h>
 
 #include "common.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace pts {
 namespace {
@@ -52,11 +49,10 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kVecPerThread = 8;                           // 8 x 16 B per thread
 constexpr int kChunk = kThreads * kVecPerThread * 8;       // 16384 elements per CTA
-constexpr int kMaxCluster = 16;                            // above 8 needs the non-portable opt-in
+constexpr int kMaxChunks = 64;                             // vocabularies up to 1,048,576
 constexpr float kEps32 = 1e-8f;
 constexpr double kEps = 1e-8;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMaxDraws = 2 * PTS_MAX_TREE_NODES + 2;
 
 struct RowStat {
   float m;
@@ -72,7 +68,7 @@ struct AcceptParams {
   const int32_t* parents;
   const int32_t* tokens;
   const float* draft_probs;
-  int batch, num_rows, vocab, cluster, max_nodes, out_stride;
+  int batch, num_rows, vocab, max_nodes, out_stride;
   int64_t eos;
   float inv_temp;
   int use_temp;
@@ -83,6 +79,8 @@ struct AcceptParams {
   int32_t* out_hidden;
   int32_t* out_counts;
   RowStat* row_ws;
+  struct Part* part_ws;
+  unsigned* row_ctr;
   unsigned* req_ctr;
 };
 
@@ -133,65 +131,30 @@ __device__ __forceinline__ uint32_t scale_pair(uint32_t v, float inv_t) {
 }
 
 // (max, sum of exp(x - max), first index of max) partials.
-struct Part {
-  float m;
+struct __align__(16) Part {
   double s;
+  float m;
   int idx;
 };
 
 __device__ __forceinline__ Part merge(const Part& a, const Part& b) {
-  if (b.m == -INFINITY) return a;
-  if (a.m == -INFINITY) return b;
+  if (b.idx == INT_MAX) return a;
+  if (a.idx == INT_MAX) return b;
   Part r;
   if (a.m == b.m) {
-    r.m = a.m;
     r.s = a.s + b.s;
+    r.m = a.m;
     r.idx = min(a.idx, b.idx);
   } else if (a.m > b.m) {
-    r.m = a.m;
     r.s = a.s + b.s * (double)expf(b.m - a.m);
+    r.m = a.m;
     r.idx = a.idx;
   } else {
-    r.m = b.m;
     r.s = b.s + a.s * (double)expf(a.m - b.m);
+    r.m = b.m;
     r.idx = b.idx;
   }
   return r;
-}
-
-__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
-  uint32_t local = (uint32_t)__cvta_generic_to_shared(p), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
-  return remote;
-}
-
-__device__ __forceinline__ void mbar_init_local(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(count)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
-  uint64_t t0 = 0;
-  for (int it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    if (it == 0) t0 = t;
-    else if (t - t0 > 2000000000ull) return false;
-  }
 }
 
 __device__ __forceinline__ int block_reduce_min(int v, int* sm) {
@@ -211,24 +174,63 @@ __device__ __forceinline__ int block_reduce_min(int v, int* sm) {
   return sm[0];
 }
 
+// Walk state in dynamic shared memory, sized for the call's largest tree
+// (capacity `cap` nodes), so streaming CTAs of small trees stay light.
 struct WalkSmem {
-  int32_t token[PTS_MAX_TREE_NODES];
-  int16_t sticky_t[PTS_MAX_TREE_NODES];    // time p_alpha was last set directly (-1: never)
-  int16_t reset_t[PTS_MAX_TREE_NODES];     // time the node's subtree was last recomputed
-  int16_t first_child[PTS_MAX_TREE_NODES];
-  int16_t next_sib[PTS_MAX_TREE_NODES];
-  int16_t first_valid[PTS_MAX_TREE_NODES];
-  int16_t parent[PTS_MAX_TREE_NODES];
-  int16_t path[PTS_MAX_TREE_NODES];
-  int16_t path_rmax[PTS_MAX_TREE_NODES];
-  int16_t sib[PTS_MAX_TREE_NODES];
-  float path_pa[PTS_MAX_TREE_NODES];
-  float mb[PTS_MAX_TREE_NODES];
-  float ms[PTS_MAX_TREE_NODES];
-  float stored_pa[PTS_MAX_TREE_NODES];
-  float uni[kMaxDraws];
-  uint8_t valid[PTS_MAX_TREE_NODES];
+  int32_t* token;
+  int16_t* sticky_t;       // time p_alpha was last set directly (-1: never)
+  int16_t* reset_t;        // time the node's subtree was last recomputed
+  int16_t* first_child;
+  int16_t* next_sib;
+  int16_t* first_valid;
+  int16_t* parent;
+  int16_t* path;
+  int16_t* path_rmax;
+  int16_t* sib;            // children of every node, contiguous per parent
+  int16_t* child_start;
+  int16_t* child_cnt;
+  float* path_pa;
+  float* mb;
+  float* ms;
+  float* stored_pa;
+  float* uni;              // 2 * cap + 2 uniforms
+  uint8_t* valid;
 };
+
+__host__ __device__ inline size_t walk_smem_bytes(int cap) {
+  cap = (cap + 15) & ~15;
+  return (size_t)cap * (4 + 11 * 2 + 4 * 4 + 1) + (size_t)(2 * cap + 2) * 4 + 64;
+}
+
+__device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
+  cap = (cap + 15) & ~15;
+  WalkSmem w;
+  uint8_t* q = base;
+  auto take = [&](size_t bytes) {
+    uint8_t* r = q;
+    q += (bytes + 15) & ~(size_t)15;
+    return r;
+  };
+  w.token = (int32_t*)take(cap * 4);
+  w.path_pa = (float*)take(cap * 4);
+  w.mb = (float*)take(cap * 4);
+  w.ms = (float*)take(cap * 4);
+  w.stored_pa = (float*)take(cap * 4);
+  w.uni = (float*)take((2 * cap + 2) * 4);
+  w.sticky_t = (int16_t*)take(cap * 2);
+  w.reset_t = (int16_t*)take(cap * 2);
+  w.first_child = (int16_t*)take(cap * 2);
+  w.next_sib = (int16_t*)take(cap * 2);
+  w.first_valid = (int16_t*)take(cap * 2);
+  w.parent = (int16_t*)take(cap * 2);
+  w.path = (int16_t*)take(cap * 2);
+  w.path_rmax = (int16_t*)take(cap * 2);
+  w.sib = (int16_t*)take(cap * 2);
+  w.child_start = (int16_t*)take(cap * 2);
+  w.child_cnt = (int16_t*)take(cap * 2);
+  w.valid = (uint8_t*)take(cap);
+  return w;
+}
 
 __device__ void write_counts(const AcceptParams& p, int b, int n_out, int total, int acc, int node) {
   int32_t* c = p.out_counts + (int64_t)b * 4;
@@ -285,128 +287,89 @@ __device__ __forceinline__ float ratio_of(float mb, float ms) {
   return ms > kEps32 ? __fdiv_rn(mb, ms) : 0.0f;
 }
 
-// Traversal verification (verify_tree_traversal, verification.py:377-524) by
-// one warp; see the file comment for the lazily evaluated p_alpha.
-__device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, WalkSmem& w) {
-  const int lane = threadIdx.x & 31;
-  __shared__ int s_state, s_parent, s_nsib;
-  __shared__ double s_old_ms_rej, s_p_old;
-  int16_t* s_sib = w.sib;
+// Traversal verification (verify_tree_traversal, verification.py:377-524),
+// one thread; see the file comment for the lazily evaluated p_alpha.
+__device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w) {
   int accepted = 0;
-  int depth = 0;           // path[0..depth] is the current descent path (lane 0)
+  int depth = 0;           // w.path[0..depth]: the current descent path
   int draw = 0;
   int T = 1;               // time stamp of the next direct p_alpha assignment
-  if (lane == 0) {
-    w.path[0] = 0;
-    w.path_pa[0] = w.stored_pa[0];
-    w.path_rmax[0] = -1;
-  }
+  w.path[0] = 0;
+  w.path_pa[0] = w.stored_pa[0];
+  w.path_rmax[0] = -1;
   const int max_iter = 2 * n + 2;
   for (int it = 0; it < max_iter; ++it) {                             // :377
-    if (lane == 0) {
-      // descend to the first valid leaf (:379-389), p_alpha evaluated lazily
-      int u = w.path[depth];
-      for (int c = w.first_valid[u]; c >= 0; c = w.first_valid[u]) {
-        const int rmax = max(w.path_rmax[depth], w.reset_t[u]);
-        const float pa = w.sticky_t[c] > rmax ? w.stored_pa[c]
-                                               : fminf(__fmul_rn(w.path_pa[depth], ratio_of(w.mb[c], w.ms[c])), 1.0f);
-        ++depth;
-        w.path[depth] = (int16_t)c;
-        w.path_pa[depth] = pa;
-        w.path_rmax[depth] = (int16_t)rmax;
-        u = c;
-      }
-      const int cand = u;
-      int state = 0;
-      if (!w.valid[cand]) {                                           // :391
-        state = 1;
-      } else {
-        const float p_val = w.path_pa[depth];                         // :395
-        const float eta = w.uni[draw++];                              // :396
-        if (eta < p_val) {
-          accepted = cand;
-          state = 1;
-        } else {
-          w.valid[cand] = 0;                                          // :403
-          const int parent = w.parent[cand];
-          s_old_ms_rej = (double)w.ms[cand];
-          w.ms[cand] = 0.0f;
-          if (parent < 0) {                                           // :408
-            accepted = 0;
-            state = 1;
-          } else {
-            if (w.first_valid[parent] == cand) {
-              int c = w.next_sib[cand];
-              while (c >= 0 && !w.valid[c]) c = w.next_sib[c];
-              w.first_valid[parent] = (int16_t)c;
-            }
-            --depth;                                                  // back to the parent
-            if (w.first_valid[parent] >= 0) {                         // :417 any active sibling
-              int ns = 0;
-              for (int c = w.first_child[parent]; c >= 0; c = w.next_sib[c]) s_sib[ns++] = (int16_t)c;
-              s_nsib = ns;
-              s_parent = parent;
-              s_p_old = (double)w.path_pa[depth];                     // :422
-              state = 2;
-            }
-          }
-        }
-      }
-      s_state = state;
+    // descend to the first valid leaf (:379-389), p_alpha evaluated lazily
+    int u = w.path[depth];
+    float pa_u = w.path_pa[depth];
+    int rmax_u = w.path_rmax[depth];
+    for (int c = w.first_valid[u]; c >= 0; c = w.first_valid[u]) {
+      const int rmax = max(rmax_u, (int)w.reset_t[u]);
+      const float pa = w.sticky_t[c] > rmax ? w.stored_pa[c]
+                                             : fminf(__fmul_rn(pa_u, ratio_of(w.mb[c], w.ms[c])), 1.0f);
+      ++depth;
+      w.path[depth] = (int16_t)c;
+      w.path_pa[depth] = pa;
+      w.path_rmax[depth] = (int16_t)rmax;
+      u = c;
+      pa_u = pa;
+      rmax_u = rmax;
     }
-    __syncwarp();
-    const int state = s_state;
-    if (state == 1) break;
-    if (state != 2) continue;
-    // ---- rejection update (:421-458); per-child terms in parallel, sums in order
-    const int parent = s_parent, ns = s_nsib;
-    const double p_old = s_p_old;
-    const float p_old32 = (float)p_old;
-    const double old_ms_rej = s_old_ms_rej;
-    float s_tree = 0.0f, sum_mb = 0.0f;
-    for (int base = 0; base < ns; base += 32) {
-      const int i = base + lane;
-      float t = 0.0f, mbv = 0.0f;
-      if (i < ns) {
-        const int c = s_sib[i];
-        mbv = w.mb[c];
-        t = fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), w.ms[c]), 0.0f);
-      }
-      const int cnt = min(32, ns - base);
-      for (int k = 0; k < cnt; ++k) {                                 // :432-433 left to right
-        s_tree = __fadd_rn(s_tree, __shfl_sync(0xffffffffu, t, k));
-        sum_mb = __fadd_rn(sum_mb, __shfl_sync(0xffffffffu, mbv, k));
-      }
+    const int cand = u;
+    const float eta = w.uni[draw++];                                  // :396
+    if (eta < pa_u) {                                                 // :395-400
+      accepted = cand;
+      break;
+    }
+    w.valid[cand] = 0;                                                // :403
+    const double old_ms_rej = (double)w.ms[cand];
+    w.ms[cand] = 0.0f;
+    const int parent = w.parent[cand];
+    if (parent < 0) {                                                 // :408
+      accepted = 0;
+      break;
+    }
+    if (w.first_valid[parent] == cand) {
+      int c = w.next_sib[cand];
+      while (c >= 0 && !w.valid[c]) c = w.next_sib[c];
+      w.first_valid[parent] = (int16_t)c;
+    }
+    --depth;                                                          // back to the parent
+    if (w.first_valid[parent] < 0) continue;                          // :417 no active sibling
+    const float p_old32 = w.path_pa[depth];                           // :422
+    const double p_old = (double)p_old32;
+    const int c0 = w.child_start[parent], nc = w.child_cnt[parent];
+    float s_tree = 0.0f, sum_mb = 0.0f;                               // :429-433, left to right
+    for (int i = 0; i < nc; ++i) {
+      const int c = w.sib[c0 + i];
+      const float mbv = w.mb[c];
+      s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), w.ms[c]), 0.0f));
+      sum_mb = __fadd_rn(sum_mb, mbv);
     }
     double ms_denom = __dsub_rn(1.0, old_ms_rej);                     // :424
     if (ms_denom < kEps) ms_denom = kEps;
     double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
     if (S < kEps) S = kEps;                                           // :435
     const double p_new = __ddiv_rn(S, __dsub_rn(__dadd_rn(S, 1.0), p_old));   // :439
+    const double old_mb_rej = (double)w.mb[cand];                     // :451
+    const double mb_rej = __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S);
     const float ms_denom32 = __double2float_rn(ms_denom);
     const float S32 = __double2float_rn(S);
-    for (int i = lane; i < ns; i += 32) {                             // :443-448
-      const int c = s_sib[i];
+    for (int i = 0; i < nc; ++i) {                                    // :443-448
+      const int c = w.sib[c0 + i];
       if (!w.valid[c]) continue;
       const float msv = w.ms[c], mbv = w.mb[c];
       w.ms[c] = __fdiv_rn(msv, ms_denom32);
       w.mb[c] = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
     }
-    if (lane == 0) {
-      const int cand = w.path[depth + 1];
-      const double old_mb_rej = (double)w.mb[cand];                   // :451-452
-      w.mb[cand] = __double2float_rn(
-          __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S));
-      const float p_new32 = __double2float_rn(p_new);                 // :440 (sticky)
-      w.stored_pa[parent] = p_new32;
-      w.sticky_t[parent] = (int16_t)T;
-      w.reset_t[parent] = (int16_t)T;
-      w.path_pa[depth] = p_new32;
-      ++T;
-    }
-    __syncwarp();
+    w.mb[cand] = __double2float_rn(mb_rej);                           // :452
+    const float p_new32 = __double2float_rn(p_new);                   // :440, direct assignment
+    w.stored_pa[parent] = p_new32;
+    w.sticky_t[parent] = (int16_t)T;
+    w.reset_t[parent] = (int16_t)T;
+    w.path_pa[depth] = p_new32;
+    ++T;
   }
-  if (lane != 0) return;
   // :480-524 output
   int d = 0;
   for (int c = accepted; c >= 0; c = w.parent[c]) w.path[d++] = (int16_t)c;   // reversed path
@@ -436,28 +399,34 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, Walk
   write_counts(p, b, n_out > p.out_stride ? -2 : n_out, n_out, n_out > 0 ? n_out - 1 : 0, accepted);
 }
 
+// Request of `row`: the warp finds the last request whose first row is <= row
+// with one parallel sweep over row_indptr (no dependent load chain).
+__device__ __forceinline__ int find_request(const int32_t* row_indptr, int batch, int row) {
+  const int lane = threadIdx.x & 31;
+  int best = 0;
+  for (int base = 0; base < batch; base += 32) {
+    const int b = base + lane;
+    const bool le = b < batch && row_indptr[b] <= row;
+    const unsigned m = __ballot_sync(0xffffffffu, le);
+    if (m) best = base + 31 - __clz(m);
+    if (m != 0xffffffffu) break;
+  }
+  return best;
+}
+
 __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams p) {
   __shared__ Part s_warp[kWarps];
-  __shared__ Part s_rank[kMaxCluster];
-  __shared__ __align__(8) uint64_t s_bar;
   __shared__ int s_red_i[kWarps];
   __shared__ int s_flag;
   __shared__ float s_m, s_s, s_qmax;
-  __shared__ int s_arg, s_tie, s_ok;
+  __shared__ int s_arg, s_tie;
   __shared__ int s_b, s_lo, s_n;
   extern __shared__ __align__(16) uint8_t dyn_smem[];
-  WalkSmem& w = *reinterpret_cast<WalkSmem*>(dyn_smem);
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nchunks = gridDim.x;
   const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
-  const int base = rank * kChunk;
-
-  if (rank == 0 && tid == 0) {
-    mbar_init_local(&s_bar, (uint32_t)p.cluster);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
+  const int base = chunk * kChunk;
 
   // ---- 1. load the chunk and reduce each thread's values ---------------------
   uint32_t raw[kVecPerThread * 4];
@@ -480,8 +449,6 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
       }
     }
   }
-  // rank 0's barrier must be initialised before any rank arrives on it
-  cluster.sync();
   if (p.use_temp) {
 #pragma unroll
     for (int i = 0; i < kVecPerThread * 4; ++i) raw[i] = scale_pair(raw[i], p.inv_temp);
@@ -506,13 +473,13 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
       if (x0 == mt && e0 + 2 * j < p.vocab) first = e0 + 2 * j;
     }
   }
-  Part part{mt, (double)st, first};
-  if (mt == -INFINITY) part = Part{-INFINITY, 0.0, INT_MAX};
+  Part part{(double)st, mt, first};
+  if (first == INT_MAX) part = Part{0.0, -INFINITY, INT_MAX};
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     Part other;
-    other.m = __shfl_xor_sync(0xffffffffu, part.m, o);
     other.s = __shfl_xor_sync(0xffffffffu, part.s, o);
+    other.m = __shfl_xor_sync(0xffffffffu, part.m, o);
     other.idx = __shfl_xor_sync(0xffffffffu, part.idx, o);
     part = (lane & o) ? merge(other, part) : merge(part, other);
   }
@@ -521,32 +488,30 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
   if (tid == 0) {
     Part c = s_warp[0];
     for (int i = 1; i < kWarps; ++i) c = merge(c, s_warp[i]);
-    // push this CTA's partial into rank 0's slot and arrive on its barrier
-    Part* dst = cluster.map_shared_rank(&s_rank[rank], 0);
-    *dst = c;
-    mbar_arrive_remote(mapa_shared(&s_bar, 0));
-  }
-  if (rank != 0) return;
-
-  // ---- 2. row statistics (rank 0) ---------------------------------------------
-  if (tid == 0) {
-    s_ok = mbar_wait_cluster(&s_bar, 0);
-    if (s_ok) {
-      Part r = s_rank[0];
-      for (int i = 1; i < p.cluster; ++i) r = merge(r, s_rank[i]);
-      const float sf = (float)r.s;
-      const float qmax = round_to_bf16(__fdiv_rn(1.0f, sf));
-      s_m = r.m;
-      s_s = sf;
-      s_qmax = qmax;
-      s_arg = r.idx;
-      // a smaller value can only tie with the max after rounding if the
-      // largest bf16 value below m already does
-      s_tie = (r.m > -INFINITY) && (prob_bf16(prev_bf16(r.m), r.m, sf) == qmax);
-    }
+    p.part_ws[(int64_t)row * nchunks + chunk] = c;
+    unsigned prev;    // release: this chunk's partial; acquire: the row's others
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.row_ctr[row]) : "memory");
+    s_flag = (prev == (unsigned)(nchunks - 1));
   }
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_flag) return;
+
+  // ---- 2. row statistics (last chunk of the row) ------------------------------
+  if (tid == 0) {
+    const Part* pp = p.part_ws + (int64_t)row * nchunks;
+    Part r{__ldcg(&pp[0].s), __ldcg(&pp[0].m), __ldcg(&pp[0].idx)};
+    for (int i = 1; i < nchunks; ++i) r = merge(r, Part{__ldcg(&pp[i].s), __ldcg(&pp[i].m), __ldcg(&pp[i].idx)});
+    const float sf = (float)r.s;
+    const float qmax = round_to_bf16(__fdiv_rn(1.0f, sf));
+    s_m = r.m;
+    s_s = sf;
+    s_qmax = qmax;
+    s_arg = r.idx;
+    // a smaller value can only tie with the max after rounding if the
+    // largest bf16 value below m already does
+    s_tie = (r.m > -INFINITY) && (prob_bf16(prev_bf16(r.m), r.m, sf) == qmax);
+  }
+  __syncthreads();
   if (s_tie) {
     int best = INT_MAX;
     for (int e = tid; e < p.vocab; e += kThreads) {
@@ -558,31 +523,29 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
     best = block_reduce_min(best, s_red_i);
     if (tid == 0) s_arg = best;
   }
-  if (tid == 0) {
-    int lo = 0, hi = p.batch - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (p.row_indptr[mid] <= row) lo = mid;
-      else hi = mid - 1;
+  if (warp == 0) {
+    const int b = find_request(p.row_indptr, p.batch, row);
+    if (lane == 0) {
+      RowStat rs;
+      rs.m = s_m;
+      rs.s = s_s;
+      rs.argmax = s_arg;
+      rs.flags = s_tie;
+      p.row_ws[row] = rs;
+      s_b = b;
+      s_lo = p.row_indptr[b];
+      s_n = p.row_indptr[b + 1] - s_lo;
+      unsigned prev;    // release: this row's stats; acquire: every earlier row's
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.req_ctr[b]) : "memory");
+      s_flag = (prev == (unsigned)(s_n - 1));
     }
-    RowStat rs;
-    rs.m = s_m;
-    rs.s = s_s;
-    rs.argmax = s_arg;
-    rs.flags = s_tie;
-    p.row_ws[row] = rs;
-    s_b = lo;
-    s_lo = p.row_indptr[lo];
-    s_n = p.row_indptr[lo + 1] - s_lo;
-    unsigned prev;    // release: this row's stats; acquire: every earlier row's
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.req_ctr[lo]) : "memory");
-    s_flag = (prev == (unsigned)(s_n - 1));
   }
   __syncthreads();
   if (!s_flag) return;
 
   // ---- 3. tree walk (last row CTA of the request) ----------------------------
   const int b = s_b, lo = s_lo, n = s_n;
+  const WalkSmem w = walk_smem(dyn_smem, p.max_nodes);
   if (n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (tid == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
@@ -621,24 +584,40 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
     return;
   }
   if (tid == 0) {
-    for (int i = 0; i < n; ++i) w.first_child[i] = -1;
-    for (int i = n - 1; i >= 1; --i) {                                 // ascending child lists
+    // children in ascending order: linked lists and a contiguous (CSR) copy
+    for (int i = 0; i < n; ++i) {
+      w.first_child[i] = -1;
+      w.child_cnt[i] = 0;
+    }
+    for (int i = n - 1; i >= 1; --i) {
       const int par = w.parent[i];
       w.next_sib[i] = w.first_child[par];
       w.first_child[par] = (int16_t)i;
+      w.child_cnt[par]++;
     }
     w.next_sib[0] = -1;
-    for (int i = 0; i < n; ++i) w.first_valid[i] = w.first_child[i];
+    int o = 0;
+    for (int i = 0; i < n; ++i) {
+      w.child_start[i] = (int16_t)o;
+      for (int c = w.first_child[i]; c >= 0; c = w.next_sib[c]) w.sib[o++] = (int16_t)c;
+      w.first_valid[i] = w.first_child[i];
+    }
     if (!p.traversal) walk_greedy(p, b, lo, w);
   }
   __syncthreads();
-  if (p.traversal && warp == 0) walk_traversal(p, b, lo, n, w);
+  if (p.traversal && tid == 0) walk_traversal(p, b, lo, n, w);
 }
 
-size_t ws_layout(int num_rows, size_t* off_rows, size_t* off_qctr) {
+size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, size_t* off_rctr,
+                 size_t* off_qctr) {
+  const int nchunks = (vocab + kChunk - 1) / kChunk;
   size_t o = 0;
+  *off_parts = o;
+  o = align_up(o + (size_t)num_rows * nchunks * sizeof(Part), 256);
   *off_rows = o;
   o = align_up(o + (size_t)num_rows * sizeof(RowStat), 256);
+  *off_rctr = o;
+  o = align_up(o + (size_t)num_rows * sizeof(unsigned), 256);
   *off_qctr = o;
   o = align_up(o + (size_t)num_rows * sizeof(unsigned), 256);
   return o;
@@ -654,50 +633,36 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   if (p.max_nodes > PTS_MAX_TREE_NODES)
     return set_error(PTS_ERR_CAPACITY, "max_nodes %d above PTS_MAX_TREE_NODES %d", p.max_nodes,
                      PTS_MAX_TREE_NODES);
-  if (p.vocab > kMaxCluster * kChunk)
-    return set_error(PTS_ERR_UNSUPPORTED, "vocab %d above %d", p.vocab, kMaxCluster * kChunk);
+  if (p.vocab > kMaxChunks * kChunk)
+    return set_error(PTS_ERR_UNSUPPORTED, "vocab %d above %d", p.vocab, kMaxChunks * kChunk);
   PTS_CHECK_ARG(p.out_stride >= 1, "out_stride must be positive");
   PTS_CHECK_ARG(temperature > 0.0f, "temperature must be positive");
   if (p.num_rows > 65535) return set_error(PTS_ERR_CAPACITY, "num_rows %d above 65535", p.num_rows);
-  size_t orw, oqc;
-  const size_t need = ws_layout(p.num_rows, &orw, &oqc);
+  size_t opt, orw, orc, oqc;
+  const size_t need = ws_layout(p.num_rows, p.vocab, &opt, &orw, &orc, &oqc);
   if (!workspace || ws_bytes < need)
     return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", ws_bytes, need);
   PTS_CHECK_ARG(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
   char* ws = (char*)workspace;
-  p.cluster = (p.vocab + kChunk - 1) / kChunk;
+  const int nchunks = (p.vocab + kChunk - 1) / kChunk;
+  p.part_ws = (Part*)(ws + opt);
   p.row_ws = (RowStat*)(ws + orw);
+  p.row_ctr = (unsigned*)(ws + orc);
   p.req_ctr = (unsigned*)(ws + oqc);
   p.traversal = traversal;
   p.use_temp = (temperature != 1.0f);
   p.inv_temp = 1.0f / temperature;
   p.vec_ok = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
-  PTS_CUDA_TRY(cudaMemsetAsync(ws + oqc, 0, need - oqc, stream));
-  static bool smem_attr = false;
-  if (!smem_attr) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WalkSmem)));
-    smem_attr = true;
+  PTS_CUDA_TRY(cudaMemsetAsync(ws + orc, 0, need - orc, stream));
+  const size_t smem = walk_smem_bytes(p.max_nodes);
+  static size_t smem_attr = 0;
+  if (smem > smem_attr) {
+    PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      (int)cudaSharedmemCarveoutMaxShared));
+    smem_attr = smem;
   }
-  if (p.cluster > 8) {
-    static bool nonportable = false;
-    if (!nonportable) {
-      PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-      nonportable = true;
-    }
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.cluster, p.num_rows, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = sizeof(WalkSmem);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  PTS_CUDA_TRY(cudaLaunchKernelEx(&cfg, accept_kernel, p));
+  accept_kernel<<<dim3(nchunks, p.num_rows), kThreads, smem, stream>>>(p);
   return launch_status("accept_kernel");
 }
 
@@ -707,9 +672,9 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
 using namespace pts;
 
 extern "C" size_t pts_accept_workspace_size(int num_rows, int vocab) {
-  size_t a, b;
+  size_t a, b, c, d;
   if (num_rows <= 0 || vocab <= 0) return 0;
-  return ws_layout(num_rows, &a, &b);
+  return ws_layout(num_rows, vocab, &a, &b, &c, &d);
 }
 
 extern "C" int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
