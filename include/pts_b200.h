@@ -80,6 +80,24 @@ int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32
                          int32_t* out_counts, int out_stride, void* workspace,
                          size_t workspace_bytes, pts_stream_t stream);
 
+/* pts_accept_traversal without a workspace argument.  No counterpart in the
+ * reference: it is for callers that cannot allocate device memory (a host
+ * program holding only device pointers handed over by another runtime, or a
+ * server whose device memory is planned up front and may not call cudaMalloc
+ * later).  Scratch comes from a fixed 2 MiB device array inside the library
+ * (present on every GPU that loads it, until exit); sizes needing more are
+ * rejected with PTS_ERR_CAPACITY.  The first call on a device looks up that
+ * array's device address -- make it before any stream capture.  Calls share
+ * the array: calls whose kernels overlap on the GPU race. */
+int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride,
+                                 const int32_t* row_indptr, const int32_t* parents,
+                                 const int32_t* tokens, const float* draft_probs, int batch,
+                                 int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                                 float temperature, float top_p, int do_sample,
+                                 uint64_t philox_seed, uint64_t philox_offset, int32_t* out_tokens,
+                                 int32_t* out_hidden, int32_t* out_counts, int out_stride,
+                                 pts_stream_t stream);
+
 /* ------------------------------------------------------------------ paged KV
  * Per appended token t: batch_indices[t] = b and positions[t] = seq_lens[b] -
  * (append_indptr[b+1] - append_indptr[b]) + (t - append_indptr[b]).

@@ -34,6 +34,8 @@ SIGNATURES = {
                                     C.c_int, vp, sz, vp]),
     "pts_accept_traversal": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, f32, f32,
                                        C.c_int, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
+    "pts_accept_traversal_noalloc": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64,
+                                               f32, f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp]),
     "pts_batch_positions": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_kv_append": (C.c_int, [vp, vp, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, vp]),

@@ -40,6 +40,8 @@
 #include <float.h>
 #include <limits.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace pts {
@@ -731,4 +733,72 @@ extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, 
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
   return accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// Traversal acceptance that allocates nothing.
+//
+// Some callers cannot hand this library a workspace: a host program that only
+// receives device pointers from another runtime and has no device allocator
+// of its own, or a serving process whose device memory is planned once at
+// start-up and may not call cudaMalloc afterwards (cudaMalloc can synchronise
+// the device and fragments the planned pool).  For them the scratch that
+// pts_accept_traversal takes from the caller lives instead in the fixed
+// device array below.  The array exists in every GPU that loads the library
+// and stays there until the process exits.
+namespace pts {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;   // 2 MiB
+static __device__ __align__(256) uint8_t g_accept_scratch[kNoAllocScratchBytes];
+
+// The array's name in host code is only a host-side handle; the kernel needs
+// the device address, looked up once per device with that device current.
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[256] = {};
+  int dev = 0;
+  PTS_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) return set_error(PTS_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_accept_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(PTS_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return PTS_OK;
+}
+
+}  // namespace
+}  // namespace pts
+
+// Same arguments and results as pts_accept_traversal, without the workspace.
+// The first call on a device looks up the scratch array's device address;
+// make that first call before capturing the stream into a CUDA graph.  All
+// calls share the one array (its counters are cleared at the start of every
+// call), so two calls whose kernels overlap on the same GPU (for example on
+// two streams at once) race and must be serialised by the caller.  Sizes whose scratch exceeds 2 MiB (for example more than 4096
+// tree rows at a 262144-entry vocabulary) are rejected with PTS_ERR_CAPACITY.
+extern "C" int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                                            const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                                            int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                                            float temperature, float top_p, int do_sample, uint64_t philox_seed,
+                                            uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                                            int32_t* out_counts, int out_stride, pts_stream_t stream) {
+  if (num_rows <= 0 || vocab <= 0) return set_error(PTS_ERR_INVALID, "need num_rows > 0 and vocab > 0");
+  size_t a, b, c, d;
+  const size_t need = ws_layout(num_rows, vocab, &a, &b, &c, &d);
+  if (need > kNoAllocScratchBytes)
+    return set_error(PTS_ERR_CAPACITY,
+                     "pts_accept_traversal_noalloc: %d rows at vocab %d need %zu bytes of scratch, above the fixed %zu",
+                     num_rows, vocab, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != PTS_OK) return rc;
+  return pts_accept_traversal(logits, row_stride, row_indptr, parents, tokens, draft_probs, batch, num_rows, vocab,
+                              max_nodes, eos_token_id, temperature, top_p, do_sample, philox_seed, philox_offset,
+                              out_tokens, out_hidden, out_counts, out_stride, scratch, kNoAllocScratchBytes, stream);
 }
