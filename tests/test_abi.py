@@ -1,0 +1,39 @@
+"""The C-ABI library loads and exports every function include/pts_b200.h declares
+(no GPU needed: nothing is called except the error-string and version getters)."""
+import os
+import re
+
+from parallel_tree_spec_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "pts_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pts_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    lib = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version_and_error_string():
+    lib = _lib.lib()
+    assert lib.pts_version() >= 1
+    assert isinstance(lib.pts_last_error(), bytes)
+
+
+def test_host_side_argument_checks_need_no_gpu():
+    lib = _lib.lib()
+    # null pointers are rejected before anything touches a device
+    rc = lib.pts_accept_greedy(None, 0, None, None, None, 1, 1, 10, 1, -1, None, None, None, 1, None, 0, None)
+    assert rc == _lib.PTS_ERR_INVALID
+    rc = lib.pts_kv_append(None, None, 0, 0, None, None, None, None, None, 1, 8, 128, 16, 10, 2, None)
+    assert rc == _lib.PTS_ERR_INVALID
+    assert lib.pts_accept_workspace_size(1040, 128256) > 0
