@@ -1,31 +1,35 @@
 // Tree-masked paged attention on sm_100a (TMA + tcgen05 + TMEM).
 //
-// Work unit (one CTA): request b, KV head h and a group of up to 272 query
+// Work unit (one CTA): request b, KV head h and a group of up to 264 query
 // rows.  Query rows are (tree node, query head of h's GQA group) pairs, head
 // fastest.  Rows 0-255 of the group form two 128-row tensor-core tiles; the
-// remaining up to 16 rows (for example the 65th node of a 65-node tree with 4
-// heads per KV head) run on one warp with mma.sync from the same staged K/V.
+// remaining up to 8 rows (for example the 65th node of a 65-node tree with 4
+// heads per KV head) run on mma.sync from the same staged K/V.
 //
-// Per 64-token KV block (four 16-token pages):
-//   warp 0 (TMA)      loads K and V of the four pages into a 6-stage ring
-//                     (128-byte swizzle, two 64-column halves of D each);
-//   warp 1 (MMA)      S_t = Q_t K^T with Q_t resident in TMEM (M=128, N=64,
-//                     K=128), then O_t += P_t V with P_t in TMEM (M=128, N=128,
-//                     K=64); every operand descriptor is a base descriptor plus
-//                     a compile-time offset, issued from a converged warp;
-//   warps 2-5, 6-9    one softmax warpgroup per tile: read S_t from TMEM, apply
-//                     the scale and the tree mask, keep a running max and sum
-//                     per row (O_t is rescaled in TMEM only when the max grows
-//                     by more than 2^8), write P_t as bf16 into the first 32
-//                     columns of S_t, and at the end normalise O_t;
-//   warps 10-13       the remainder rows, FA2-style on mma.sync m16n8k16, each
-//                     warp taking 16 of the block's 64 tokens with its own
-//                     running max/sum; the four partial results are merged at
-//                     the end (legacy mma.sync is slow on sm_100, so one warp
-//                     alone could not keep pace with the tensor-core tiles).
-// Reading A from TMEM keeps the tensor pipe at its rate: with both operands in
-// shared memory a tcgen05 MMA is bound by ~128 bytes/clock of operand reads.
-// TMEM (512 columns): Q_t at 64t, S_t/P_t at 128 + 64t, O_t at 256 + 128t.
+// Per 64-token KV block (four 16-token pages), 14 warps:
+//   warps 10-13       TMA producers: warp 10 + w loads page w of the block (K
+//                     and V, two 64-column halves each, 128-byte swizzle) into
+//                     a 4-stage ring three blocks ahead of the consumers, so the
+//                     copies are spread over the four schedulers; with
+//                     remainder rows they then compute those for the current
+//                     block, transposed on mma.sync m16n8k16: S^T = K Q^T (16
+//                     tokens x 8 rows per warp), P^T handed to the next MMA by
+//                     movmatrix, O^T += V^T P^T, each warp with its own running
+//                     max/sum, the four partials merged at the end;
+//   warps 1 and 0     one MMA issuer per tile: S_t = Q_t K^T with Q_t resident in
+//                     TMEM (A from TMEM, M=128, N=64, K=128), O_t += P_t V with
+//                     P_t in shared memory (M=128, N=128, K=64).  The scores of
+//                     block j+1 are issued as soon as the softmax warps have
+//                     copied S_t(j) into registers, so the tensor pipe computes
+//                     them while the exponentials of block j run;
+//   warps 2-5, 6-9    one softmax warpgroup per tile: one thread per row reads
+//                     its 64 scores with a single TMEM load, applies the scale
+//                     and the tree mask, keeps a running max and sum (O_t is
+//                     rescaled in TMEM only when the max grows by more than
+//                     2^8), writes P_t as bf16 into one of two shared-memory
+//                     buffers in the MMA's 128-byte-swizzled layout, and at the
+//                     end normalises O_t.
+// TMEM (512 columns): Q_t at 64t, S_t at 128 + 64t, O_t at 256 + 128t.
 //
 // The tree mask: KV slots below kv_len - N are the prefix (always visible);
 // slot kv_len - N + j is visible to row i when bit j of i's mask is set.
@@ -42,18 +46,19 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kBlockN = 64;           // KV tokens per block
 constexpr int kPage = 16;
 constexpr int kD = 128;
 constexpr int kTensorRows = 256;      // two 128-row tiles
-constexpr int kSyncRows = 16;         // remainder rows on mma.sync
+constexpr int kSyncRows = 8;          // remainder rows on mma.sync (the N of its MMAs)
 constexpr int kGroupRows = kTensorRows + kSyncRows;
-constexpr int kThreads = 448;         // warp 0 TMA, 1 MMA, 2-9 softmax, 10-13 remainder rows
+constexpr int kThreads = 448;         // warps 0-1 MMA, 2-9 softmax, 10-13 TMA producers + remainder rows
 constexpr int kSyncWarps = 4;
 constexpr int kMaxSmemPages = 2048;   // page-table entries staged in shared memory
 constexpr uint32_t kKvHalf = kBlockN * 128;                   // [64 tokens x 64 dims] bf16
 constexpr uint32_t kStageBytes = 4 * kKvHalf;                 // K0 K1 V0 V1
+constexpr uint32_t kPBytes = 128 * kBlockN * 2;               // one P buffer: [128 rows x 64 tokens] bf16
 constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kColQ = 0, kColS = 128, kColO = 256;
 
@@ -61,22 +66,25 @@ struct __align__(8) Bars {
   uint64_t q_ready;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t o_full;
-  uint64_t drain;
+  uint64_t s_full[2];    // S_t(j) computed                  (tcgen05.commit)
+  uint64_t s_free[2];    // S_t(j) copied out of TMEM          (4 softmax warps)
+  uint64_t p_full[2];    // P_t(j) in shared memory, O_t ready (4 softmax warps)
+  uint64_t p_empty[2][2];  // PV_t(j) done: P buffer j % 2 free   (tcgen05.commit)
+  uint64_t o_full[2];
+  uint64_t drain[2];
   uint32_t tmem;
   int abort;
 };
 
-constexpr uint32_t kQxStride = 272;                           // padded row of the remainder queries
 constexpr uint32_t kOffKV = 0;
-constexpr uint32_t kOffQx = kOffKV + kStages * kStageBytes;
-constexpr uint32_t kOffMerge = kOffQx + kSyncRows * kQxStride;   // remainder partials of warps 11-13
-constexpr uint32_t kMergeFloats = 68;                            // per lane: 64 O + 2 m + 2 l
+constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;        // 1024-aligned (swizzle atoms)
+constexpr uint32_t kOffMerge = kOffP + 4 * kPBytes;                // remainder partials of warps 11-13
+constexpr uint32_t kMergeFloats = 36;                             // per lane: 32 O + 2 m + 2 l
 constexpr uint32_t kOffPages = kOffMerge + (kSyncWarps - 1) * 32 * kMergeFloats * 4;
 constexpr uint32_t kOffBars = kOffPages + kMaxSmemPages * 4;
 constexpr uint32_t kSmemBytes = kOffBars + 1024 + 1024;       // bars + alignment slack
+static_assert(kOffP % 1024 == 0, "P tiles must sit on 1024-byte swizzle atoms");
+static_assert(kSmemBytes <= 232448, "shared memory above the 227 KB per-CTA limit");
 
 struct AttnParams {
   const uint16_t* q;
@@ -100,14 +108,34 @@ __device__ __forceinline__ void record_abort(Bars& bars, const AttnParams& p, in
 
 __device__ __forceinline__ bool aborted(const Bars& bars) { return *(volatile const int*)&bars.abort != 0; }
 
-// Is KV slot `kv` visible to tree row `node` of a request with this prefix?
-__device__ __forceinline__ bool visible(const AttnParams& p, const uint64_t* mrow, int node, int kv, int kv_len,
-                                        int prefix) {
-  if (kv >= kv_len) return false;
-  if (kv < prefix) return true;
-  const int tn = kv - prefix;
-  if (p.mask_bits == nullptr) return tn <= node;
-  return (tn / 64 < p.mask_words) && ((__ldg(mrow + tn / 64) >> (tn % 64)) & 1ull);
+__device__ __forceinline__ uint64_t low_bits(int n) {          // n in [0, 64]
+  return n >= 64 ? ~0ull : ((1ull << n) - 1ull);
+}
+
+// Visibility of the 64 KV slots kv0 .. kv0+63 to tree row `node` (bit c = slot
+// kv0 + c): the prefix is visible, tree slot j is visible when bit j of the
+// row's mask is set (j <= node without a mask), slots past kv_len are not.
+__device__ __forceinline__ uint64_t block_visibility(const AttnParams& p, const uint64_t* mrow, int node, int kv0,
+                                                     int kv_len, int prefix) {
+  const int np = prefix - kv0;
+  if (np >= kBlockN) return ~0ull;
+  uint64_t v = np > 0 ? low_bits(np) : 0ull;
+  const int c0 = max(np, 0);
+  const int cend = min(kBlockN, kv_len - kv0);
+  if (c0 < cend) {
+    const int tn0 = kv0 + c0 - prefix;                           // tree slot of bit c0
+    uint64_t bits;
+    if (p.mask_bits == nullptr) {
+      bits = low_bits(max(0, min(64, node - tn0 + 1)));
+    } else {
+      const int w = tn0 >> 6, sh = tn0 & 63;
+      const uint64_t lo = w < p.mask_words ? __ldg(mrow + w) : 0ull;
+      const uint64_t hi = (w + 1) < p.mask_words ? __ldg(mrow + w + 1) : 0ull;
+      bits = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;
+    }
+    v |= (bits & low_bits(cend - c0)) << c0;
+  }
+  return v;
 }
 
 // Byte offset of (row, 16-byte chunk) in a 128-byte-swizzled [rows x 64] tile.
@@ -143,15 +171,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars.q_ready, 4 * n_tiles);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars.kv_full[s], 1);
-      mbar_init(&bars.kv_empty[s], sync_rows > 0 ? 1 + kSyncWarps : 1);
+      mbar_init(&bars.kv_full[s], kSyncWarps);          // one expect_tx arrival per producer warp
+      mbar_init(&bars.kv_empty[s], n_tiles + (sync_rows > 0 ? kSyncWarps : 0));
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars.s_full[t], 1);
+      mbar_init(&bars.s_free[t], 4);
       mbar_init(&bars.p_full[t], 4);
+      mbar_init(&bars.p_empty[t][0], 1);
+      mbar_init(&bars.p_empty[t][1], 1);
+      mbar_init(&bars.o_full[t], 1);
+      mbar_init(&bars.drain[t], 1);
     }
-    mbar_init(&bars.o_full, 1);
-    mbar_init(&bars.drain, 1);
     bars.abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&kv_map);
@@ -168,75 +199,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars.tmem;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int issued = 0;
-      for (int j = 0; j < n_blocks; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&bars.kv_empty[s], ((j / kStages) + 1) & 1)) {
-          record_abort(bars, p, 11);
-          break;
-        }
-        if (aborted(bars)) break;
-        mbar_arrive_expect_tx(&bars.kv_full[s], kStageBytes);
-        uint8_t* st = smem + kOffKV + s * kStageBytes;
-#pragma unroll
-        for (int pg = 0; pg < kBlockN / kPage; ++pg) {
-          const int slot = (kBlockN / kPage) * j + pg;
-          const int phys = slot >= n_pages ? p.max_pages                                 // OOB -> zero fill
-                           : (slot < kMaxSmemPages ? spages[slot] : p.page_indices[p0 + slot]);
-          const int page = (phys >= 0 && phys < p.max_pages) ? phys : p.max_pages;
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tma_load_4d(st + half * kKvHalf + pg * (kPage * 128), &kv_map, &bars.kv_full[s], half * 64, h, 0,
-                        2 * page);
-            tma_load_4d(st + (2 + half) * kKvHalf + pg * (kPage * 128), &kv_map, &bars.kv_full[s], half * 64, h,
-                        0, 2 * page + 1);
-          }
-        }
-        issued = j + 1;
-      }
-      // wait for copies still in flight before the CTA can exit
-      for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&bars.kv_full[j % kStages], (j / kStages) & 1);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    const uint32_t id_qk = idesc_bf16_f32(128, kBlockN, 0, 0);
-    const uint32_t id_pv = idesc_bf16_f32(128, kD, 0, 1);
-    const uint64_t kd0 = smem_desc(smem_u32(smem + kOffKV), 16, 1024, kSwizzle128B);
-    const uint64_t vd0 = smem_desc(smem_u32(smem + kOffKV + 2 * kKvHalf), kKvHalf, 1024, kSwizzle128B);
-    const bool leader = elect_one();
-#define PTS_QK(T, S)                                                                                        \
+  if (warp == 0 || warp == 1) {
+    // ------------------------------------------------------------ MMA issuers, one warp per tile
+    const int t = warp == 1 ? 0 : 1;
+    if (t < n_tiles) {
+      const uint32_t id_qk = idesc_bf16_f32(128, kBlockN, 0, 0);
+      const uint32_t id_pv = idesc_bf16_f32(128, kD, 0, 1);
+      const uint64_t kd0 = smem_desc(smem_u32(smem + kOffKV), 16, 1024, kSwizzle128B);
+      const uint64_t vd0 = smem_desc(smem_u32(smem + kOffKV + 2 * kKvHalf), kKvHalf, 1024, kSwizzle128B);
+      const uint64_t pd0 = smem_desc(smem_u32(smem + kOffP + 2 * t * kPBytes), 16, 1024, kSwizzle128B);
+      const uint32_t s_col = tmem + kColS + 64 * t, q_col = tmem + kColQ + 64 * t, o_col = tmem + kColO + 128 * t;
+      const bool leader = elect_one();
+#define PTS_QK(S)                                                                                           \
   do {                                                                                                      \
     if (leader) {                                                                                           \
       _Pragma("unroll") for (int k = 0; k < kD / 16; ++k) {                                                 \
         const uint64_t bd = kd0 + (uint64_t)(((S) * kStageBytes + (k / 4) * kKvHalf + (k % 4) * 32) >> 4);  \
-        mma_bf16_ts(tmem + kColS + 64 * (T), tmem + kColQ + 64 * (T) + 8 * k, bd, id_qk, k > 0);           \
+        mma_bf16_ts(s_col, q_col + 8 * k, bd, id_qk, k > 0);                                                \
       }                                                                                                     \
-      mma_commit(&bars.s_full[T]);                                                                          \
+      mma_commit(&bars.s_full[t]);                                                                          \
     }                                                                                                       \
     __syncwarp();                                                                                           \
   } while (0)
-    bool ok = mbar_wait(&bars.q_ready, 0) && mbar_wait(&bars.kv_full[0], 0);
-    if (!ok && lane == 0) record_abort(bars, p, 21);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      PTS_QK(0, 0);
-      if (n_tiles > 1) PTS_QK(1, 0);
-    }
-    for (int j0 = 0; ok && j0 < n_blocks; j0 += kStages) {
+      bool ok = mbar_wait(&bars.q_ready, 0) && mbar_wait(&bars.kv_full[0], 0);
+      if (!ok && lane == 0) record_abort(bars, p, 21);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        PTS_QK(0);
+      }
+      for (int j0 = 0; ok && j0 < n_blocks; j0 += kStages) {
 #pragma unroll
-      for (int ss = 0; ss < kStages; ++ss) {
-        const int j = j0 + ss;
-        if (j >= n_blocks || !ok) break;
-        const int s1 = (ss + 1) % kStages;
-        const bool more = j + 1 < n_blocks;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (t >= n_tiles || !ok) break;
-          bool w_ok = mbar_wait(&bars.p_full[t], j & 1) && !aborted(bars);
+        for (int ss = 0; ss < kStages; ++ss) {
+          const int j = j0 + ss;
+          if (j >= n_blocks) break;
+          const int s1 = (ss + 1) % kStages;
+          if (j + 1 < n_blocks) {
+            // scores of block j+1 once K(j+1) is staged and S_t(j) has been read
+            const bool w_ok = mbar_wait(&bars.kv_full[s1], ((j + 1) / kStages) & 1) &&
+                              mbar_wait(&bars.s_free[t], j & 1) && !aborted(bars);
+            if (!__all_sync(0xffffffffu, w_ok)) {
+              if (lane == 0) record_abort(bars, p, 23);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            PTS_QK(s1);
+          }
+          const bool w_ok = mbar_wait(&bars.p_full[t], j & 1) && !aborted(bars);
           if (!__all_sync(0xffffffffu, w_ok)) {
             if (lane == 0) record_abort(bars, p, 24);
             ok = false;
@@ -246,33 +256,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) {
 #pragma unroll
             for (int k = 0; k < kBlockN / 16; ++k) {
+              const uint64_t ad = pd0 + (uint64_t)(((ss & 1) * kPBytes + k * 32) >> 4);
               const uint64_t bd = vd0 + (uint64_t)((ss * kStageBytes + k * 2048) >> 4);
-              mma_bf16_ts(tmem + kColO + 128 * t, tmem + kColS + 64 * t + 8 * k, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+              mma_bf16_ss(o_col, ad, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
             }
-            if (t == n_tiles - 1) mma_commit(&bars.kv_empty[ss]);
+            mma_commit(&bars.p_empty[t][ss & 1]);
+            mma_commit(&bars.kv_empty[ss]);
           }
           __syncwarp();
-          if (more) {
-            // S_t of the next block overwrites P_t only after this PV (in-order pipe)
-            w_ok = (t != 0 || mbar_wait(&bars.kv_full[s1], ((j + 1) / kStages) & 1));
-            if (!__all_sync(0xffffffffu, w_ok)) {
-              if (lane == 0) record_abort(bars, p, 23);
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            PTS_QK(t, s1);
-          }
         }
       }
-    }
 #undef PTS_QK
-    if (leader) {
-      mma_commit(&bars.o_full);
-      mma_commit(&bars.drain);
+      if (leader) {
+        mma_commit(&bars.o_full[t]);
+        mma_commit(&bars.drain[t]);
+      }
+      __syncwarp();
+      mbar_wait(&bars.drain[t], 0);
     }
-    __syncwarp();
-    mbar_wait(&bars.drain, 0);
   } else if (warp < 10) {
     // ------------------------------------------------------------ softmax warpgroups
     const int t = (warp - 2) >> 2;                      // tile of this warpgroup
@@ -284,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = active_tile && (t * 128 + r_local) < tensor_rows;
     const int node = R / p.g, hh = R % p.g;
     const uint64_t* mrow = p.mask_bits ? p.mask_bits + (int64_t)(q0 + node) * p.mask_words : nullptr;
+    const uint32_t prow = smem_u32(smem + kOffP + 2 * t * kPBytes) + r_local * 128;   // this row of P_t, buffer 0
+    const uint32_t pswz = (uint32_t)(r_local & 7);
     if (active_tile) {
       // this row's query into TMEM columns 64t.. (two bf16 per column)
       const uint16_t* qrow = p.q + ((int64_t)(q0 + node) * p.Hq + h * p.g + hh) * kD;
@@ -314,68 +317,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      uint32_t sr[64];
+      tmem_ld32_x2(tmem + lane_base + kColS + 64 * t, sr);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.s_free[t]);
+      // visibility: whole block for prefix blocks, else per slot
       const int kv0 = j * kBlockN;
-      // visibility of the block's 64 slots: prefix, tree part (mask or causal), kv_len
-      uint64_t vis = ~0ull;
-      if (!valid) {
-        vis = 0;
-      } else if (kv0 + kBlockN > prefix) {
-        vis = 0;
-        for (int c = 0; c < kBlockN; ++c) {
-          const int kv = kv0 + c;
-          bool v;
-          if (kv >= kv_len) v = false;
-          else if (kv < prefix) v = true;
-          else {
-            const int tn = kv - prefix;
-            v = p.mask_bits == nullptr ? (tn <= node)
-                                       : (tn / 64 < p.mask_words) && ((__ldg(mrow + tn / 64) >> (tn % 64)) & 1ull);
-          }
-          vis |= (uint64_t)v << c;
-        }
-      }
-      // pass 1: block max
-      float mblk = -INFINITY;
+      if (!valid || kv0 + kBlockN > prefix) {
+        const uint64_t vis = valid ? block_visibility(p, mrow, node, kv0, kv_len, prefix) : 0ull;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[32];
-        tmem_ld32(tmem + lane_base + kColS + 64 * t + 32 * half, sr);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if ((vis >> (32 * half + c)) & 1ull) mblk = fmaxf(mblk, __uint_as_float(sr[c]) * p.scale_log2);
+        for (int c = 0; c < kBlockN; ++c)
+          if (!((vis >> c) & 1ull)) sr[c] = __float_as_uint(-INFINITY);
       }
-      // lazy rescale: warp-uniform decision, per-row factors
-      const bool need = valid && (mblk > m_used + kRescaleThreshold);
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBlockN; c += 8) {
+        mx0 = fmax3(mx0, __uint_as_float(sr[c + 0]), __uint_as_float(sr[c + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = fmax3(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = fmax3(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      const float mblk = fmax3(mx0, mx1, fmaxf(mx2, mx3)) * p.scale_log2;
+      // lazy rescale: per-row factor, O_t touched only when some row needs it
+      const bool need = mblk > m_used + kRescaleThreshold;
       float alpha = 1.0f;
       if (need) {
         alpha = (m_used == -INFINITY) ? 0.0f : fast_exp2(m_used - mblk);
         l_sum *= alpha;
         m_used = mblk;
       }
-      // pass 2: P = exp2(x - m_used) as bf16 pairs into the first 32 columns of S_t
+      const float msub = m_used == -INFINITY ? 0.0f : m_used;
+      float ls0 = 0.0f, ls1 = 0.0f;
       uint32_t pk[32];
-      float ls = 0.0f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[32];
-        tmem_ld32(tmem + lane_base + kColS + 64 * t + 32 * half, sr);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const int cc = 32 * half + c;
-          const float e0 = ((vis >> cc) & 1ull) ? fast_exp2(__uint_as_float(sr[c]) * p.scale_log2 - m_used) : 0.0f;
-          const float e1 = ((vis >> (cc + 1)) & 1ull) ? fast_exp2(__uint_as_float(sr[c + 1]) * p.scale_log2 - m_used) : 0.0f;
-          ls += e0 + e1;
-          pk[cc / 2] = pack_bf16x2(e0, e1);
+      for (int c = 0; c < kBlockN; c += 2) {
+        const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -msub));
+        const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -msub));
+        ls0 += e0;
+        ls1 += e1;
+        pk[c / 2] = pack_bf16x2(e0, e1);
+      }
+      l_sum += ls0 + ls1;
+      // P buffer j % 2 is free once PV_t(j-2) has completed
+      if (j > 1) {
+        if (!mbar_wait(&bars.p_empty[t][j & 1], ((j >> 1) - 1) & 1)) {
+          record_abort(bars, p, 33);
+          ok = false;
+          break;
         }
       }
-      l_sum += ls;
-      tmem_st32(tmem + lane_base + kColS + 64 * t, pk);
-      tmem_st_wait();
-      // O_t is stable here: its last update (PV of the previous block) completed
-      // before this block's S_t was committed
+      const uint32_t pbuf = prow + (uint32_t)(j & 1) * kPBytes;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        st_shared_v4(pbuf + (((uint32_t)ch ^ pswz) << 4), pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      fence_proxy_async_smem();
       if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_t may be rescaled once its last update, PV_t(j-1), has completed
+        if (!mbar_wait(&bars.p_empty[t][(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          record_abort(bars, p, 35);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         for (int cb = 0; cb < 4; ++cb) {
           uint32_t o[32];
           const uint32_t oa = tmem + lane_base + kColO + 128 * t + 32 * cb;
@@ -384,17 +389,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
           tmem_st32(oa, o);
-          tmem_st_wait();
         }
+        tmem_st_wait();
       }
-      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.p_full[t]);
       if (aborted(bars)) ok = false;
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && mbar_wait(&bars.o_full, 0)) {
+    if (ok && mbar_wait(&bars.o_full[t], 0)) {
       tc_fence_after();
       const float inv = (valid && l_sum > 0.0f) ? 1.0f / l_sum : 0.0f;
       uint16_t* orow = p.out + ((int64_t)(q0 + node) * p.Hq + h * p.g + hh) * kD;
@@ -418,181 +422,217 @@ __global__ void __launch_bounds__(kThreads, 1)
       record_abort(bars, p, 32);
     }
   } else {
-    // ------------------------------------------------------------ remainder rows (mma.sync)
-    const int wr = warp - 10;                              // this warp's 16 tokens of every block
-    const int gq = lane >> 2, tq = lane & 3;               // fragment row group / column pair
-    const int rA = row0 + kTensorRows + gq, rB = rA + 8;  // this lane's two rows
-    const bool vA = gq < sync_rows, vB = gq + 8 < sync_rows;
-    const int nodeA = rA / p.g, nodeB = rB / p.g;
-    const uint64_t* mA = (p.mask_bits && vA) ? p.mask_bits + (int64_t)(q0 + nodeA) * p.mask_words : nullptr;
-    const uint64_t* mB = (p.mask_bits && vB) ? p.mask_bits + (int64_t)(q0 + nodeB) * p.mask_words : nullptr;
-    // without remainder rows these warps take no part in the ring (they do not
-    // gate kv_empty, so they must not wait on kv_full either)
-    if (sync_rows > 0) {
-      // remainder queries -> shared memory (padded rows), A fragments by ldmatrix
-      uint8_t* qx = smem + kOffQx;
-      for (int e = wr * 32 + lane; e < kSyncRows * 16; e += kSyncWarps * 32) {
-        const int r = e / 16, v = e % 16;
-        const int R = row0 + kTensorRows + r;
-        uint4 x = make_uint4(0, 0, 0, 0);
-        if (r < sync_rows)
-          x = *(const uint4*)(p.q + ((int64_t)(q0 + R / p.g) * p.Hq + h * p.g + R % p.g) * kD + 8 * v);
-        *(uint4*)(qx + r * kQxStride + 16 * v) = x;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kSyncWarps * 32) : "memory");
-      const uint32_t qx_s = smem_u32(qx);
-      const int mi = lane >> 3, rr = lane & 7;
-      uint32_t qa[8][4];
+    // ------------------------------------------------------------ TMA producers + remainder rows
+    // Warp 10 + w loads page w of every block (K and V, both 64-column halves)
+    // kAhead blocks in front of the consumers, so the TMA traffic is spread
+    // over the four schedulers; with remainder rows it then computes them for
+    // the current block (mma.sync, transposed).
+    const int wr = warp - 10;                              // this warp's page / 16 tokens of every block
+    const bool rem = sync_rows > 0;
+    const int gq = lane >> 2, tq = lane & 3;               // fragment group / thread in group
+    const int mi = lane >> 3, rr = lane & 7;               // ldmatrix: matrix / row supplied by this lane
+    auto produce = [&](int blk) -> bool {
+      const int s = blk % kStages;
+      const bool w_ok = mbar_wait_lazy(&bars.kv_empty[s], ((blk / kStages) + 1) & 1, 200) && !aborted(bars);
+      if (!__all_sync(0xffffffffu, w_ok)) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars.kv_full[s], kStageBytes / kSyncWarps);
+        const int slot = (kBlockN / kPage) * blk + wr;
+        const int phys = slot >= n_pages ? p.max_pages                                   // OOB -> zero fill
+                         : (slot < kMaxSmemPages ? spages[slot] : p.page_indices[p0 + slot]);
+        const int page = (phys >= 0 && phys < p.max_pages) ? phys : p.max_pages;
+        uint8_t* st = smem + kOffKV + s * kStageBytes + wr * (kPage * 128);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        ldmatrix_x4(qx_s + (rr + 8 * (mi & 1)) * kQxStride + 2 * (16 * kk + 8 * (mi >> 1)), qa[kk][0], qa[kk][1],
-                    qa[kk][2], qa[kk][3]);
-      float o[16][4];
-#pragma unroll
-      for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
-      float mA_run = -INFINITY, mB_run = -INFINITY, lA = 0.0f, lB = 0.0f;
-      const uint32_t kv_s = smem_u32(smem + kOffKV);
-      bool ok = true;
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&bars.kv_full[s], (j / kStages) & 1) || aborted(bars)) {
-          if (lane == 0) record_abort(bars, p, 41);
-          ok = false;
-          break;
+        for (int half = 0; half < 2; ++half) {
+          tma_load_4d(st + half * kKvHalf, &kv_map, &bars.kv_full[s], half * 64, h, 0, 2 * page);
+          tma_load_4d(st + (2 + half) * kKvHalf, &kv_map, &bars.kv_full[s], half * 64, h, 0, 2 * page + 1);
         }
-        const uint32_t kb = kv_s + s * kStageBytes, vb = kb + 2 * kKvHalf;
-        float sc[2][4];
+      }
+      __syncwarp();
+      return true;
+    };
+    // Q^T as the B operand: column gq is remainder row gq
+    uint32_t qb[8][2];
+    {
+      const int R = row0 + kTensorRows + gq;
+      const bool v = gq < sync_rows;
+      const uint16_t* qrow = p.q + ((int64_t)(q0 + R / p.g) * p.Hq + h * p.g + R % p.g) * kD;
 #pragma unroll
-        for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+      for (int kk = 0; kk < 8; ++kk) {
+        qb[kk][0] = v ? *(const uint32_t*)(qrow + 16 * kk + 2 * tq) : 0u;
+        qb[kk][1] = v ? *(const uint32_t*)(qrow + 16 * kk + 8 + 2 * tq) : 0u;
+      }
+    }
+    // this lane's softmax rows: 2tq and 2tq+1
+    int rnode[2];
+    bool rvalid[2];
+    const uint64_t* rmask[2];
 #pragma unroll
-        for (int kp = 0; kp < 4; ++kp) {                   // k-steps 2kp, 2kp+1 (32 dims)
-          const int dim = 32 * kp + 8 * mi;
+    for (int i = 0; i < 2; ++i) {
+      const int r = 2 * tq + i;
+      rvalid[i] = r < sync_rows;
+      rnode[i] = (row0 + kTensorRows + r) / p.g;
+      rmask[i] = (p.mask_bits && rvalid[i]) ? p.mask_bits + (int64_t)(q0 + rnode[i]) * p.mask_words : nullptr;
+    }
+    float o[8][4];
 #pragma unroll
-          for (int n = 0; n < 2; ++n) {
-            uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(kb + (dim / 64) * kKvHalf + sw128(16 * wr + 8 * n + rr, (dim % 64) / 8), b0, b1, b2, b3);
-            mma_m16n8k16(sc[n], qa[2 * kp], b0, b1);
-            mma_m16n8k16(sc[n], qa[2 * kp + 1], b2, b3);
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+    const uint32_t kv_s = smem_u32(smem + kOffKV);
+    constexpr int kAhead = kStages - 1;
+    bool ok = true;
+    int produced = 0;
+    for (int blk = 0; ok && blk < min(kAhead, n_blocks); ++blk) {
+      ok = produce(blk);
+      if (ok) produced = blk + 1;
+    }
+    for (int j = 0; ok && j < n_blocks; ++j) {
+      if (j + kAhead < n_blocks) {
+        ok = produce(j + kAhead);
+        if (!ok) break;
+        produced = j + kAhead + 1;
+      }
+      if (!rem) continue;
+      const int s = j % kStages;
+      if (!mbar_wait(&bars.kv_full[s], (j / kStages) & 1) || aborted(bars)) {
+        ok = false;
+        break;
+      }
+      const uint32_t kb = kv_s + s * kStageBytes, vb = kb + 2 * kKvHalf;
+      // S^T (16 tokens x 8 rows), two accumulation chains
+      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int tok = 16 * wr + rr + 8 * (mi & 1), dim = 16 * kk + 8 * (mi >> 1);
+        uint32_t a[4];
+        ldmatrix_x4(kb + (dim / 64) * kKvHalf + sw128(tok, (dim % 64) / 8), a[0], a[1], a[2], a[3]);
+        if (kk & 1) mma_m16n8k16(sb, a, qb[kk][0], qb[kk][1]);
+        else mma_m16n8k16(sa, a, qb[kk][0], qb[kk][1]);
+      }
+      // element e: token gq + 8 (e >> 1), row 2tq + (e & 1)
+      float x[4];
+      const int kv0 = j * kBlockN;
+      const bool full = kv0 + kBlockN <= prefix;
+      uint64_t vis[2] = {~0ull, ~0ull};
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          vis[i] = rvalid[i] ? block_visibility(p, rmask[i], rnode[i], kv0, kv_len, prefix) : 0ull;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 16 * wr + gq + 8 * (e >> 1);
+        x[e] = ((vis[e & 1] >> c) & 1ull) && rvalid[e & 1] ? (sa[e] + sb[e]) * p.scale_log2 : -INFINITY;
+      }
+      float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
+#pragma unroll
+      for (int off = 4; off <= 16; off <<= 1) {
+        mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
+        mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], off));
+      }
+      float alpha[2], msub[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float nm = fmaxf(m_run[i], mx[i]);
+        alpha[i] = (m_run[i] == -INFINITY) ? 0.0f : fast_exp2(m_run[i] - nm);
+        m_run[i] = nm;
+        msub[i] = nm == -INFINITY ? 0.0f : nm;
+      }
+      float ex[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ex[e] = fast_exp2(x[e] - msub[e & 1]);
+      l_run[0] = l_run[0] * alpha[0] + ex[0] + ex[2];
+      l_run[1] = l_run[1] * alpha[1] + ex[1] + ex[3];
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= alpha[0];
+        o[mt][1] *= alpha[1];
+        o[mt][2] *= alpha[0];
+        o[mt][3] *= alpha[1];
+      }
+      // P^T as the B operand: (token 2tq.., row gq) by transposing the 8x8 blocks
+      const uint32_t pb0 = movmatrix_trans(pack_bf16x2(ex[0], ex[1]));
+      const uint32_t pb1 = movmatrix_trans(pack_bf16x2(ex[2], ex[3]));
+      // O^T (128 dims x 8 rows) += V^T P^T, A = V^T by transposing loads
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int tok = 16 * wr + 8 * (mi >> 1) + rr, dim = 16 * mt + 8 * (mi & 1);
+        uint32_t a[4];
+        ldmatrix_x4_trans(vb + (dim / 64) * kKvHalf + sw128(tok, (dim % 64) / 8), a[0], a[1], a[2], a[3]);
+        mma_m16n8k16(o[mt], a, pb0, pb1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.kv_empty[s]);
+    }
+    if (!ok && lane == 0) record_abort(bars, p, 41);
+    // the copies this warp issued must land before the CTA can exit
+    for (int blk = max(0, produced - kStages); blk < produced; ++blk)
+      mbar_wait(&bars.kv_full[blk % kStages], (blk / kStages) & 1);
+    if (rem) {
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
+      l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
+    }
+    // merge the four warps' partial results (same fragment layout in every warp)
+    float* slot = (float*)(smem + kOffMerge);
+    if (wr > 0) {
+      float* my = slot + ((wr - 1) * 32 + lane) * kMergeFloats;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) my[4 * mt + e] = o[mt][e];
+      my[32] = m_run[0];
+      my[33] = m_run[1];
+      my[34] = l_run[0];
+      my[35] = l_run[1];
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kSyncWarps * 32) : "memory");
+    if (wr == 0 && ok) {
+      float M[2] = {m_run[0], m_run[1]};
+      for (int w = 0; w < kSyncWarps - 1; ++w) {
+        const float* other = slot + (w * 32 + lane) * kMergeFloats;
+        M[0] = fmaxf(M[0], other[32]);
+        M[1] = fmaxf(M[1], other[33]);
+      }
+      float L[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float f = (m_run[i] == -INFINITY) ? 0.0f : fast_exp2(m_run[i] - M[i]);
+        L[i] = l_run[i] * f;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][i] *= f;
+          o[mt][2 + i] *= f;
+        }
+      }
+      for (int w = 0; w < kSyncWarps - 1; ++w) {
+        const float* other = slot + (w * 32 + lane) * kMergeFloats;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float f = (other[32 + i] == -INFINITY) ? 0.0f : fast_exp2(other[32 + i] - M[i]);
+          L[i] += other[34 + i] * f;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][i] += other[4 * mt + i] * f;
+            o[mt][2 + i] += other[4 * mt + 2 + i] * f;
           }
         }
-        const int kv0 = j * kBlockN + 16 * wr;
-        float mxA = -INFINITY, mxB = -INFINITY;
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int kv = kv0 + 8 * n + 2 * tq + e;
-            const float xa = (vA && visible(p, mA, nodeA, kv, kv_len, prefix)) ? sc[n][e] * p.scale_log2 : -INFINITY;
-            const float xb = (vB && visible(p, mB, nodeB, kv, kv_len, prefix)) ? sc[n][2 + e] * p.scale_log2 : -INFINITY;
-            sc[n][e] = xa;
-            sc[n][2 + e] = xb;
-            mxA = fmaxf(mxA, xa);
-            mxB = fmaxf(mxB, xb);
-          }
-        }
-#pragma unroll
-        for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-          mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o2));
-          mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o2));
-        }
-        const float nA = fmaxf(mA_run, mxA), nB = fmaxf(mB_run, mxB);
-        const float aA = (mA_run == -INFINITY) ? 0.0f : fast_exp2(mA_run - nA);
-        const float aB = (mB_run == -INFINITY) ? 0.0f : fast_exp2(mB_run - nB);
-        mA_run = nA;
-        mB_run = nB;
-        lA *= aA;
-        lB *= aB;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-          o[nt][0] *= aA;
-          o[nt][1] *= aA;
-          o[nt][2] *= aB;
-          o[nt][3] *= aB;
-        }
-        uint32_t pa[4];
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          const float e0 = nA == -INFINITY ? 0.0f : fast_exp2(sc[n][0] - nA);
-          const float e1 = nA == -INFINITY ? 0.0f : fast_exp2(sc[n][1] - nA);
-          const float e2 = nB == -INFINITY ? 0.0f : fast_exp2(sc[n][2] - nB);
-          const float e3 = nB == -INFINITY ? 0.0f : fast_exp2(sc[n][3] - nB);
-          lA += e0 + e1;
-          lB += e2 + e3;
-          pa[2 * n + 0] = pack_bf16x2(e0, e1);
-          pa[2 * n + 1] = pack_bf16x2(e2, e3);
-        }
-#pragma unroll
-        for (int np = 0; np < 8; ++np) {                   // two 8-dim n-tiles per ldmatrix.x4.trans
-          const int tok = 16 * wr + 8 * (mi & 1) + rr;
-          const int dim = 16 * np + 8 * (mi >> 1);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(vb + (dim / 64) * kKvHalf + sw128(tok, (dim % 64) / 8), b0, b1, b2, b3);
-          mma_m16n8k16(o[2 * np], pa, b0, b1);
-          mma_m16n8k16(o[2 * np + 1], pa, b2, b3);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.kv_empty[s]);
       }
 #pragma unroll
-      for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-        lA += __shfl_xor_sync(0xffffffffu, lA, o2);
-        lB += __shfl_xor_sync(0xffffffffu, lB, o2);
-      }
-      // merge the four warps' partial results (same fragment layout in every warp)
-      float* slot = (float*)(smem + kOffMerge);
-      if (wr > 0) {
-        float* my = slot + ((wr - 1) * 32 + lane) * kMergeFloats;
+      for (int i = 0; i < 2; ++i) {
+        if (!rvalid[i]) continue;
+        const int R = row0 + kTensorRows + 2 * tq + i;
+        uint16_t* orow = p.out + ((int64_t)(q0 + R / p.g) * p.Hq + h * p.g + R % p.g) * kD;
+        const float inv = L[i] > 0.0f ? 1.0f / L[i] : 0.0f;
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) my[4 * nt + e] = o[nt][e];
-        my[64] = mA_run;
-        my[65] = mB_run;
-        my[66] = lA;
-        my[67] = lB;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kSyncWarps * 32) : "memory");
-      if (wr == 0 && ok) {
-        float MA = mA_run, MB = mB_run;
-        for (int w = 0; w < kSyncWarps - 1; ++w) {
-          const float* other = slot + (w * 32 + lane) * kMergeFloats;
-          MA = fmaxf(MA, other[64]);
-          MB = fmaxf(MB, other[65]);
-        }
-        const float sA = (mA_run == -INFINITY) ? 0.0f : fast_exp2(mA_run - MA);
-        const float sB = (mB_run == -INFINITY) ? 0.0f : fast_exp2(mB_run - MB);
-        float LA = lA * sA, LB = lB * sB;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-          o[nt][0] *= sA;
-          o[nt][1] *= sA;
-          o[nt][2] *= sB;
-          o[nt][3] *= sB;
-        }
-        for (int w = 0; w < kSyncWarps - 1; ++w) {
-          const float* other = slot + (w * 32 + lane) * kMergeFloats;
-          const float fA = (other[64] == -INFINITY) ? 0.0f : fast_exp2(other[64] - MA);
-          const float fB = (other[65] == -INFINITY) ? 0.0f : fast_exp2(other[65] - MB);
-          LA += other[66] * fA;
-          LB += other[67] * fB;
-#pragma unroll
-          for (int nt = 0; nt < 16; ++nt) {
-            o[nt][0] += other[4 * nt + 0] * fA;
-            o[nt][1] += other[4 * nt + 1] * fA;
-            o[nt][2] += other[4 * nt + 2] * fB;
-            o[nt][3] += other[4 * nt + 3] * fB;
-          }
-        }
-        const float iA = LA > 0.0f ? 1.0f / LA : 0.0f, iB = LB > 0.0f ? 1.0f / LB : 0.0f;
-        uint16_t* oA = p.out + ((int64_t)(q0 + nodeA) * p.Hq + h * p.g + rA % p.g) * kD;
-        uint16_t* oB = p.out + ((int64_t)(q0 + nodeB) * p.Hq + h * p.g + rB % p.g) * kD;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-          const int c = 8 * nt + 2 * tq;
-          if (vA) *(uint32_t*)(oA + c) = pack_bf16x2(o[nt][0] * iA, o[nt][1] * iA);
-          if (vB) *(uint32_t*)(oB + c) = pack_bf16x2(o[nt][2] * iB, o[nt][3] * iB);
+        for (int mt = 0; mt < 8; ++mt) {
+          const uint32_t lo = pack_bf16x2(o[mt][i] * inv, o[mt][2 + i] * inv);
+          orow[16 * mt + gq] = (uint16_t)(lo & 0xffffu);
+          orow[16 * mt + gq + 8] = (uint16_t)(lo >> 16);
         }
       }
+    }
     }
   }
   tc_fence_before();
@@ -650,7 +690,7 @@ extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int3
   if (head_dim != kD) return set_error(PTS_ERR_UNSUPPORTED, "head_dim %d (this build: 128)", head_dim);
   if (page_len != kPage) return set_error(PTS_ERR_UNSUPPORTED, "page_len %d (this build: 16)", page_len);
   const int g = num_qo_heads / num_kv_heads;
-  if (g > 16 || kGroupRows % g != 0) return set_error(PTS_ERR_UNSUPPORTED, "GQA group %d (this build: 1..16, power of 2)", g);
+  if (g > 16) return set_error(PTS_ERR_UNSUPPORTED, "GQA group %d (this build: 1..16)", g);
   if (mask_bits) {
     if (max_qo_len > PTS_MAX_TREE_NODES)
       return set_error(PTS_ERR_CAPACITY, "tree of %d rows above %d", max_qo_len, PTS_MAX_TREE_NODES);

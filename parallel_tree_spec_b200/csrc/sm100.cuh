@@ -52,14 +52,45 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware park the thread for up to `hint_ns` while the
+// phase is incomplete (it resumes as soon as the phase completes), so waiting
+// warps do not take issue slots from the warps that share their scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Gives up after
-// `timeout_ns` and returns false so the caller can bail out instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = 2000000000ull) {
+// `timeout_cycles` SM clocks (4e9: about 2 s at the B200's top clock) and
+// returns false so the caller can bail out instead of hanging.  The bound is
+// kept with clock64, which is cheap to read in the polling loop.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          long long timeout_cycles = 4000000000ll) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (clock64() - t0 > timeout_cycles) return false;
+  }
+}
+
+// Wait for a phase without occupying the scheduler: poll, then sleep
+// `sleep_ns` between polls.  For waiters that run ahead of their consumers
+// (a producer several stages in front), where reacting late costs nothing.
+__device__ __forceinline__ bool mbar_wait_lazy(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                               long long timeout_cycles = 4000000000ll) {
+  const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > timeout_ns) return false;
+    if (clock64() - t0 > timeout_cycles) return false;
+    __nanosleep(sleep_ns);
   }
 }
 
@@ -250,6 +281,25 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Transpose of an 8x8 b16 matrix held in mma fragment layout (lane 4r+c holds
+// elements (r, 2c) and (r, 2c+1); afterwards it holds (2c, r) and (2c+1, r)).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
 }  // namespace sm100
