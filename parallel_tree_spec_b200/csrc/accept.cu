@@ -84,6 +84,8 @@ struct AcceptParams {
   struct Part* part_ws;
   unsigned* row_ctr;
   unsigned* req_ctr;
+  unsigned* walk_ctr;      // [0] requests published, [1] requests claimed by walkers
+  int* walk_q;             // published requests (b + 1; 0 = not yet)
 };
 
 __device__ __forceinline__ float load_scaled(const AcceptParams& p, const uint16_t* row, int i) {
@@ -177,15 +179,22 @@ __device__ __forceinline__ int block_reduce_min(int v, int* sm) {
 }
 
 // Walk state in dynamic shared memory, sized for the call's largest tree
-// (capacity `cap` nodes), so streaming CTAs of small trees stay light.
+// (capacity `cap` nodes), so streaming CTAs of small trees stay light.  The
+// fields a traversal descent reads for a node sit in one 16-byte record.
+struct __align__(16) NodeRec {
+  int16_t first_valid;     // first child still valid (-1: none)
+  int16_t sticky_t;        // time p_alpha was last set directly (-1: never)
+  int16_t reset_t;         // time the node's subtree was last recomputed
+  int16_t parent;
+  float stored_pa;         // p_alpha set directly at time sticky_t
+  float ratio;             // Mb/Ms (0 when Ms <= eps), kept current
+};
+
 struct WalkSmem {
+  NodeRec* rec;
   int32_t* token;
-  int16_t* sticky_t;       // time p_alpha was last set directly (-1: never)
-  int16_t* reset_t;        // time the node's subtree was last recomputed
   int16_t* first_child;
   int16_t* next_sib;
-  int16_t* first_valid;
-  int16_t* parent;
   int16_t* path;
   int16_t* path_rmax;
   int16_t* sib;            // children of every node, contiguous per parent
@@ -194,14 +203,13 @@ struct WalkSmem {
   float* path_pa;
   float* mb;
   float* ms;
-  float* stored_pa;
   float* uni;              // 2 * cap + 2 uniforms
   uint8_t* valid;
 };
 
 __host__ __device__ inline size_t walk_smem_bytes(int cap) {
   cap = (cap + 15) & ~15;
-  return (size_t)cap * (4 + 11 * 2 + 4 * 4 + 1) + (size_t)(2 * cap + 2) * 4 + 64;
+  return (size_t)cap * (16 + 4 + 7 * 2 + 3 * 4 + 1) + (size_t)(2 * cap + 2) * 4 + 80;
 }
 
 __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
@@ -213,18 +221,14 @@ __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
     q += (bytes + 15) & ~(size_t)15;
     return r;
   };
+  w.rec = (NodeRec*)take(cap * 16);
   w.token = (int32_t*)take(cap * 4);
   w.path_pa = (float*)take(cap * 4);
   w.mb = (float*)take(cap * 4);
   w.ms = (float*)take(cap * 4);
-  w.stored_pa = (float*)take(cap * 4);
   w.uni = (float*)take((2 * cap + 2) * 4);
-  w.sticky_t = (int16_t*)take(cap * 2);
-  w.reset_t = (int16_t*)take(cap * 2);
   w.first_child = (int16_t*)take(cap * 2);
   w.next_sib = (int16_t*)take(cap * 2);
-  w.first_valid = (int16_t*)take(cap * 2);
-  w.parent = (int16_t*)take(cap * 2);
   w.path = (int16_t*)take(cap * 2);
   w.path_rmax = (int16_t*)take(cap * 2);
   w.sib = (int16_t*)take(cap * 2);
@@ -289,58 +293,72 @@ __device__ __forceinline__ float ratio_of(float mb, float ms) {
   return ms > kEps32 ? __fdiv_rn(mb, ms) : 0.0f;
 }
 
-// Traversal verification (verify_tree_traversal, verification.py:377-524),
-// one thread; see the file comment for the lazily evaluated p_alpha.
+// Traversal verification (verify_tree_traversal, verification.py:377-524) by
+// one thread (its loop is a chain of dependent shared-memory accesses, which
+// lane-parallel versions only lengthen).  See the file comment for the lazily
+// evaluated p_alpha.
 __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w) {
   int accepted = 0;
   int depth = 0;           // w.path[0..depth]: the current descent path
   int draw = 0;
   int T = 1;               // time stamp of the next direct p_alpha assignment
   w.path[0] = 0;
-  w.path_pa[0] = w.stored_pa[0];
+  w.path_pa[0] = w.rec[0].stored_pa;
   w.path_rmax[0] = -1;
   const int max_iter = 2 * n + 2;
   for (int it = 0; it < max_iter; ++it) {                             // :377
+    const float eta = w.uni[draw++];                                  // :396, loaded ahead of the descent
     // descend to the first valid leaf (:379-389), p_alpha evaluated lazily
     int u = w.path[depth];
     float pa_u = w.path_pa[depth];
     int rmax_u = w.path_rmax[depth];
-    for (int c = w.first_valid[u]; c >= 0; c = w.first_valid[u]) {
-      const int rmax = max(rmax_u, (int)w.reset_t[u]);
-      const float pa = w.sticky_t[c] > rmax ? w.stored_pa[c]
-                                             : fminf(__fmul_rn(pa_u, ratio_of(w.mb[c], w.ms[c])), 1.0f);
+    NodeRec ru = w.rec[u];
+    while (ru.first_valid >= 0) {
+      const int c = ru.first_valid;
+      const NodeRec rc = w.rec[c];
+      const int rmax = max(rmax_u, (int)ru.reset_t);
+      const float pa = rc.sticky_t > rmax ? rc.stored_pa : fminf(__fmul_rn(pa_u, rc.ratio), 1.0f);
       ++depth;
       w.path[depth] = (int16_t)c;
       w.path_pa[depth] = pa;
       w.path_rmax[depth] = (int16_t)rmax;
       u = c;
+      ru = rc;
       pa_u = pa;
       rmax_u = rmax;
     }
     const int cand = u;
-    const float eta = w.uni[draw++];                                  // :396
     if (eta < pa_u) {                                                 // :395-400
       accepted = cand;
       break;
     }
     w.valid[cand] = 0;                                                // :403
     const double old_ms_rej = (double)w.ms[cand];
+    const double old_mb_rej = (double)w.mb[cand];
     w.ms[cand] = 0.0f;
-    const int parent = w.parent[cand];
+    const int parent = ru.parent;
     if (parent < 0) {                                                 // :408
       accepted = 0;
       break;
     }
-    if (w.first_valid[parent] == cand) {
-      int c = w.next_sib[cand];
-      while (c >= 0 && !w.valid[c]) c = w.next_sib[c];
-      w.first_valid[parent] = (int16_t)c;
-    }
     --depth;                                                          // back to the parent
-    if (w.first_valid[parent] < 0) continue;                          // :417 no active sibling
+    const int c0 = w.child_start[parent], nc = w.child_cnt[parent];
+    if (w.rec[parent].first_valid == cand) {
+      int next = -1;
+      bool after = false;
+      for (int i = 0; i < nc; ++i) {
+        const int c = w.sib[c0 + i];
+        if (after && w.valid[c]) {
+          next = c;
+          break;
+        }
+        if (c == cand) after = true;
+      }
+      w.rec[parent].first_valid = (int16_t)next;
+      if (next < 0) continue;                                         // :417 no active sibling
+    }
     const float p_old32 = w.path_pa[depth];                           // :422
     const double p_old = (double)p_old32;
-    const int c0 = w.child_start[parent], nc = w.child_cnt[parent];
     float s_tree = 0.0f, sum_mb = 0.0f;                               // :429-433, left to right
     for (int i = 0; i < nc; ++i) {
       const int c = w.sib[c0 + i];
@@ -352,29 +370,31 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
     if (ms_denom < kEps) ms_denom = kEps;
     double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
     if (S < kEps) S = kEps;                                           // :435
-    const double p_new = __ddiv_rn(S, __dsub_rn(__dadd_rn(S, 1.0), p_old));   // :439
-    const double old_mb_rej = (double)w.mb[cand];                     // :451
-    const double mb_rej = __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S);
+    const double p_new = __ddiv_rn(S, __dsub_rn(__dadd_rn(S, 1.0), p_old));                   // :439
+    const double mb_rej = __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S);   // :451
     const float ms_denom32 = __double2float_rn(ms_denom);
     const float S32 = __double2float_rn(S);
     for (int i = 0; i < nc; ++i) {                                    // :443-448
       const int c = w.sib[c0 + i];
       if (!w.valid[c]) continue;
       const float msv = w.ms[c], mbv = w.mb[c];
-      w.ms[c] = __fdiv_rn(msv, ms_denom32);
-      w.mb[c] = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
+      const float ms_new = __fdiv_rn(msv, ms_denom32);
+      const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
+      w.ms[c] = ms_new;
+      w.mb[c] = mb_new;
+      w.rec[c].ratio = ratio_of(mb_new, ms_new);
     }
     w.mb[cand] = __double2float_rn(mb_rej);                           // :452
     const float p_new32 = __double2float_rn(p_new);                   // :440, direct assignment
-    w.stored_pa[parent] = p_new32;
-    w.sticky_t[parent] = (int16_t)T;
-    w.reset_t[parent] = (int16_t)T;
+    w.rec[parent].stored_pa = p_new32;
+    w.rec[parent].sticky_t = (int16_t)T;
+    w.rec[parent].reset_t = (int16_t)T;
     w.path_pa[depth] = p_new32;
     ++T;
   }
   // :480-524 output
   int d = 0;
-  for (int c = accepted; c >= 0; c = w.parent[c]) w.path[d++] = (int16_t)c;   // reversed path
+  for (int c = accepted; c >= 0; c = w.rec[c].parent) w.path[d++] = (int16_t)c;   // reversed path
   int32_t* ot = p.out_tokens + (int64_t)b * p.out_stride;
   int32_t* oh = p.out_hidden + (int64_t)b * p.out_stride;
   int n_out = 0;
@@ -399,6 +419,99 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
     n_out++;
   }
   write_counts(p, b, n_out > p.out_stride ? -2 : n_out, n_out, n_out > 0 ? n_out - 1 : 0, accepted);
+}
+
+// Thread groups that run a tree walk: the whole CTA (streaming kernel for
+// unaligned rows) or one warp (walker warp of the persistent kernel).
+struct CtaGroup {
+  __device__ int rank() const { return threadIdx.x; }
+  __device__ int size() const { return kThreads; }
+  __device__ void sync() const { __syncthreads(); }
+  __device__ bool any(bool v, int* sm) const { return block_reduce_min(v ? 0 : 1, sm) == 0; }
+};
+struct WarpGroup {
+  __device__ int rank() const { return threadIdx.x & 31; }
+  __device__ int size() const { return 32; }
+  __device__ void sync() const { __syncwarp(); }
+  __device__ bool any(bool v, int*) const {
+    __syncwarp();
+    return __any_sync(0xffffffffu, v);
+  }
+};
+
+// Load request b's tree (rows lo .. lo+n-1), the target probability of every
+// node's token under its parent's row and the traversal uniforms, build the
+// child lists, then walk (greedy or traversal) on the group's first thread.
+template <class G>
+__device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
+  if (n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
+    if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
+    return;
+  }
+  int bad = 0;
+  for (int i = g.rank(); i < n; i += g.size()) {
+    const int par = p.parents[lo + i];
+    const int tok = p.tokens[lo + i];
+    if ((i == 0 && par != -1) || (i > 0 && (par < 0 || par >= i))) bad = 1;
+    NodeRec r;
+    r.first_valid = -1;
+    r.sticky_t = i == 0 ? 0 : -1;
+    r.reset_t = -1;
+    r.parent = (int16_t)par;
+    r.stored_pa = 1.0f;
+    r.ratio = 0.0f;
+    w.token[i] = tok;
+    w.valid[i] = 1;
+    if (p.traversal) {
+      if (i == 0) {
+        w.mb[0] = 1.0f;
+        w.ms[0] = 1.0f;
+      } else if (par >= 0 && par < i) {
+        const RowStat* rs = p.row_ws + lo + par;
+        const float pm = __ldcg(&rs->m), ps = __ldcg(&rs->s);
+        const float x = (tok >= 0 && tok < p.vocab)
+                            ? load_scaled(p, p.logits + (int64_t)(lo + par) * p.row_stride, tok)
+                            : -INFINITY;
+        w.mb[i] = prob_bf16(x, pm, ps);                                // :349
+        w.ms[i] = p.draft_probs[lo + i];                               // :353
+      }
+      if (i == 0 || (par >= 0 && par < i)) r.ratio = ratio_of(w.mb[i], w.ms[i]);
+    }
+    w.rec[i] = r;
+  }
+  if (p.traversal)
+    for (int k = g.rank(); k < 2 * n + 2; k += g.size())
+      w.uni[k] = philox_uniform(p.seed, p.offset, (uint32_t)b, (uint32_t)k);
+  bad = g.any(bad != 0, red_sm);
+  g.sync();
+  if (bad) {
+    if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
+    return;
+  }
+  if (g.rank() == 0) {
+    // children in ascending order: linked lists and a contiguous (CSR) copy
+    for (int i = 0; i < n; ++i) {
+      w.first_child[i] = -1;
+      w.child_cnt[i] = 0;
+    }
+    for (int i = n - 1; i >= 1; --i) {
+      const int par = w.rec[i].parent;
+      w.next_sib[i] = w.first_child[par];
+      w.first_child[par] = (int16_t)i;
+      w.child_cnt[par]++;
+    }
+    w.next_sib[0] = -1;
+    int o = 0;
+    for (int i = 0; i < n; ++i) {
+      w.child_start[i] = (int16_t)o;
+      for (int c = w.first_child[i]; c >= 0; c = w.next_sib[c]) w.sib[o++] = (int16_t)c;
+      w.rec[i].first_valid = w.first_child[i];
+    }
+    if (!p.traversal) walk_greedy(p, b, lo, w);
+  }
+  g.sync();
+  if (p.traversal && g.rank() == 0) walk_traversal(p, b, lo, n, w);
+  g.sync();
 }
 
 // Request of `row`: the warp finds the last request whose first row is <= row
@@ -459,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
 #pragma unroll
   for (int i = 1; i < kVecPerThread * 4; ++i) m2 = bf16x2_max(m2, raw[i]);
   const float mt = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u));
-  const float mlog = mt * kLog2e;
+  const float mlog = mt == -INFINITY ? 0.0f : mt * kLog2e;   // all -inf: every term is 0
   float st = 0.0f;
   int first = INT_MAX;
 #pragma unroll
@@ -546,72 +659,426 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
   if (!s_flag) return;
 
   // ---- 3. tree walk (last row CTA of the request) ----------------------------
-  const int b = s_b, lo = s_lo, n = s_n;
-  const WalkSmem w = walk_smem(dyn_smem, p.max_nodes);
-  if (n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
-    if (tid == 0) write_counts(p, b, -1, 0, 0, 0);
-    return;
+  walk_request(p, s_b, s_lo, s_n, walk_smem(dyn_smem, p.max_nodes), CtaGroup{}, s_red_i);
+}
+
+// ---------------------------------------------------------------------------
+// Persistent streaming kernel (rows 16-byte aligned, vocabulary a multiple of 8).
+//
+// One CTA per SM.  The rows are dealt out whole, round-robin (CTA c takes rows
+// c, c + G, ...), so a row's chunks are reduced inside one CTA; only the last
+// num_rows % G rows are split by chunk over all CTAs and merged through the
+// workspace (partials + acquire/release counter), which keeps every CTA's item
+// count within one of the others.  Each CTA streams its items -- 32 KB chunks
+// of a row -- through a ring of shared-memory slots:
+//   warp 0        producer: one cp.async.bulk (1-D, no multicast) per item,
+//                 kSSlots items ahead of the consumers;
+//   warps 1-8     consumers: 64 values per thread (eight 16-byte shared loads,
+//                 the slot released right after), thread max by packed bf16x2
+//                 max, sum of exp(x - max) with packed f32x2 FMA/add and MUFU
+//                 exp2, folded into a running (max, sum) per thread; the warp's
+//                 max and its first index are updated only when a chunk raises
+//                 it (searched by the threads that hold it), and the warp's
+//                 partial of the row is reduced and handed over once per row;
+//   warp 9        merger: combines the 8 warp partials of a row (or of a chunk
+//                 of a split row), derives the row statistics with the tie
+//                 rescan, and counts the request's finished rows;
+//   warp 10       walker: claims the next slot of the workspace's publication
+//                 list and runs the tree walk of the request the mergers publish
+//                 there (the walks of different requests run on different SMs,
+//                 each as soon as the request's last row is done, while the
+//                 other warps stream the following rows).
+constexpr int kSChunk = 16384;                 // elements per item (32 KB)
+constexpr int kSSlots = 5;
+constexpr int kSConsumerWarps = 8;
+constexpr int kSConsumers = kSConsumerWarps * 32;
+constexpr int kSThreads = kSConsumers + 96;    // + producer, merger and walker warps
+constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (8)
+constexpr long long kSpinLimit = 4000000000ll;     // clock cycles, about 2 s
+
+struct __align__(16) StreamCtl {
+  uint64_t full[kSSlots];
+  uint64_t empty[kSSlots];
+  uint64_t seg_full[2];       // 16 consumer warps wrote their partials of a segment
+  uint64_t seg_empty[2];      // the merger has read them
+  Part seg[2][kSConsumerWarps];
+};
+
+constexpr size_t kSRingBytes = (size_t)kSSlots * kSChunk * 2;
+constexpr size_t kSCtlOff = kSRingBytes;
+constexpr size_t kSWalkOff = (kSCtlOff + sizeof(StreamCtl) + 127) & ~(size_t)127;
+
+// The work of CTA c: first its whole rows, then its chunks of the split rows.
+struct StreamPlan {
+  int G, nchunks, whole_rows_per_cta, split_first_row, split_items;
+  __device__ int items(int c) const {
+    const int extra = split_items > c ? (split_items - c + G - 1) / G : 0;
+    return whole_rows_per_cta * nchunks + extra;
   }
-  int bad = 0;
-  for (int i = tid; i < n; i += kThreads) {
-    const int par = p.parents[lo + i];
-    const int tok = p.tokens[lo + i];
-    if ((i == 0 && par != -1) || (i > 0 && (par < 0 || par >= i))) bad = 1;
-    w.parent[i] = (int16_t)par;
-    w.token[i] = tok;
-    w.valid[i] = 1;
-    w.sticky_t[i] = i == 0 ? 0 : -1;
-    w.reset_t[i] = -1;
-    w.stored_pa[i] = 1.0f;
-    if (p.traversal) {
-      if (i == 0) {
-        w.mb[0] = 1.0f;
-        w.ms[0] = 1.0f;
-      } else if (par >= 0 && par < i) {
-        const RowStat* rs = p.row_ws + lo + par;
-        const float pm = __ldcg(&rs->m), ps = __ldcg(&rs->s);
-        const float x = (tok >= 0 && tok < p.vocab)
-                            ? load_scaled(p, p.logits + (int64_t)(lo + par) * p.row_stride, tok)
-                            : -INFINITY;
-        w.mb[i] = prob_bf16(x, pm, ps);                                // :349
-        w.ms[i] = p.draft_probs[lo + i];                               // :353
+  // row, chunk and whether item k ends a segment (a whole row, or one split chunk)
+  __device__ void item(int c, int k, int& row, int& chunk, bool& seg_end, bool& whole) const {
+    const int n1 = whole_rows_per_cta * nchunks;
+    if (k < n1) {
+      row = c + (k / nchunks) * G;
+      chunk = k % nchunks;
+      seg_end = chunk == nchunks - 1;
+      whole = true;
+    } else {
+      const int j = c + (k - n1) * G;
+      row = split_first_row + j / nchunks;
+      chunk = j % nchunks;
+      seg_end = true;
+      whole = nchunks == 1;
+    }
+  }
+};
+
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   su32(dst)),
+               "l"(src), "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void s_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void s_mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void s_mbar_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(su32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Bounded wait (kSpinLimit clocks); false on timeout.  sleep_ns > 0 for
+// waiters that can react late.
+__device__ __forceinline__ bool s_mbar_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns) {
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kSpinLimit) return false;
+    if (sleep_ns) __nanosleep(sleep_ns);
+  }
+}
+// Row statistics from the row's merged partial `r` (valid in lane 0), by one
+// warp (the warp rescans the row when a value below the max can round to the
+// same probability); returns true, with the request, when the row completes it.
+__device__ bool finish_row_warp(const AcceptParams& p, int row, Part r, int* out_b) {
+  const int lane = threadIdx.x & 31;
+  float m = 0.0f, sf = 0.0f, qmax = 0.0f;
+  int arg = 0, tie = 0;
+  if (lane == 0) {
+    m = r.m;
+    sf = (float)r.s;
+    qmax = round_to_bf16(__fdiv_rn(1.0f, sf));
+    arg = r.idx;
+    tie = (r.m > -INFINITY) && (prob_bf16(prev_bf16(r.m), r.m, sf) == qmax);
+  }
+  m = __shfl_sync(0xffffffffu, m, 0);
+  sf = __shfl_sync(0xffffffffu, sf, 0);
+  qmax = __shfl_sync(0xffffffffu, qmax, 0);
+  arg = __shfl_sync(0xffffffffu, arg, 0);
+  tie = __shfl_sync(0xffffffffu, tie, 0);
+  if (tie) {
+    const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
+    int best = INT_MAX;
+    for (int e = lane; e < p.vocab; e += 32)
+      if (prob_bf16(load_scaled(p, rp, e), m, sf) == qmax) {
+        best = e;
+        break;
       }
-    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+    arg = best;
   }
-  if (p.traversal)
-    for (int k = tid; k < 2 * n + 2; k += kThreads) w.uni[k] = philox_uniform(p.seed, p.offset, (uint32_t)b, (uint32_t)k);
-  bad = block_reduce_min(bad ? 0 : 1, s_red_i) == 0;
-  if (bad) {
-    if (tid == 0) write_counts(p, b, -1, 0, 0, 0);
-    return;
+  const int b = find_request(p.row_indptr, p.batch, row);
+  int flag = 0;
+  if (lane == 0) {
+    RowStat rs;
+    rs.m = m;
+    rs.s = sf;
+    rs.argmax = arg;
+    rs.flags = tie;
+    p.row_ws[row] = rs;
+    const int n = p.row_indptr[b + 1] - p.row_indptr[b];
+    unsigned prev;    // release: this row's stats; acquire: every earlier row's
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.req_ctr[b]) : "memory");
+    flag = (prev == (unsigned)(n - 1));
   }
+  *out_b = b;
+  return __shfl_sync(0xffffffffu, flag, 0) != 0;
+}
+
+__device__ __forceinline__ Part shfl_part(const Part& x, int src_lane_xor) {
+  Part o;
+  o.s = __shfl_xor_sync(0xffffffffu, x.s, src_lane_xor);
+  o.m = __shfl_xor_sync(0xffffffffu, x.m, src_lane_xor);
+  o.idx = __shfl_xor_sync(0xffffffffu, x.idx, src_lane_xor);
+  return o;
+}
+
+__global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const AcceptParams p, const StreamPlan plan) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint8_t* ring = sm;
+  StreamCtl& ctl = *reinterpret_cast<StreamCtl*>(sm + kSCtlOff);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x;
+  const int n_items = plan.items(c);
+  const Part kNone{0.0, -INFINITY, INT_MAX};
+
   if (tid == 0) {
-    // children in ascending order: linked lists and a contiguous (CSR) copy
-    for (int i = 0; i < n; ++i) {
-      w.first_child[i] = -1;
-      w.child_cnt[i] = 0;
+    for (int i = 0; i < kSSlots; ++i) {
+      s_mbar_init(&ctl.full[i], 1);
+      s_mbar_init(&ctl.empty[i], kSConsumerWarps);
     }
-    for (int i = n - 1; i >= 1; --i) {
-      const int par = w.parent[i];
-      w.next_sib[i] = w.first_child[par];
-      w.first_child[par] = (int16_t)i;
-      w.child_cnt[par]++;
+    for (int i = 0; i < 2; ++i) {
+      s_mbar_init(&ctl.seg_full[i], kSConsumerWarps);
+      s_mbar_init(&ctl.seg_empty[i], 1);
     }
-    w.next_sib[0] = -1;
-    int o = 0;
-    for (int i = 0; i < n; ++i) {
-      w.child_start[i] = (int16_t)o;
-      for (int c = w.first_child[i]; c >= 0; c = w.next_sib[c]) w.sib[o++] = (int16_t)c;
-      w.first_valid[i] = w.first_child[i];
-    }
-    if (!p.traversal) walk_greedy(p, b, lo, w);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (p.traversal && tid == 0) walk_traversal(p, b, lo, n, w);
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    int issued = 0;
+    for (int k = 0; k < n_items; ++k) {
+      const int slot = k % kSSlots;
+      const bool ok = s_mbar_wait(&ctl.empty[slot], ((k / kSSlots) + 1) & 1, 32);
+      if (!__all_sync(0xffffffffu, ok)) break;                       // consumers gave up
+      if (lane == 0) {
+        int row, chunk;
+        bool seg_end, whole;
+        plan.item(c, k, row, chunk, seg_end, whole);
+        const int n_el = min(kSChunk, p.vocab - chunk * kSChunk);
+        s_mbar_expect(&ctl.full[slot], (uint32_t)n_el * 2);
+        bulk_g2s(ring + (size_t)slot * kSChunk * 2, p.logits + (int64_t)row * p.row_stride + (int64_t)chunk * kSChunk,
+                 (uint32_t)n_el * 2, &ctl.full[slot]);
+      }
+      __syncwarp();
+      issued = k + 1;
+    }
+    // copies in flight must land before the CTA exits
+    for (int k = max(0, issued - kSSlots); k < issued; ++k) s_mbar_wait(&ctl.full[k % kSSlots], (k / kSSlots) & 1, 32);
+  } else if (warp <= kSConsumerWarps) {
+    // ---------------------------------------------------------------- consumers
+    const int ct = tid - 32, cw = warp - 1;
+    // running partial of the current segment: per thread (max, sum relative to
+    // it), per warp (max, first index of it; the same in every lane)
+    float m_t = -INFINITY;
+    double s_t = 0.0;
+    float w_m = -INFINITY;
+    int w_idx = INT_MAX;
+    int seg = 0;
+    for (int k = 0; k < n_items; ++k) {
+      const int slot = k % kSSlots;
+      int row, chunk;
+      bool seg_end, whole;
+      plan.item(c, k, row, chunk, seg_end, whole);
+      const int base = chunk * kSChunk;
+      const int n_el = min(kSChunk, p.vocab - base);
+      if (!s_mbar_wait(&ctl.full[slot], (k / kSSlots) & 1, 0)) break;
+      const uint8_t* src = ring + (size_t)slot * kSChunk * 2;
+      uint32_t v[kSVec * 4];
+#pragma unroll
+      for (int q = 0; q < kSVec; ++q) {
+        const int vi = q * kSConsumers + ct;
+        uint4 x = make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);   // -inf padding
+        if (vi * 8 < n_el) x = *reinterpret_cast<const uint4*>(src + (size_t)vi * 16);
+        v[4 * q + 0] = x.x;
+        v[4 * q + 1] = x.y;
+        v[4 * q + 2] = x.z;
+        v[4 * q + 3] = x.w;
+      }
+      __syncwarp();
+      if (lane == 0) s_mbar_arrive(&ctl.empty[slot]);
+      if (p.use_temp) {
+#pragma unroll
+        for (int i = 0; i < kSVec * 4; ++i) v[i] = scale_pair(v[i], p.inv_temp);
+      }
+      uint32_t m2 = v[0];
+#pragma unroll
+      for (int i = 1; i < kSVec * 4; ++i) m2 = bf16x2_max(m2, v[i]);
+      const float mt = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u));
+      if (mt > -INFINITY) {
+        const float mlog = mt * kLog2e;
+        const uint64_t sc2 = f2(kLog2e, kLog2e), nm2 = f2(-mlog, -mlog);
+        uint64_t acc_a = f2(0.0f, 0.0f), acc_b = f2(0.0f, 0.0f);
+#pragma unroll
+        for (int i = 0; i < kSVec * 4; ++i) {
+          float a, b;
+          f2_split(ffma2(f2(__uint_as_float(v[i] << 16), __uint_as_float(v[i] & 0xffff0000u)), sc2, nm2), a, b);
+          const uint64_t e = f2(ex2_approx(a), ex2_approx(b));
+          if (i & 1) acc_b = fadd2(acc_b, e);
+          else acc_a = fadd2(acc_a, e);
+        }
+        float s0, s1, s2, s3;
+        f2_split(acc_a, s0, s1);
+        f2_split(acc_b, s2, s3);
+        const double st = (double)((s0 + s1) + (s2 + s3));
+        // fold into this thread's running partial of the segment
+        if (mt > m_t) {
+          s_t = s_t * (double)ex2_approx((m_t - mt) * kLog2e) + st;
+          m_t = mt;
+        } else {
+          s_t += st * (double)ex2_approx((mt - m_t) * kLog2e);
+        }
+      }
+      // the first index of the warp's max changes only when some lane raises it
+      // (an equal max keeps the earlier, smaller index)
+      if (__any_sync(0xffffffffu, mt > w_m)) {
+        float wm = mt;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+        // branchless scan from the last value to the first: the smallest index
+        // holding wm wins (padding is -inf and never equals the finite wm)
+        int fi = INT_MAX;
+#pragma unroll
+        for (int q = kSVec - 1; q >= 0; --q) {
+#pragma unroll
+          for (int j = 3; j >= 0; --j) {
+            const int e = base + (q * kSConsumers + ct) * 8 + 2 * j;
+            const uint32_t u = v[4 * q + j];
+            fi = (__uint_as_float(u & 0xffff0000u) == wm) ? e + 1 : fi;
+            fi = (__uint_as_float(u << 16) == wm) ? e : fi;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) fi = min(fi, __shfl_xor_sync(0xffffffffu, fi, o));
+        w_m = wm;
+        w_idx = fi;
+      }
+      if (seg_end) {
+        // the warp's partial of the segment: sums relative to the warp max
+        double ws = (m_t == -INFINITY) ? 0.0 : s_t * (double)ex2_approx((m_t - w_m) * kLog2e);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+        const int buf = seg & 1;
+        if (!s_mbar_wait(&ctl.seg_empty[buf], ((seg >> 1) + 1) & 1, 0)) break;
+        if (lane == 0) {
+          ctl.seg[buf][cw] = (w_idx == INT_MAX) ? kNone : Part{ws, w_m, w_idx};
+          s_mbar_arrive(&ctl.seg_full[buf]);
+        }
+        __syncwarp();
+        m_t = -INFINITY;
+        s_t = 0.0;
+        w_m = -INFINITY;
+        w_idx = INT_MAX;
+        ++seg;
+      }
+    }
+  } else if (warp == kSConsumerWarps + 1) {
+    // ---------------------------------------------------------------- merger
+    int seg = 0;
+    for (int k = 0; k < n_items; ++k) {
+      int row, chunk;
+      bool seg_end, whole;
+      plan.item(c, k, row, chunk, seg_end, whole);
+      if (!seg_end) continue;
+      const int buf = seg & 1;
+      if (!s_mbar_wait(&ctl.seg_full[buf], (seg >> 1) & 1, 0)) break;
+      // the 16 warp partials, merged pairwise in warp order
+      Part x = lane < kSConsumerWarps ? ctl.seg[buf][lane] : kNone;
+      __syncwarp();
+      if (lane == 0) s_mbar_arrive(&ctl.seg_empty[buf]);
+#pragma unroll
+      for (int o = 1; o < kSConsumerWarps; o <<= 1) {
+        const Part y = shfl_part(x, o);
+        x = (lane & o) ? merge(y, x) : merge(x, y);
+      }
+      ++seg;
+      bool row_done = whole;
+      if (!whole) {
+        // one chunk of a split row: publish it; the last chunk to arrive merges the row
+        unsigned prev = 0;
+        if (lane == 0) {
+          p.part_ws[(int64_t)row * plan.nchunks + chunk] = x;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.row_ctr[row]) : "memory");
+        }
+        row_done = __shfl_sync(0xffffffffu, prev, 0) == (unsigned)(plan.nchunks - 1);
+        if (row_done && lane == 0) {
+          const Part* pp = p.part_ws + (int64_t)row * plan.nchunks;
+          x = Part{__ldcg(&pp[0].s), __ldcg(&pp[0].m), __ldcg(&pp[0].idx)};
+          for (int i = 1; i < plan.nchunks; ++i)
+            x = merge(x, Part{__ldcg(&pp[i].s), __ldcg(&pp[i].m), __ldcg(&pp[i].idx)});
+        }
+      }
+      if (!row_done) continue;
+      int b;
+      if (finish_row_warp(p, row, x, &b) && lane == 0) {
+        // publish the request for whichever walker claimed the next slot
+        const unsigned slot = atomicAdd(&p.walk_ctr[0], 1u);
+        asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p.walk_q + slot), "r"(b + 1) : "memory");
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------------------------------------------------------- walker
+    // Claims the next publication slot and walks the request that lands in it,
+    // so the walks of different requests run on different SMs.
+    const WalkSmem w = walk_smem(sm + kSWalkOff, p.max_nodes);
+    for (;;) {
+      unsigned t = 0;
+      if (lane == 0) t = atomicAdd(&p.walk_ctr[1], 1u);
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if (t >= (unsigned)p.batch) break;
+      int v = 0;
+      if (lane == 0) {
+        const long long t0 = clock64();
+        for (;;) {
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p.walk_q + t) : "memory");
+          if (v != 0 || clock64() - t0 > 10 * kSpinLimit) break;   // bounded (about 20 s)
+          __nanosleep(256);
+        }
+      }
+      v = __shfl_sync(0xffffffffu, v, 0);
+      if (v == 0) break;
+      const int b = v - 1;
+      const int lo = p.row_indptr[b];
+      walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr);
+    }
+  }
+}
+
+int stream_sm_count() {
+  static int count[256] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return 0;
+  if (!count[dev]) {
+    int c = 0;
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    count[dev] = c;
+  }
+  return count[dev];
 }
 
 size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, size_t* off_rctr,
-                 size_t* off_qctr) {
+                 size_t* off_qctr, size_t* off_walk = nullptr) {
   const int nchunks = (vocab + kChunk - 1) / kChunk;
   size_t o = 0;
   *off_parts = o;
@@ -622,6 +1089,8 @@ size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, s
   o = align_up(o + (size_t)num_rows * sizeof(unsigned), 256);
   *off_qctr = o;
   o = align_up(o + (size_t)num_rows * sizeof(unsigned), 256);
+  if (off_walk) *off_walk = o;
+  o = align_up(o + 2 * sizeof(unsigned) + (size_t)num_rows * sizeof(int), 256);
   return o;
 }
 
@@ -640,8 +1109,8 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   PTS_CHECK_ARG(p.out_stride >= 1, "out_stride must be positive");
   PTS_CHECK_ARG(temperature > 0.0f, "temperature must be positive");
   if (p.num_rows > 65535) return set_error(PTS_ERR_CAPACITY, "num_rows %d above 65535", p.num_rows);
-  size_t opt, orw, orc, oqc;
-  const size_t need = ws_layout(p.num_rows, p.vocab, &opt, &orw, &orc, &oqc);
+  size_t opt, orw, orc, oqc, owk;
+  const size_t need = ws_layout(p.num_rows, p.vocab, &opt, &orw, &orc, &oqc, &owk);
   if (!workspace || ws_bytes < need)
     return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", ws_bytes, need);
   PTS_CHECK_ARG(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
@@ -651,11 +1120,30 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   p.row_ws = (RowStat*)(ws + orw);
   p.row_ctr = (unsigned*)(ws + orc);
   p.req_ctr = (unsigned*)(ws + oqc);
+  p.walk_ctr = (unsigned*)(ws + owk);
+  p.walk_q = (int*)(ws + owk + 2 * sizeof(unsigned));
   p.traversal = traversal;
   p.use_temp = (temperature != 1.0f);
   p.inv_temp = 1.0f / temperature;
   p.vec_ok = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
   PTS_CUDA_TRY(cudaMemsetAsync(ws + orc, 0, need - orc, stream));
+  const int sms = stream_sm_count();
+  if (p.vec_ok && p.vocab % 8 == 0 && sms > 0) {
+    StreamPlan plan;
+    plan.G = min(sms, p.num_rows * nchunks);
+    plan.nchunks = nchunks;
+    plan.whole_rows_per_cta = p.num_rows / plan.G;
+    plan.split_first_row = plan.whole_rows_per_cta * plan.G;
+    plan.split_items = (p.num_rows - plan.split_first_row) * nchunks;
+    const size_t ssmem = kSWalkOff + walk_smem_bytes(p.max_nodes);
+    static size_t ssmem_attr = 0;
+    if (ssmem > ssmem_attr) {
+      PTS_CUDA_TRY(cudaFuncSetAttribute(accept_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
+      ssmem_attr = ssmem;
+    }
+    accept_stream_kernel<<<plan.G, kSThreads, ssmem, stream>>>(p, plan);
+    return launch_status("accept_stream_kernel");
+  }
   const size_t smem = walk_smem_bytes(p.max_nodes);
   static size_t smem_attr = 0;
   if (smem > smem_attr) {
