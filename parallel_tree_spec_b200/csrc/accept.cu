@@ -54,6 +54,7 @@ constexpr int kChunk = kThreads * kVecPerThread * 8;       // 16384 elements per
 constexpr int kMaxChunks = 64;                             // vocabularies up to 1,048,576
 constexpr float kEps32 = 1e-8f;
 constexpr double kEps = 1e-8;
+constexpr int kSibBatch = 8;                               // sibling groups up to this size live in registers
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct RowStat {
@@ -187,7 +188,7 @@ struct __align__(16) NodeRec {
   int16_t reset_t;         // time the node's subtree was last recomputed
   int16_t parent;
   float stored_pa;         // p_alpha set directly at time sticky_t
-  float ratio;             // Mb/Ms (0 when Ms <= eps), kept current
+  int32_t pad;
 };
 
 struct WalkSmem {
@@ -317,7 +318,7 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
       const int c = ru.first_valid;
       const NodeRec rc = w.rec[c];
       const int rmax = max(rmax_u, (int)ru.reset_t);
-      const float pa = rc.sticky_t > rmax ? rc.stored_pa : fminf(__fmul_rn(pa_u, rc.ratio), 1.0f);
+      const float pa = rc.sticky_t > rmax ? rc.stored_pa : fminf(__fmul_rn(pa_u, ratio_of(w.mb[c], w.ms[c])), 1.0f);
       ++depth;
       w.path[depth] = (int16_t)c;
       w.path_pa[depth] = pa;
@@ -342,48 +343,98 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
       break;
     }
     --depth;                                                          // back to the parent
+    double S_out = 0.0;
     const int c0 = w.child_start[parent], nc = w.child_cnt[parent];
-    if (w.rec[parent].first_valid == cand) {
-      int next = -1;
-      bool after = false;
-      for (int i = 0; i < nc; ++i) {
-        const int c = w.sib[c0 + i];
-        if (after && w.valid[c]) {
-          next = c;
-          break;
-        }
-        if (c == cand) after = true;
-      }
-      w.rec[parent].first_valid = (int16_t)next;
-      if (next < 0) continue;                                         // :417 no active sibling
-    }
+    const int fv_old = w.rec[parent].first_valid;
     const float p_old32 = w.path_pa[depth];                           // :422
     const double p_old = (double)p_old32;
     float s_tree = 0.0f, sum_mb = 0.0f;                               // :429-433, left to right
-    for (int i = 0; i < nc; ++i) {
-      const int c = w.sib[c0 + i];
-      const float mbv = w.mb[c];
-      s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), w.ms[c]), 0.0f));
-      sum_mb = __fadd_rn(sum_mb, mbv);
-    }
     double ms_denom = __dsub_rn(1.0, old_ms_rej);                     // :424
     if (ms_denom < kEps) ms_denom = kEps;
-    double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
-    if (S < kEps) S = kEps;                                           // :435
+    if (nc <= kSibBatch) {
+      // the sibling group in registers: one round of independent loads
+      int cs[kSibBatch];
+      float mbs[kSibBatch], mss[kSibBatch];
+      bool vs[kSibBatch];
+#pragma unroll
+      for (int k = 0; k < kSibBatch; ++k) cs[k] = k < nc ? w.sib[c0 + k] : 0;
+#pragma unroll
+      for (int k = 0; k < kSibBatch; ++k) {
+        mbs[k] = k < nc ? w.mb[cs[k]] : 0.0f;
+        mss[k] = k < nc ? w.ms[cs[k]] : 0.0f;
+        vs[k] = k < nc && w.valid[cs[k]];
+      }
+      if (fv_old == cand) {
+        int next = -1;
+        bool after = false;
+#pragma unroll
+        for (int k = 0; k < kSibBatch; ++k) {
+          if (next < 0 && after && vs[k]) next = cs[k];
+          if (k < nc && cs[k] == cand) after = true;
+        }
+        w.rec[parent].first_valid = (int16_t)next;
+        if (next < 0) continue;                                       // :417 no active sibling
+      }
+#pragma unroll
+      for (int k = 0; k < kSibBatch; ++k) {
+        if (k < nc) {
+          s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbs[k]), mss[k]), 0.0f));
+          sum_mb = __fadd_rn(sum_mb, mbs[k]);
+        }
+      }
+      double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
+      if (S < kEps) S = kEps;                                         // :435
+      const float ms_denom32 = __double2float_rn(ms_denom);
+      const float S32 = __double2float_rn(S);
+#pragma unroll
+      for (int k = 0; k < kSibBatch; ++k) {                           // :443-448
+        if (vs[k]) {
+          const float ms_new = __fdiv_rn(mss[k], ms_denom32);
+          const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbs[k]), mss[k]), 0.0f), S32);
+          w.ms[cs[k]] = ms_new;
+          w.mb[cs[k]] = mb_new;
+        }
+      }
+      S_out = S;
+    } else {
+      if (fv_old == cand) {
+        int next = -1;
+        bool after = false;
+        for (int i = 0; i < nc; ++i) {
+          const int c = w.sib[c0 + i];
+          if (after && w.valid[c]) {
+            next = c;
+            break;
+          }
+          if (c == cand) after = true;
+        }
+        w.rec[parent].first_valid = (int16_t)next;
+        if (next < 0) continue;                                       // :417 no active sibling
+      }
+      for (int i = 0; i < nc; ++i) {
+        const int c = w.sib[c0 + i];
+        const float mbv = w.mb[c];
+        s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), w.ms[c]), 0.0f));
+        sum_mb = __fadd_rn(sum_mb, mbv);
+      }
+      double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
+      if (S < kEps) S = kEps;                                         // :435
+      const float ms_denom32 = __double2float_rn(ms_denom);
+      const float S32 = __double2float_rn(S);
+      for (int i = 0; i < nc; ++i) {                                  // :443-448
+        const int c = w.sib[c0 + i];
+        if (!w.valid[c]) continue;
+        const float msv = w.ms[c], mbv = w.mb[c];
+        const float ms_new = __fdiv_rn(msv, ms_denom32);
+        const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
+        w.ms[c] = ms_new;
+        w.mb[c] = mb_new;
+      }
+      S_out = S;
+    }
+    const double S = S_out;
     const double p_new = __ddiv_rn(S, __dsub_rn(__dadd_rn(S, 1.0), p_old));                   // :439
     const double mb_rej = __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S);   // :451
-    const float ms_denom32 = __double2float_rn(ms_denom);
-    const float S32 = __double2float_rn(S);
-    for (int i = 0; i < nc; ++i) {                                    // :443-448
-      const int c = w.sib[c0 + i];
-      if (!w.valid[c]) continue;
-      const float msv = w.ms[c], mbv = w.mb[c];
-      const float ms_new = __fdiv_rn(msv, ms_denom32);
-      const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
-      w.ms[c] = ms_new;
-      w.mb[c] = mb_new;
-      w.rec[c].ratio = ratio_of(mb_new, ms_new);
-    }
     w.mb[cand] = __double2float_rn(mb_rej);                           // :452
     const float p_new32 = __double2float_rn(p_new);                   // :440, direct assignment
     w.rec[parent].stored_pa = p_new32;
@@ -448,36 +499,50 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
   }
+  constexpr int kOwn = 8;                                  // nodes per thread per pass
   int bad = 0;
-  for (int i = g.rank(); i < n; i += g.size()) {
-    const int par = p.parents[lo + i];
-    const int tok = p.tokens[lo + i];
-    if ((i == 0 && par != -1) || (i > 0 && (par < 0 || par >= i))) bad = 1;
-    NodeRec r;
-    r.first_valid = -1;
-    r.sticky_t = i == 0 ? 0 : -1;
-    r.reset_t = -1;
-    r.parent = (int16_t)par;
-    r.stored_pa = 1.0f;
-    r.ratio = 0.0f;
-    w.token[i] = tok;
-    w.valid[i] = 1;
-    if (p.traversal) {
-      if (i == 0) {
-        w.mb[0] = 1.0f;
-        w.ms[0] = 1.0f;
-      } else if (par >= 0 && par < i) {
-        const RowStat* rs = p.row_ws + lo + par;
-        const float pm = __ldcg(&rs->m), ps = __ldcg(&rs->s);
-        const float x = (tok >= 0 && tok < p.vocab)
-                            ? load_scaled(p, p.logits + (int64_t)(lo + par) * p.row_stride, tok)
-                            : -INFINITY;
-        w.mb[i] = prob_bf16(x, pm, ps);                                // :349
-        w.ms[i] = p.draft_probs[lo + i];                               // :353
-      }
-      if (i == 0 || (par >= 0 && par < i)) r.ratio = ratio_of(w.mb[i], w.ms[i]);
+  for (int pass = 0; pass * kOwn * g.size() < n; ++pass) {
+    // every global load of a pass is issued before any result is used
+    int par[kOwn], tok[kOwn];
+    float msv[kOwn], pm[kOwn], ps[kOwn], x[kOwn];
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int i = (pass * kOwn + t) * g.size() + g.rank();
+      par[t] = i < n ? p.parents[lo + i] : -1;
+      tok[t] = i < n ? p.tokens[lo + i] : -1;
+      msv[t] = (p.traversal && i > 0 && i < n) ? p.draft_probs[lo + i] : 1.0f;           // :353
     }
-    w.rec[i] = r;
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int i = (pass * kOwn + t) * g.size() + g.rank();
+      const bool use = p.traversal && i > 0 && i < n && par[t] >= 0 && par[t] < i;
+      pm[t] = use ? __ldcg(&p.row_ws[lo + par[t]].m) : 0.0f;
+      ps[t] = use ? __ldcg(&p.row_ws[lo + par[t]].s) : 1.0f;
+      x[t] = (use && tok[t] >= 0 && tok[t] < p.vocab)
+                 ? load_scaled(p, p.logits + (int64_t)(lo + par[t]) * p.row_stride, tok[t])
+                 : -INFINITY;
+    }
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int i = (pass * kOwn + t) * g.size() + g.rank();
+      if (i >= n) continue;
+      if ((i == 0 && par[t] != -1) || (i > 0 && (par[t] < 0 || par[t] >= i))) bad = 1;
+      NodeRec r;
+      r.first_valid = -1;
+      r.sticky_t = i == 0 ? 0 : -1;
+      r.reset_t = -1;
+      r.parent = (int16_t)par[t];
+      r.stored_pa = 1.0f;
+      r.pad = 0;
+      w.token[i] = tok[t];
+      w.valid[i] = 1;
+      if (p.traversal) {
+        const float mb = i == 0 ? 1.0f : (par[t] >= 0 && par[t] < i ? prob_bf16(x[t], pm[t], ps[t]) : 0.0f);   // :349
+        w.mb[i] = mb;
+        w.ms[i] = msv[t];
+      }
+      w.rec[i] = r;
+    }
   }
   if (p.traversal)
     for (int k = g.rank(); k < 2 * n + 2; k += g.size())
@@ -488,8 +553,59 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
   }
-  if (g.rank() == 0) {
-    // children in ascending order: linked lists and a contiguous (CSR) copy
+  // children in ascending node order: counts and sibling ranks from one pass
+  // over the parents (read by every thread at once), then CSR and linked lists
+  if (n <= kOwn * g.size()) {
+    int cnt[kOwn], rnk[kOwn], px[kOwn];
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int xi = t * g.size() + g.rank();
+      cnt[t] = 0;
+      rnk[t] = 0;
+      px[t] = xi < n ? w.rec[xi].parent : -2;
+    }
+    const int own = (n + g.size() - 1) / g.size();           // <= kOwn
+    for (int j = 0; j < n; ++j) {
+      const int pj = w.rec[j].parent;
+#pragma unroll
+      for (int t = 0; t < kOwn; ++t) {
+        if (t >= own) break;
+        const int xi = t * g.size() + g.rank();
+        cnt[t] += (pj == xi) ? 1 : 0;
+        rnk[t] += (j < xi && pj == px[t]) ? 1 : 0;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int xi = t * g.size() + g.rank();
+      if (xi < n) w.child_cnt[xi] = (int16_t)cnt[t];
+    }
+    g.sync();
+    if (g.rank() == 0) {
+      int o = 0;
+      for (int i = 0; i < n; ++i) {
+        w.child_start[i] = (int16_t)o;
+        o += w.child_cnt[i];
+      }
+    }
+    g.sync();
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int xi = t * g.size() + g.rank();
+      if (xi >= 1 && xi < n) w.sib[w.child_start[px[t]] + rnk[t]] = (int16_t)xi;
+    }
+    g.sync();
+#pragma unroll
+    for (int t = 0; t < kOwn; ++t) {
+      const int xi = t * g.size() + g.rank();
+      if (xi >= n) continue;
+      const int fc = cnt[t] > 0 ? w.sib[w.child_start[xi]] : -1;
+      w.first_child[xi] = (int16_t)fc;
+      w.rec[xi].first_valid = (int16_t)fc;
+      w.next_sib[xi] = (xi >= 1 && rnk[t] + 1 < w.child_cnt[px[t]]) ? w.sib[w.child_start[px[t]] + rnk[t] + 1] : -1;
+    }
+    g.sync();
+  } else if (g.rank() == 0) {
     for (int i = 0; i < n; ++i) {
       w.first_child[i] = -1;
       w.child_cnt[i] = 0;
@@ -507,10 +623,12 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
       for (int c = w.first_child[i]; c >= 0; c = w.next_sib[c]) w.sib[o++] = (int16_t)c;
       w.rec[i].first_valid = w.first_child[i];
     }
-    if (!p.traversal) walk_greedy(p, b, lo, w);
   }
   g.sync();
-  if (p.traversal && g.rank() == 0) walk_traversal(p, b, lo, n, w);
+  if (g.rank() == 0) {
+    if (p.traversal) walk_traversal(p, b, lo, n, w);
+    else walk_greedy(p, b, lo, w);
+  }
   g.sync();
 }
 
