@@ -791,27 +791,27 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
 // of a row -- through a ring of shared-memory slots:
 //   warp 0        producer: one cp.async.bulk (1-D, no multicast) per item,
 //                 kSSlots items ahead of the consumers;
-//   warps 1-8     consumers: 64 values per thread (eight 16-byte shared loads,
+//   warps 1-16    consumers: 32 values per thread (four 16-byte shared loads,
 //                 the slot released right after), thread max by packed bf16x2
 //                 max, sum of exp(x - max) with packed f32x2 FMA/add and MUFU
 //                 exp2, folded into a running (max, sum) per thread; the warp's
 //                 max and its first index are updated only when a chunk raises
 //                 it (searched by the threads that hold it), and the warp's
 //                 partial of the row is reduced and handed over once per row;
-//   warp 9        merger: combines the 8 warp partials of a row (or of a chunk
+//   warp 17       merger: combines the 16 warp partials of a row (or of a chunk
 //                 of a split row), derives the row statistics with the tie
 //                 rescan, and counts the request's finished rows;
-//   warp 10       walker: claims the next slot of the workspace's publication
+//   warp 18       walker: claims the next slot of the workspace's publication
 //                 list and runs the tree walk of the request the mergers publish
 //                 there (the walks of different requests run on different SMs,
 //                 each as soon as the request's last row is done, while the
 //                 other warps stream the following rows).
 constexpr int kSChunk = 16384;                 // elements per item (32 KB)
 constexpr int kSSlots = 5;
-constexpr int kSConsumerWarps = 8;
+constexpr int kSConsumerWarps = 16;
 constexpr int kSConsumers = kSConsumerWarps * 32;
 constexpr int kSThreads = kSConsumers + 96;    // + producer, merger and walker warps
-constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (8)
+constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (4)
 constexpr long long kSpinLimit = 4000000000ll;     // clock cycles, about 2 s
 
 struct __align__(16) StreamCtl {
