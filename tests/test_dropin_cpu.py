@@ -1,0 +1,99 @@
+"""Host-side parts of the drop-in modules, on CPU: the Tree mirror against the
+reference's golden masks, page bookkeeping of KvCachePool / RequestKvCache,
+and the reference's error behaviour (no GPU needed, no kernel is called)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as att
+from parallel_tree_spec_b200 import cache_manager as cm
+from parallel_tree_spec_b200 import verification as ver
+from parallel_tree_spec_b200 import workload as wl
+from parallel_tree_spec_b200.tree import Tree
+
+
+def test_tree_mask_matches_reference_golden(mask_golden):
+    """Tree.create_attention_mask gives the reference's bits (tree.py:167-194)."""
+    for rec in mask_golden:
+        t = Tree.from_arrays(rec["parents"], list(range(len(rec["parents"]))))
+        m = t.create_attention_mask(prefix_length=rec["prefix"])
+        assert list(m.shape) == rec["shape"]
+        flat = m.reshape(-1).numpy().astype(bool)
+        bits = np.unpackbits(np.asarray(rec["packed"], np.uint8))[: flat.size].astype(bool)
+        assert np.array_equal(flat, bits)
+
+
+def test_tree_columns_depths_and_children():
+    rng = np.random.default_rng(5)
+    w = wl.make_tree(rng, 4, 5, 1000)
+    t = Tree.from_arrays(w.parents, w.tokens, w.draft_probs)
+    par, tok, prob, _ = t.as_arrays()
+    assert np.array_equal(par, w.parents) and np.array_equal(tok, w.tokens)
+    assert np.allclose(prob[1:], w.draft_probs[1:])
+    data = t.get_tree_data()
+    depth = np.zeros(len(w.parents), np.int64)
+    for i in range(1, len(w.parents)):
+        depth[i] = depth[w.parents[i]] + 1
+    assert np.array_equal(np.asarray(data["depths"]).reshape(-1), depth)
+    for i in range(t.current_size):
+        kids = [c for c in range(len(w.parents)) if w.parents[c] == i]
+        assert t.get_children_indices(i).tolist() == kids
+        assert t.get_children_ids(i).tolist() == [int(w.tokens[c]) for c in kids]
+    assert t.get_depth() == int(depth.max())
+    assert np.array_equal(t.create_attention_mask(prefix_length=9)[0, 0].numpy(), att.tree_mask(w.parents, 9))
+
+
+def test_tree_add_nodes_levels():
+    """add_nodes appends levels whose entries name a parent by its position in
+    the current leaves (tree.py:78-121)."""
+    t = Tree(7)
+    t.add_nodes(torch.tensor([[[11, 12]]]), torch.tensor([[[0.6, 0.3]]]), torch.tensor([[[0, 0]]]))
+    t.add_nodes(torch.tensor([[[21, 22, 23]]]), torch.tensor([[[0.5, 0.2, 0.9]]]), torch.tensor([[[0, 1, 1]]]))
+    par, tok, _, _ = t.as_arrays()
+    assert par.tolist() == [-1, 0, 0, 1, 2, 2]
+    assert tok.tolist() == [7, 11, 12, 21, 22, 23]
+    assert t.available_leaves == [3, 4, 5]
+    assert t.find_child_index(2, 23) == 5
+
+
+def test_tree_errors():
+    t = Tree.from_arrays([-1, 0, 0], [1, 2, 3])
+    with pytest.raises(IndexError):
+        t.get_node(3)
+    with pytest.raises(ValueError):
+        Tree.from_arrays([-1, 2, 0], [1, 2, 3])
+
+
+def test_pool_and_request_page_bookkeeping():
+    pool = cm.KvCachePool(10, 1, 2, 8, 16, torch.bfloat16, "cpu")
+    a = cm.RequestKvCache(pool, 16, 37)                       # 3 pages, 5 tokens on the last
+    assert (a.kv_page_indices, a.kv_last_page_len, a.kv_len) == ([0, 1, 2], 5, 37)
+    a.increment(30)                                           # 67 tokens: 5 pages, 3 on the last
+    assert (len(a.kv_page_indices), a.kv_last_page_len, a.kv_len) == (5, 3, 67)
+    b = cm.RequestKvCache(pool, 16, 16)
+    assert b.kv_page_indices == [5] and b.kv_last_page_len == 16
+    a.decrement(20)                                           # 47 tokens: 3 pages
+    assert (len(a.kv_page_indices), a.kv_last_page_len) == (3, 15)
+    assert pool.num_free_pages() == 10 - 3 - 1
+    with pytest.raises(AssertionError):                       # cache_manager.py:92
+        pool.allocate(100)
+    a.release()
+    b.release()
+    assert pool.num_free_pages() == 10
+
+
+def test_reference_error_types():
+    """Unknown modes and methods raise ValueError; CPU logits are refused
+    (this path has no CPU implementation)."""
+    pool = cm.KvCachePool(4, 1, 2, 8, 16, torch.bfloat16, "cpu")
+    r = cm.RequestKvCache(pool, 16, 5)
+    with pytest.raises(ValueError):
+        cm.getKvCacheBatchPosition([r], "sideways", "cpu")
+    t = Tree.from_arrays([-1, 0], [1, 2])
+    x = torch.zeros(2, 32, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ver.verify_tree_exact(t, x)
+    with pytest.raises(ValueError):
+        ver.verify_tree_traversal(t, x)
+    with pytest.raises(ValueError):
+        ver.verify_tree_exact(t, x, root_ind=1)
