@@ -85,9 +85,30 @@ struct AcceptParams {
   struct Part* part_ws;
   unsigned* row_ctr;
   unsigned* req_ctr;
-  unsigned* walk_ctr;      // [0] requests published, [1] requests claimed by walkers
-  int* walk_q;             // published requests (b + 1; 0 = not yet)
+  unsigned* walk_ctr;      // [1]: requests claimed by the persistent kernel's walkers
+  unsigned* row_done;      // per row: 1 once its statistics are in row_ws (release/acquire)
 };
+
+constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
+
+// Publishes row `row`'s statistics (already stored by this thread in row_ws).
+__device__ __forceinline__ void publish_row(const AcceptParams& p, int row) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.row_done + row), "r"(1u) : "memory");
+}
+
+// Bounded wait until row `row`'s statistics are published; false on timeout.
+__device__ __forceinline__ bool wait_row(const AcceptParams& p, int row) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.row_done + row) : "memory");
+  if (v) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    __nanosleep(128);
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.row_done + row) : "memory");
+    if (v) return true;
+    if (clock64() - t0 > kRowWaitLimit) return false;
+  }
+}
 
 __device__ __forceinline__ float load_scaled(const AcceptParams& p, const uint16_t* row, int i) {
   float x = bf16_bits_to_float(row[i]);
@@ -255,6 +276,10 @@ __device__ void walk_greedy(const AcceptParams& p, int b, int lo, const WalkSmem
   int bonus = -1, last_tok = -1;
   while (w.first_child[cur] >= 0) {                                   // :232
     total++;
+    if (!wait_row(p, lo + cur)) {
+      write_counts(p, b, -3, 0, 0, 0);
+      return;
+    }
     const int tok = __ldcg(&p.row_ws[lo + cur].argmax);               // :73
     int match = -1;
     for (int c = w.first_child[cur]; c >= 0; c = w.next_sib[c])
@@ -280,7 +305,13 @@ __device__ void walk_greedy(const AcceptParams& p, int b, int lo, const WalkSmem
     }
   }
   if (n_out == 0 || p.eos < 0 || (int64_t)last_tok != p.eos) {        // :257
-    if (bonus < 0) bonus = __ldcg(&p.row_ws[lo + cur].argmax);        // :260-262
+    if (bonus < 0) {
+      if (!wait_row(p, lo + cur)) {
+        write_counts(p, b, -3, 0, 0, 0);
+        return;
+      }
+      bonus = __ldcg(&p.row_ws[lo + cur].argmax);                     // :260-262
+    }
     if (n_out < p.out_stride) {
       ot[n_out] = bonus;
       oh[n_out] = cur;
@@ -462,6 +493,10 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
     if (p.eos >= 0 && (int64_t)tok == p.eos) break;
   }
   if (!(n_out > 0 && p.eos >= 0 && (int64_t)last_tok == p.eos)) {
+    if (!wait_row(p, lo + accepted)) {                                // a leaf row may still stream
+      write_counts(p, b, -3, 0, 0, 0);
+      return;
+    }
     const int bonus = __ldcg(&p.row_ws[lo + accepted].argmax);        // :511
     if (n_out < p.out_stride) {
       ot[n_out] = bonus;
@@ -495,12 +530,12 @@ struct WarpGroup {
 // child lists, then walk (greedy or traversal) on the group's first thread.
 template <class G>
 __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
-  if (n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
+  if (n <= 0 || n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
   }
   constexpr int kOwn = 8;                                  // nodes per thread per pass
-  int bad = 0;
+  int bad = 0, late = 0;
   for (int pass = 0; pass * kOwn * g.size() < n; ++pass) {
     // every global load of a pass is issued before any result is used
     int par[kOwn], tok[kOwn];
@@ -515,7 +550,11 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
 #pragma unroll
     for (int t = 0; t < kOwn; ++t) {
       const int i = (pass * kOwn + t) * g.size() + g.rank();
-      const bool use = p.traversal && i > 0 && i < n && par[t] >= 0 && par[t] < i;
+      bool use = p.traversal && i > 0 && i < n && par[t] >= 0 && par[t] < i;
+      if (use && !wait_row(p, lo + par[t])) {                  // parents' rows stream first
+        late = 1;
+        use = false;
+      }
       pm[t] = use ? __ldcg(&p.row_ws[lo + par[t]].m) : 0.0f;
       ps[t] = use ? __ldcg(&p.row_ws[lo + par[t]].s) : 1.0f;
       x[t] = (use && tok[t] >= 0 && tok[t] < p.vocab)
@@ -548,9 +587,10 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
     for (int k = g.rank(); k < 2 * n + 2; k += g.size())
       w.uni[k] = philox_uniform(p.seed, p.offset, (uint32_t)b, (uint32_t)k);
   bad = g.any(bad != 0, red_sm);
+  late = g.any(late != 0, red_sm);
   g.sync();
-  if (bad) {
-    if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
+  if (bad || late) {
+    if (g.rank() == 0) write_counts(p, b, bad ? -1 : -3, 0, 0, 0);
     return;
   }
   // children in ascending node order: counts and sibling ranks from one pass
@@ -765,6 +805,7 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
       rs.argmax = s_arg;
       rs.flags = s_tie;
       p.row_ws[row] = rs;
+      publish_row(p, row);
       s_b = b;
       s_lo = p.row_indptr[b];
       s_n = p.row_indptr[b + 1] - s_lo;
@@ -813,6 +854,7 @@ constexpr int kSConsumers = kSConsumerWarps * 32;
 constexpr int kSThreads = kSConsumers + 96;    // + producer, merger and walker warps
 constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (4)
 constexpr long long kSpinLimit = 4000000000ll;     // clock cycles, about 2 s
+constexpr size_t kMaxDynSmem = 232448;             // 227 KB per CTA
 
 struct __align__(16) StreamCtl {
   uint64_t full[kSSlots];
@@ -826,30 +868,58 @@ constexpr size_t kSRingBytes = (size_t)kSSlots * kSChunk * 2;
 constexpr size_t kSCtlOff = kSRingBytes;
 constexpr size_t kSWalkOff = (kSCtlOff + sizeof(StreamCtl) + 127) & ~(size_t)127;
 
-// The work of CTA c: first its whole rows, then its chunks of the split rows.
+// The work of CTA c.  Rows are taken in "stream order": the internal rows
+// (every request's root and every row with children) of all requests first,
+// then the leaf rows, each group in row order.  Position q of the stream order
+// is a whole row of CTA q % G while q < split_first_row; the remaining
+// num_rows % G positions are split by chunk over all CTAs.  A traversal walk
+// needs the statistics of internal rows only (its target probabilities come
+// from the parents' rows) and one leaf row at most (the bonus token), so the
+// walks start while the leaf rows still stream.
 struct StreamPlan {
   int G, nchunks, whole_rows_per_cta, split_first_row, split_items;
+  int num_rows, mask_words;
   __device__ int items(int c) const {
     const int extra = split_items > c ? (split_items - c + G - 1) / G : 0;
     return whole_rows_per_cta * nchunks + extra;
   }
-  // row, chunk and whether item k ends a segment (a whole row, or one split chunk)
-  __device__ void item(int c, int k, int& row, int& chunk, bool& seg_end, bool& whole) const {
+  // row, chunk and whether item k ends a segment (a whole row, or one split
+  // chunk); `mine` lists the CTA's whole rows, `split` the split rows
+  __device__ void item(int c, int k, const uint16_t* mine, const uint16_t* split, int& row, int& chunk,
+                       bool& seg_end, bool& whole) const {
     const int n1 = whole_rows_per_cta * nchunks;
     if (k < n1) {
-      row = c + (k / nchunks) * G;
+      row = mine[k / nchunks];
       chunk = k % nchunks;
       seg_end = chunk == nchunks - 1;
       whole = true;
     } else {
       const int j = c + (k - n1) * G;
-      row = split_first_row + j / nchunks;
+      row = split[j / nchunks];
       chunk = j % nchunks;
       seg_end = true;
       whole = nchunks == 1;
     }
   }
 };
+
+// Shared-memory bytes of the stream-order tables (internal-row bit mask, the
+// CTA's whole rows, the split rows, scan scratch), placed after the walk state.
+__host__ __device__ inline size_t order_smem_bytes(const StreamPlan& pl) {
+  return (size_t)pl.mask_words * 4 + (((size_t)pl.whole_rows_per_cta * 2 + 15) & ~(size_t)15) +
+         (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4;
+}
+
+// First row of the request that holds `row` (binary search over row_indptr).
+__device__ __forceinline__ int request_first_row(const int32_t* indptr, int batch, int row) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(indptr + mid) <= row) lo = mid;
+    else hi = mid - 1;
+  }
+  return __ldg(indptr + lo);
+}
 
 __device__ __forceinline__ uint64_t f2(float a, float b) {
   uint64_t r;
@@ -905,8 +975,8 @@ __device__ __forceinline__ bool s_mbar_wait(uint64_t* bar, uint32_t parity, uint
 }
 // Row statistics from the row's merged partial `r` (valid in lane 0), by one
 // warp (the warp rescans the row when a value below the max can round to the
-// same probability); returns true, with the request, when the row completes it.
-__device__ bool finish_row_warp(const AcceptParams& p, int row, Part r, int* out_b) {
+// same probability), stored and published in the workspace.
+__device__ void finish_row_warp(const AcceptParams& p, int row, Part r) {
   const int lane = threadIdx.x & 31;
   float m = 0.0f, sf = 0.0f, qmax = 0.0f;
   int arg = 0, tie = 0;
@@ -934,8 +1004,6 @@ __device__ bool finish_row_warp(const AcceptParams& p, int row, Part r, int* out
     for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
     arg = best;
   }
-  const int b = find_request(p.row_indptr, p.batch, row);
-  int flag = 0;
   if (lane == 0) {
     RowStat rs;
     rs.m = m;
@@ -943,13 +1011,9 @@ __device__ bool finish_row_warp(const AcceptParams& p, int row, Part r, int* out
     rs.argmax = arg;
     rs.flags = tie;
     p.row_ws[row] = rs;
-    const int n = p.row_indptr[b + 1] - p.row_indptr[b];
-    unsigned prev;    // release: this row's stats; acquire: every earlier row's
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.req_ctr[b]) : "memory");
-    flag = (prev == (unsigned)(n - 1));
+    publish_row(p, row);
   }
-  *out_b = b;
-  return __shfl_sync(0xffffffffu, flag, 0) != 0;
+  __syncwarp();
 }
 
 __device__ __forceinline__ Part shfl_part(const Part& x, int src_lane_xor) {
@@ -969,6 +1033,13 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   const int n_items = plan.items(c);
   const Part kNone{0.0, -INFINITY, INT_MAX};
 
+  // stream-order tables after the walk state
+  uint8_t* otab = sm + ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15);
+  uint32_t* imask = reinterpret_cast<uint32_t*>(otab);
+  uint16_t* mine = reinterpret_cast<uint16_t*>(otab + (size_t)plan.mask_words * 4);
+  uint16_t* split = mine + ((plan.whole_rows_per_cta + 7) & ~7);
+  int* scan = reinterpret_cast<int*>(split + ((plan.num_rows - plan.split_first_row + 7) & ~7));
+
   if (tid == 0) {
     for (int i = 0; i < kSSlots; ++i) {
       s_mbar_init(&ctl.full[i], 1);
@@ -979,6 +1050,52 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       s_mbar_init(&ctl.seg_empty[i], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // ---- stream order (every CTA computes it for its own rows) ---------------
+  for (int i = tid; i < plan.mask_words; i += kSThreads) imask[i] = 0u;
+  __syncthreads();
+  for (int j = tid; j < plan.num_rows; j += kSThreads) {
+    const int lo = request_first_row(p.row_indptr, p.batch, j);
+    const int pj = p.parents[j];
+    const int r = (j == lo) ? j : ((pj >= 0 && pj < j - lo) ? lo + pj : -1);
+    if (r >= 0) atomicOr(&imask[r >> 5], 1u << (r & 31));
+  }
+  __syncthreads();
+  {
+    const int per = (plan.num_rows + kSThreads - 1) / kSThreads;
+    const int r0 = min(tid * per, plan.num_rows), r1 = min(r0 + per, plan.num_rows);
+    int cnt = 0;
+    for (int r = r0; r < r1; ++r) cnt += (imask[r >> 5] >> (r & 31)) & 1;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) scan[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < kSThreads / 32 ? scan[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      if (lane < kSThreads / 32) scan[lane] = v;
+    }
+    __syncthreads();
+    const int n_int = scan[kSThreads / 32 - 1];
+    int ib = (warp ? scan[warp - 1] : 0) + incl - cnt;       // internal rows before r0
+    for (int r = r0; r < r1; ++r) {
+      const int in = (imask[r >> 5] >> (r & 31)) & 1;
+      const int q = in ? ib : n_int + (r - ib);
+      ib += in;
+      if (q < plan.split_first_row) {
+        if (q % plan.G == c) mine[q / plan.G] = (uint16_t)r;
+      } else {
+        split[q - plan.split_first_row] = (uint16_t)r;
+      }
+    }
   }
   __syncthreads();
 
@@ -992,7 +1109,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       if (lane == 0) {
         int row, chunk;
         bool seg_end, whole;
-        plan.item(c, k, row, chunk, seg_end, whole);
+        plan.item(c, k, mine, split, row, chunk, seg_end, whole);
         const int n_el = min(kSChunk, p.vocab - chunk * kSChunk);
         s_mbar_expect(&ctl.full[slot], (uint32_t)n_el * 2);
         bulk_g2s(ring + (size_t)slot * kSChunk * 2, p.logits + (int64_t)row * p.row_stride + (int64_t)chunk * kSChunk,
@@ -1017,7 +1134,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       const int slot = k % kSSlots;
       int row, chunk;
       bool seg_end, whole;
-      plan.item(c, k, row, chunk, seg_end, whole);
+      plan.item(c, k, mine, split, row, chunk, seg_end, whole);
       const int base = chunk * kSChunk;
       const int n_el = min(kSChunk, p.vocab - base);
       if (!s_mbar_wait(&ctl.full[slot], (k / kSSlots) & 1, 0)) break;
@@ -1116,7 +1233,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     for (int k = 0; k < n_items; ++k) {
       int row, chunk;
       bool seg_end, whole;
-      plan.item(c, k, row, chunk, seg_end, whole);
+      plan.item(c, k, mine, split, row, chunk, seg_end, whole);
       if (!seg_end) continue;
       const int buf = seg & 1;
       if (!s_mbar_wait(&ctl.seg_full[buf], (seg >> 1) & 1, 0)) break;
@@ -1147,36 +1264,20 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
         }
       }
       if (!row_done) continue;
-      int b;
-      if (finish_row_warp(p, row, x, &b) && lane == 0) {
-        // publish the request for whichever walker claimed the next slot
-        const unsigned slot = atomicAdd(&p.walk_ctr[0], 1u);
-        asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p.walk_q + slot), "r"(b + 1) : "memory");
-      }
-      __syncwarp();
+      finish_row_warp(p, row, x);
     }
   } else {
     // ---------------------------------------------------------------- walker
-    // Claims the next publication slot and walks the request that lands in it,
-    // so the walks of different requests run on different SMs.
+    // Claims the next request and walks it, waiting for each row it reads
+    // (parents' rows, the bonus row) to be published: the walks of different
+    // requests run on different SMs while the leaf rows still stream.
     const WalkSmem w = walk_smem(sm + kSWalkOff, p.max_nodes);
     for (;;) {
       unsigned t = 0;
       if (lane == 0) t = atomicAdd(&p.walk_ctr[1], 1u);
       t = __shfl_sync(0xffffffffu, t, 0);
       if (t >= (unsigned)p.batch) break;
-      int v = 0;
-      if (lane == 0) {
-        const long long t0 = clock64();
-        for (;;) {
-          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p.walk_q + t) : "memory");
-          if (v != 0 || clock64() - t0 > 10 * kSpinLimit) break;   // bounded (about 20 s)
-          __nanosleep(256);
-        }
-      }
-      v = __shfl_sync(0xffffffffu, v, 0);
-      if (v == 0) break;
-      const int b = v - 1;
+      const int b = (int)t;
       const int lo = p.row_indptr[b];
       walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr);
     }
@@ -1208,7 +1309,7 @@ size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, s
   *off_qctr = o;
   o = align_up(o + (size_t)num_rows * sizeof(unsigned), 256);
   if (off_walk) *off_walk = o;
-  o = align_up(o + 2 * sizeof(unsigned) + (size_t)num_rows * sizeof(int), 256);
+  o = align_up(o + 2 * sizeof(unsigned) + (size_t)num_rows * sizeof(unsigned), 256);   // walk_ctr, row_done
   return o;
 }
 
@@ -1239,13 +1340,16 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   p.row_ctr = (unsigned*)(ws + orc);
   p.req_ctr = (unsigned*)(ws + oqc);
   p.walk_ctr = (unsigned*)(ws + owk);
-  p.walk_q = (int*)(ws + owk + 2 * sizeof(unsigned));
+  p.row_done = (unsigned*)(ws + owk + 2 * sizeof(unsigned));
   p.traversal = traversal;
   p.use_temp = (temperature != 1.0f);
   p.inv_temp = 1.0f / temperature;
   p.vec_ok = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
   PTS_CUDA_TRY(cudaMemsetAsync(ws + orc, 0, need - orc, stream));
   const int sms = stream_sm_count();
+  int dev = 0;
+  PTS_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) return set_error(PTS_ERR_UNSUPPORTED, "device ordinal %d", dev);
   if (p.vec_ok && p.vocab % 8 == 0 && sms > 0) {
     StreamPlan plan;
     plan.G = min(sms, p.num_rows * nchunks);
@@ -1253,22 +1357,27 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
     plan.whole_rows_per_cta = p.num_rows / plan.G;
     plan.split_first_row = plan.whole_rows_per_cta * plan.G;
     plan.split_items = (p.num_rows - plan.split_first_row) * nchunks;
-    const size_t ssmem = kSWalkOff + walk_smem_bytes(p.max_nodes);
-    static size_t ssmem_attr = 0;
-    if (ssmem > ssmem_attr) {
-      PTS_CUDA_TRY(cudaFuncSetAttribute(accept_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
-      ssmem_attr = ssmem;
+    plan.num_rows = p.num_rows;
+    plan.mask_words = (p.num_rows + 31) / 32;
+    const size_t ssmem = ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan);
+    if (ssmem <= kMaxDynSmem) {
+      static size_t ssmem_attr[256] = {};
+      if (ssmem > ssmem_attr[dev]) {
+        PTS_CUDA_TRY(
+            cudaFuncSetAttribute(accept_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
+        ssmem_attr[dev] = ssmem;
+      }
+      accept_stream_kernel<<<plan.G, kSThreads, ssmem, stream>>>(p, plan);
+      return launch_status("accept_stream_kernel");
     }
-    accept_stream_kernel<<<plan.G, kSThreads, ssmem, stream>>>(p, plan);
-    return launch_status("accept_stream_kernel");
   }
   const size_t smem = walk_smem_bytes(p.max_nodes);
-  static size_t smem_attr = 0;
-  if (smem > smem_attr) {
+  static size_t smem_attr[256] = {};
+  if (smem > smem_attr[dev]) {
     PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                       (int)cudaSharedmemCarveoutMaxShared));
-    smem_attr = smem;
+    smem_attr[dev] = smem;
   }
   accept_kernel<<<dim3(nchunks, p.num_rows), kThreads, smem, stream>>>(p);
   return launch_status("accept_kernel");

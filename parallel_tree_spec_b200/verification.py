@@ -143,6 +143,8 @@ def _results(ot, oh, oc, device_out):
     res = []
     for b in range(oc.shape[0]):
         n = int(oc[b, 0])
+        if n == -3:
+            raise RuntimeError(f"acceptance of tree {b} timed out waiting for its rows' statistics")
         if n < 0:
             raise ValueError(f"tree {b} is malformed (parents must precede children, root first)")
         toks = ot[b, :n].to(torch.long).unsqueeze(0)
