@@ -54,7 +54,6 @@ constexpr int kChunk = kThreads * kVecPerThread * 8;       // 16384 elements per
 constexpr int kMaxChunks = 64;                             // vocabularies up to 1,048,576
 constexpr float kEps32 = 1e-8f;
 constexpr double kEps = 1e-8;
-constexpr int kSibBatch = 8;                               // sibling groups up to this size live in registers
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct RowStat {
@@ -94,6 +93,27 @@ constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
 // Publishes row `row`'s statistics (already stored by this thread in row_ws).
 __device__ __forceinline__ void publish_row(const AcceptParams& p, int row) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.row_done + row), "r"(1u) : "memory");
+}
+
+__device__ __forceinline__ bool row_published(const AcceptParams& p, int row) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.row_done + row) : "memory");
+  return v != 0;
+}
+
+// Bounded wait, by a whole warp, until every lane's row (row < 0: none) is
+// published; false (in every lane) on timeout.  The loop condition is
+// warp-uniform, so the warp leaves it converged.
+__device__ __forceinline__ bool wait_rows_warp(const AcceptParams& p, int row) {
+  bool ready = row < 0 || row_published(p, row);
+  if (__all_sync(0xffffffffu, ready)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    __nanosleep(128);
+    if (!ready) ready = row_published(p, row);
+    if (__all_sync(0xffffffffu, ready)) return true;
+    if (__any_sync(0xffffffffu, clock64() - t0 > kRowWaitLimit)) return false;
+  }
 }
 
 // Bounded wait until row `row`'s statistics are published; false on timeout.
@@ -201,37 +221,46 @@ __device__ __forceinline__ int block_reduce_min(int v, int* sm) {
 }
 
 // Walk state in dynamic shared memory, sized for the call's largest tree
-// (capacity `cap` nodes), so streaming CTAs of small trees stay light.  The
-// fields a traversal descent reads for a node sit in one 16-byte record.
+// (capacity `cap` nodes), so streaming CTAs of small trees stay light.
+//
+// Children are numbered in CSR order: the children of every node occupy
+// consecutive "slots" in ascending node order (the order Tree.add_nodes
+// appends them, tree.py:108-119); the root takes slot n-1.  A node's Mb, Ms
+// and valid flag live at its slot, so a sibling group is one contiguous run
+// of slots, read in one round of loads.  The node record holds what a descent
+// step reads (first 16 bytes) and the node's slot, its sibling run and its
+// child run (second 16 bytes).
 struct __align__(16) NodeRec {
   int16_t first_valid;     // first child still valid (-1: none)
   int16_t sticky_t;        // time p_alpha was last set directly (-1: never)
-  int16_t reset_t;         // time the node's subtree was last recomputed
+  int16_t reset_t;         // time the node's subtree was last recomputed (-1: never)
   int16_t parent;
   float stored_pa;         // p_alpha set directly at time sticky_t
-  int32_t pad;
+  float ratio;             // Mb / Ms (0 when Ms <= eps), kept current with Mb and Ms
+  int16_t slot;            // this node's slot
+  int16_t sib_start;       // slots of its parent's children (the root: its own slot)
+  int16_t sib_cnt;
+  int16_t child_start;     // slots of its children
+  int16_t child_cnt;
+  int16_t pad[3];
 };
+static_assert(sizeof(NodeRec) == 32, "node record is two 16-byte words");
 
 struct WalkSmem {
-  NodeRec* rec;
-  int32_t* token;
-  int16_t* first_child;
-  int16_t* next_sib;
-  int16_t* path;
+  NodeRec* rec;            // by node
+  int32_t* token;          // by node
+  float2* val;             // by slot: (Mb, Ms); during set-up: child counts and slot bases
+  int16_t* sid;            // by slot: node
+  uint8_t* valid;          // by slot
+  int16_t* path;           // the descent path (nodes); during set-up: nothing
   int16_t* path_rmax;
-  int16_t* sib;            // children of every node, contiguous per parent
-  int16_t* child_start;
-  int16_t* child_cnt;
-  float* path_pa;
-  float* mb;
-  float* ms;
+  float* path_pa;          // during set-up: the nodes' Ms
   float* uni;              // 2 * cap + 2 uniforms
-  uint8_t* valid;
 };
 
 __host__ __device__ inline size_t walk_smem_bytes(int cap) {
   cap = (cap + 15) & ~15;
-  return (size_t)cap * (16 + 4 + 7 * 2 + 3 * 4 + 1) + (size_t)(2 * cap + 2) * 4 + 80;
+  return (size_t)cap * (32 + 4 + 8 + 2 + 1 + 2 + 2 + 4) + (size_t)(2 * cap + 2) * 4 + 160;
 }
 
 __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
@@ -243,20 +272,15 @@ __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
     q += (bytes + 15) & ~(size_t)15;
     return r;
   };
-  w.rec = (NodeRec*)take(cap * 16);
-  w.token = (int32_t*)take(cap * 4);
-  w.path_pa = (float*)take(cap * 4);
-  w.mb = (float*)take(cap * 4);
-  w.ms = (float*)take(cap * 4);
-  w.uni = (float*)take((2 * cap + 2) * 4);
-  w.first_child = (int16_t*)take(cap * 2);
-  w.next_sib = (int16_t*)take(cap * 2);
-  w.path = (int16_t*)take(cap * 2);
-  w.path_rmax = (int16_t*)take(cap * 2);
-  w.sib = (int16_t*)take(cap * 2);
-  w.child_start = (int16_t*)take(cap * 2);
-  w.child_cnt = (int16_t*)take(cap * 2);
-  w.valid = (uint8_t*)take(cap);
+  w.rec = (NodeRec*)take((size_t)cap * 32);
+  w.val = (float2*)take((size_t)cap * 8);
+  w.token = (int32_t*)take((size_t)cap * 4);
+  w.path_pa = (float*)take((size_t)cap * 4);
+  w.uni = (float*)take((size_t)(2 * cap + 2) * 4);
+  w.sid = (int16_t*)take((size_t)cap * 2);
+  w.path = (int16_t*)take((size_t)cap * 2);
+  w.path_rmax = (int16_t*)take((size_t)cap * 2);
+  w.valid = (uint8_t*)take((size_t)cap);
   return w;
 }
 
@@ -268,29 +292,42 @@ __device__ void write_counts(const AcceptParams& p, int b, int n_out, int total,
   c[3] = node;
 }
 
-// Greedy walk (verify_tree_exact, verification.py:185-268), one thread.
-__device__ void walk_greedy(const AcceptParams& p, int b, int lo, const WalkSmem& w) {
+__device__ __forceinline__ float ratio_of(float mb, float ms) {
+  return ms > kEps32 ? __fdiv_rn(mb, ms) : 0.0f;
+}
+
+// First child of `node` whose token is `tok` (-1: none), by one warp.
+__device__ __forceinline__ int match_child(const WalkSmem& w, const NodeRec& r, int tok) {
+  const int lane = threadIdx.x & 31;
+  for (int base = 0; base < r.child_cnt; base += 32) {
+    const int k = base + lane;
+    const int c = k < r.child_cnt ? w.sid[r.child_start + k] : -1;
+    const unsigned m = __ballot_sync(0xffffffffu, c >= 0 && w.token[c] == tok);
+    if (m) return __shfl_sync(0xffffffffu, c, __ffs(m) - 1);
+  }
+  return -1;
+}
+
+// Greedy walk (verify_tree_exact, verification.py:185-268), by one warp.
+__device__ void walk_greedy_warp(const AcceptParams& p, int b, int lo, const WalkSmem& w) {
+  const int lane = threadIdx.x & 31;
   int32_t* ot = p.out_tokens + (int64_t)b * p.out_stride;
   int32_t* oh = p.out_hidden + (int64_t)b * p.out_stride;
   int cur = 0, total = 0, acc = 0, n_out = 0;
   int bonus = -1, last_tok = -1;
-  while (w.first_child[cur] >= 0) {                                   // :232
+  NodeRec r = w.rec[0];
+  while (r.child_cnt > 0) {                                           // :232
     total++;
-    if (!wait_row(p, lo + cur)) {
-      write_counts(p, b, -3, 0, 0, 0);
+    if (!wait_rows_warp(p, lo + cur)) {
+      if (lane == 0) write_counts(p, b, -3, 0, 0, 0);
       return;
     }
     const int tok = __ldcg(&p.row_ws[lo + cur].argmax);               // :73
-    int match = -1;
-    for (int c = w.first_child[cur]; c >= 0; c = w.next_sib[c])
-      if (w.token[c] == tok) {
-        match = c;
-        break;
-      }
+    const int match = match_child(w, r, tok);
     if (match >= 0) {                                                 // :237
       bonus = -1;
       acc++;
-      if (n_out < p.out_stride) {
+      if (lane == 0 && n_out < p.out_stride) {
         ot[n_out] = tok;
         oh[n_out] = cur;
       }
@@ -298,7 +335,8 @@ __device__ void walk_greedy(const AcceptParams& p, int b, int lo, const WalkSmem
       last_tok = tok;
       if (p.eos >= 0 && (int64_t)tok == p.eos) break;                 // :242
       cur = match;                                                    // :245
-      if (w.first_child[cur] < 0) break;                              // :249
+      r = w.rec[cur];
+      if (r.child_cnt == 0) break;                                    // :249
     } else {
       bonus = tok;
       break;
@@ -306,175 +344,23 @@ __device__ void walk_greedy(const AcceptParams& p, int b, int lo, const WalkSmem
   }
   if (n_out == 0 || p.eos < 0 || (int64_t)last_tok != p.eos) {        // :257
     if (bonus < 0) {
-      if (!wait_row(p, lo + cur)) {
-        write_counts(p, b, -3, 0, 0, 0);
+      if (!wait_rows_warp(p, lo + cur)) {
+        if (lane == 0) write_counts(p, b, -3, 0, 0, 0);
         return;
       }
       bonus = __ldcg(&p.row_ws[lo + cur].argmax);                     // :260-262
     }
-    if (n_out < p.out_stride) {
+    if (lane == 0 && n_out < p.out_stride) {
       ot[n_out] = bonus;
       oh[n_out] = cur;
     }
     n_out++;
   }
-  write_counts(p, b, n_out > p.out_stride ? -2 : n_out, total, acc, cur);
+  if (lane == 0) write_counts(p, b, n_out > p.out_stride ? -2 : n_out, total, acc, cur);
 }
 
-__device__ __forceinline__ float ratio_of(float mb, float ms) {
-  return ms > kEps32 ? __fdiv_rn(mb, ms) : 0.0f;
-}
-
-// Traversal verification (verify_tree_traversal, verification.py:377-524) by
-// one thread (its loop is a chain of dependent shared-memory accesses, which
-// lane-parallel versions only lengthen).  See the file comment for the lazily
-// evaluated p_alpha.
-__device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w) {
-  int accepted = 0;
-  int depth = 0;           // w.path[0..depth]: the current descent path
-  int draw = 0;
-  int T = 1;               // time stamp of the next direct p_alpha assignment
-  w.path[0] = 0;
-  w.path_pa[0] = w.rec[0].stored_pa;
-  w.path_rmax[0] = -1;
-  const int max_iter = 2 * n + 2;
-  for (int it = 0; it < max_iter; ++it) {                             // :377
-    const float eta = w.uni[draw++];                                  // :396, loaded ahead of the descent
-    // descend to the first valid leaf (:379-389), p_alpha evaluated lazily
-    int u = w.path[depth];
-    float pa_u = w.path_pa[depth];
-    int rmax_u = w.path_rmax[depth];
-    NodeRec ru = w.rec[u];
-    while (ru.first_valid >= 0) {
-      const int c = ru.first_valid;
-      const NodeRec rc = w.rec[c];
-      const int rmax = max(rmax_u, (int)ru.reset_t);
-      const float pa = rc.sticky_t > rmax ? rc.stored_pa : fminf(__fmul_rn(pa_u, ratio_of(w.mb[c], w.ms[c])), 1.0f);
-      ++depth;
-      w.path[depth] = (int16_t)c;
-      w.path_pa[depth] = pa;
-      w.path_rmax[depth] = (int16_t)rmax;
-      u = c;
-      ru = rc;
-      pa_u = pa;
-      rmax_u = rmax;
-    }
-    const int cand = u;
-    if (eta < pa_u) {                                                 // :395-400
-      accepted = cand;
-      break;
-    }
-    w.valid[cand] = 0;                                                // :403
-    const double old_ms_rej = (double)w.ms[cand];
-    const double old_mb_rej = (double)w.mb[cand];
-    w.ms[cand] = 0.0f;
-    const int parent = ru.parent;
-    if (parent < 0) {                                                 // :408
-      accepted = 0;
-      break;
-    }
-    --depth;                                                          // back to the parent
-    double S_out = 0.0;
-    const int c0 = w.child_start[parent], nc = w.child_cnt[parent];
-    const int fv_old = w.rec[parent].first_valid;
-    const float p_old32 = w.path_pa[depth];                           // :422
-    const double p_old = (double)p_old32;
-    float s_tree = 0.0f, sum_mb = 0.0f;                               // :429-433, left to right
-    double ms_denom = __dsub_rn(1.0, old_ms_rej);                     // :424
-    if (ms_denom < kEps) ms_denom = kEps;
-    if (nc <= kSibBatch) {
-      // the sibling group in registers: one round of independent loads
-      int cs[kSibBatch];
-      float mbs[kSibBatch], mss[kSibBatch];
-      bool vs[kSibBatch];
-#pragma unroll
-      for (int k = 0; k < kSibBatch; ++k) cs[k] = k < nc ? w.sib[c0 + k] : 0;
-#pragma unroll
-      for (int k = 0; k < kSibBatch; ++k) {
-        mbs[k] = k < nc ? w.mb[cs[k]] : 0.0f;
-        mss[k] = k < nc ? w.ms[cs[k]] : 0.0f;
-        vs[k] = k < nc && w.valid[cs[k]];
-      }
-      if (fv_old == cand) {
-        int next = -1;
-        bool after = false;
-#pragma unroll
-        for (int k = 0; k < kSibBatch; ++k) {
-          if (next < 0 && after && vs[k]) next = cs[k];
-          if (k < nc && cs[k] == cand) after = true;
-        }
-        w.rec[parent].first_valid = (int16_t)next;
-        if (next < 0) continue;                                       // :417 no active sibling
-      }
-#pragma unroll
-      for (int k = 0; k < kSibBatch; ++k) {
-        if (k < nc) {
-          s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbs[k]), mss[k]), 0.0f));
-          sum_mb = __fadd_rn(sum_mb, mbs[k]);
-        }
-      }
-      double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
-      if (S < kEps) S = kEps;                                         // :435
-      const float ms_denom32 = __double2float_rn(ms_denom);
-      const float S32 = __double2float_rn(S);
-#pragma unroll
-      for (int k = 0; k < kSibBatch; ++k) {                           // :443-448
-        if (vs[k]) {
-          const float ms_new = __fdiv_rn(mss[k], ms_denom32);
-          const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbs[k]), mss[k]), 0.0f), S32);
-          w.ms[cs[k]] = ms_new;
-          w.mb[cs[k]] = mb_new;
-        }
-      }
-      S_out = S;
-    } else {
-      if (fv_old == cand) {
-        int next = -1;
-        bool after = false;
-        for (int i = 0; i < nc; ++i) {
-          const int c = w.sib[c0 + i];
-          if (after && w.valid[c]) {
-            next = c;
-            break;
-          }
-          if (c == cand) after = true;
-        }
-        w.rec[parent].first_valid = (int16_t)next;
-        if (next < 0) continue;                                       // :417 no active sibling
-      }
-      for (int i = 0; i < nc; ++i) {
-        const int c = w.sib[c0 + i];
-        const float mbv = w.mb[c];
-        s_tree = __fadd_rn(s_tree, fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), w.ms[c]), 0.0f));
-        sum_mb = __fadd_rn(sum_mb, mbv);
-      }
-      double S = __dadd_rn((double)s_tree, __dmul_rn(p_old, __dsub_rn(1.0, (double)sum_mb)));
-      if (S < kEps) S = kEps;                                         // :435
-      const float ms_denom32 = __double2float_rn(ms_denom);
-      const float S32 = __double2float_rn(S);
-      for (int i = 0; i < nc; ++i) {                                  // :443-448
-        const int c = w.sib[c0 + i];
-        if (!w.valid[c]) continue;
-        const float msv = w.ms[c], mbv = w.mb[c];
-        const float ms_new = __fdiv_rn(msv, ms_denom32);
-        const float mb_new = __fdiv_rn(fmaxf(__fsub_rn(__fmul_rn(p_old32, mbv), msv), 0.0f), S32);
-        w.ms[c] = ms_new;
-        w.mb[c] = mb_new;
-      }
-      S_out = S;
-    }
-    const double S = S_out;
-    const double p_new = __ddiv_rn(S, __dsub_rn(__dadd_rn(S, 1.0), p_old));                   // :439
-    const double mb_rej = __ddiv_rn(fmax(__dsub_rn(__dmul_rn(p_old, old_mb_rej), old_ms_rej), 0.0), S);   // :451
-    w.mb[cand] = __double2float_rn(mb_rej);                           // :452
-    const float p_new32 = __double2float_rn(p_new);                   // :440, direct assignment
-    w.rec[parent].stored_pa = p_new32;
-    w.rec[parent].sticky_t = (int16_t)T;
-    w.rec[parent].reset_t = (int16_t)T;
-    w.path_pa[depth] = p_new32;
-    ++T;
-  }
-  // :480-524 output
+// Output of a traversal walk (verification.py:480-524), by one thread.
+__device__ void traversal_output(const AcceptParams& p, int b, int lo, int accepted, const WalkSmem& w) {
   int d = 0;
   for (int c = accepted; c >= 0; c = w.rec[c].parent) w.path[d++] = (int16_t)c;   // reversed path
   int32_t* ot = p.out_tokens + (int64_t)b * p.out_stride;
@@ -507,8 +393,196 @@ __device__ void walk_traversal(const AcceptParams& p, int b, int lo, int n, cons
   write_counts(p, b, n_out > p.out_stride ? -2 : n_out, n_out, n_out > 0 ? n_out - 1 : 0, accepted);
 }
 
-// Thread groups that run a tree walk: the whole CTA (streaming kernel for
-// unaligned rows) or one warp (walker warp of the persistent kernel).
+// Traversal verification (verify_tree_traversal, verification.py:377-524) by
+// one warp.  The loop is sequential (each iteration depends on the last), so
+// the warp keeps its dependent chain short: every lane computes the same
+// control values (lane 0 alone stores the shared ones: stores of one
+// sub-word location by all 32 lanes measured up to 8x slower), a descent
+// step is one record load and a multiply
+// (Mb/Ms is kept current per node), the rejected node's sibling group is one
+// run of slots spread over the lanes, its fp32 sums are taken left to right
+// from shuffles issued eight at a time, the siblings' fp32 divisions run in
+// parallel lanes, and p_new and the rejected node's Mb share one fp64
+// division (lanes 0 and 1).  Fp32 tensor and fp64 scalar operations are
+// replayed with explicitly rounded operations in the reference's order.  See
+// the file comment for the lazily evaluated p_alpha.
+__device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w) {
+  const int lane = threadIdx.x & 31;
+  constexpr unsigned kFull = 0xffffffffu;
+  int accepted = 0;
+  int depth = 0;           // w.path[0..depth]: the current descent path
+  int draw = 0;
+  int T = 1;               // time stamp of the next direct p_alpha assignment
+  int u = 0;               // the node the next descent starts from (w.path[depth])
+  if (lane == 0) {
+    w.path[0] = 0;
+    w.path_pa[0] = w.rec[0].stored_pa;
+    w.path_rmax[0] = -1;
+  }
+  const int max_iter = 2 * n + 2;
+  for (int it = 0; it < max_iter; ++it) {                             // :377
+    __syncwarp();
+    const float eta = w.uni[draw++];                                  // :396, drawn once per iteration
+    // descend to the first valid leaf (:379-389), p_alpha evaluated lazily
+    NodeRec ru = w.rec[u];
+    float pa_u = w.path_pa[depth];
+    int rmax_u = w.path_rmax[depth];
+    while (ru.first_valid >= 0) {
+      const int c = ru.first_valid;
+      const NodeRec rc = w.rec[c];
+      const int rmax = max(rmax_u, (int)ru.reset_t);
+      const float pa = rc.sticky_t > rmax ? rc.stored_pa : fminf(__fmul_rn(pa_u, rc.ratio), 1.0f);
+      ++depth;
+      if (lane == 0) {
+        w.path[depth] = (int16_t)c;
+        w.path_pa[depth] = pa;
+        w.path_rmax[depth] = (int16_t)rmax;
+      }
+      u = c;
+      ru = rc;
+      pa_u = pa;
+      rmax_u = rmax;
+    }
+    const int cand = u;
+    if (eta < pa_u) {                                                 // :395-400
+      accepted = cand;
+      break;
+    }
+    const int parent = ru.parent;
+    if (parent < 0) {                                                 // :408
+      accepted = 0;
+      break;
+    }
+    --depth;                                                          // back to the parent
+    u = parent;
+    const int s0 = ru.sib_start, nc = ru.sib_cnt, cslot = ru.slot;
+    __syncwarp();                                                     // lane 0's path entries
+    const float p_old32 = w.path_pa[depth];                           // :422
+    const float2 cv = w.val[cslot];
+    const float old_mb32 = cv.x, old_ms32 = cv.y;
+    double q;
+    // the parent's children left to right (:429-433): the rejected node counts
+    // with Ms = 0 (:404) and is no longer valid; it was the parent's first
+    // valid child, so the lowest valid slot after it is the new first one
+    if (nc <= 32) {
+      const int sl = s0 + lane;
+      const bool has = lane < nc;
+      const float2 v = has ? w.val[sl] : make_float2(0.0f, 0.0f);
+      const int ck = has ? w.sid[sl] : 0;
+      const bool vk = has && sl != cslot && w.valid[sl];
+      const unsigned vm = __ballot_sync(kFull, vk);
+      const int next = vm ? __shfl_sync(kFull, ck, __ffs(vm) - 1) : -1;
+      if (lane == 0) {
+        w.valid[cslot] = 0;                                           // :403
+        w.val[cslot].y = 0.0f;                                        // :404
+        w.rec[parent].first_valid = (int16_t)next;
+      }
+      if (vm == 0u) continue;                                         // :417 no active sibling
+      const float mbk = v.x, msk = sl == cslot ? 0.0f : v.y;
+      const float tk = has ? fmaxf(__fsub_rn(__fmul_rn(p_old32, mbk), msk), 0.0f) : 0.0f;
+      // left-to-right fp32 sums; terms past the group add +0.0, which leaves
+      // these non-negative sums unchanged
+      float s_tree = 0.0f, sum_mb = 0.0f;
+      for (int j0 = 0; j0 < nc; j0 += 8) {
+        float a[8], m[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          a[q] = __shfl_sync(kFull, tk, (j0 + q) & 31);
+          m[q] = __shfl_sync(kFull, mbk, (j0 + q) & 31);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const bool in = j0 + q < nc;
+          s_tree = __fadd_rn(s_tree, in ? a[q] : 0.0f);
+          sum_mb = __fadd_rn(sum_mb, in ? m[q] : 0.0f);
+        }
+      }
+      double S = __dadd_rn((double)s_tree, __dmul_rn((double)p_old32, __dsub_rn(1.0, (double)sum_mb)));
+      if (S < kEps) S = kEps;                                         // :435
+      double ms_denom = __dsub_rn(1.0, (double)old_ms32);             // :424
+      if (ms_denom < kEps) ms_denom = kEps;
+      const float ms_denom32 = __double2float_rn(ms_denom);
+      const float S32 = __double2float_rn(S);
+      // lane 1: the rejected node's Mb (:451); every other lane: p_new (:439)
+      const double p_old = (double)p_old32;
+      const double num = lane == 1 ? fmax(__dsub_rn(__dmul_rn(p_old, (double)old_mb32), (double)old_ms32), 0.0) : S;
+      const double den = lane == 1 ? S : __dsub_rn(__dadd_rn(S, 1.0), p_old);
+      q = __ddiv_rn(num, den);
+      // every lane divides (no divergent branch); valid siblings store (:443-448)
+      const float ms_new = __fdiv_rn(msk, ms_denom32);
+      const float mb_new = __fdiv_rn(tk, S32);
+      const float ratio = __fdiv_rn(mb_new, ms_new > kEps32 ? ms_new : 1.0f);
+      if (vk) {
+        w.val[sl] = make_float2(mb_new, ms_new);
+        w.rec[ck].ratio = ms_new > kEps32 ? ratio : 0.0f;
+      }
+    } else {
+      float s_tree = 0.0f, sum_mb = 0.0f;
+      int next = -1;
+      for (int base = 0; base < nc; base += 32) {
+        const int k = base + lane;
+        const bool has = k < nc;
+        const int sl = s0 + k;
+        const float2 v = has ? w.val[sl] : make_float2(0.0f, 0.0f);
+        const int ck = has ? w.sid[sl] : 0;
+        const bool vk = has && sl != cslot && w.valid[sl];
+        const float mbk = v.x, msk = sl == cslot ? 0.0f : v.y;
+        const float tk = has ? fmaxf(__fsub_rn(__fmul_rn(p_old32, mbk), msk), 0.0f) : 0.0f;
+        const int cnt = min(32, nc - base);
+        for (int j = 0; j < cnt; ++j) {
+          s_tree = __fadd_rn(s_tree, __shfl_sync(kFull, tk, j));
+          sum_mb = __fadd_rn(sum_mb, __shfl_sync(kFull, mbk, j));
+        }
+        const unsigned vm = __ballot_sync(kFull, vk);
+        if (next < 0 && vm) next = __shfl_sync(kFull, ck, __ffs(vm) - 1);
+      }
+      if (lane == 0) {
+        w.valid[cslot] = 0;                                           // :403
+        w.val[cslot].y = 0.0f;                                        // :404
+        w.rec[parent].first_valid = (int16_t)next;
+      }
+      if (next < 0) continue;                                         // :417 no active sibling
+      double S = __dadd_rn((double)s_tree, __dmul_rn((double)p_old32, __dsub_rn(1.0, (double)sum_mb)));
+      if (S < kEps) S = kEps;                                         // :435
+      double ms_denom = __dsub_rn(1.0, (double)old_ms32);             // :424
+      if (ms_denom < kEps) ms_denom = kEps;
+      const float ms_denom32 = __double2float_rn(ms_denom);
+      const float S32 = __double2float_rn(S);
+      const double p_old = (double)p_old32;
+      const double num = lane == 1 ? fmax(__dsub_rn(__dmul_rn(p_old, (double)old_mb32), (double)old_ms32), 0.0) : S;
+      const double den = lane == 1 ? S : __dsub_rn(__dadd_rn(S, 1.0), p_old);
+      q = __ddiv_rn(num, den);
+      __syncwarp();
+      for (int base = 0; base < nc; base += 32) {
+        const int sl = s0 + base + lane;
+        if (base + lane >= nc || sl == cslot || !w.valid[sl]) continue;
+        const float2 v = w.val[sl];
+        const float t = fmaxf(__fsub_rn(__fmul_rn(p_old32, v.x), v.y), 0.0f);
+        const float ms_new = __fdiv_rn(v.y, ms_denom32);
+        const float mb_new = __fdiv_rn(t, S32);
+        w.val[sl] = make_float2(mb_new, ms_new);
+        w.rec[w.sid[sl]].ratio = ratio_of(mb_new, ms_new);
+      }
+    }
+    const float p_new32 = __double2float_rn(__shfl_sync(kFull, q, 0));       // :440, direct assignment
+    const float mb_rej32 = __double2float_rn(__shfl_sync(kFull, q, 1));      // :452
+    if (lane == 0) {
+      w.val[cslot].x = mb_rej32;
+      w.rec[parent].stored_pa = p_new32;
+      w.rec[parent].sticky_t = (int16_t)T;
+      w.rec[parent].reset_t = (int16_t)T;
+      w.path_pa[depth] = p_new32;
+    }
+    ++T;
+  }
+  __syncwarp();
+  if (lane == 0) traversal_output(p, b, lo, accepted, w);
+  __syncwarp();
+}
+
+// Thread groups that run the set-up of a tree walk: the whole CTA (streaming
+// kernel for unaligned rows) or one warp (walker warp of the persistent
+// kernel).  The walk itself always runs on the group's first warp.
 struct CtaGroup {
   __device__ int rank() const { return threadIdx.x; }
   __device__ int size() const { return kThreads; }
@@ -525,149 +599,131 @@ struct WarpGroup {
   }
 };
 
-// Load request b's tree (rows lo .. lo+n-1), the target probability of every
-// node's token under its parent's row and the traversal uniforms, build the
-// child lists, then walk (greedy or traversal) on the group's first thread.
+// Load request b's tree (rows lo .. lo+n-1) and the traversal uniforms, build
+// the child runs (a stable counting sort of the nodes by parent), then
+// (traversal) wait for the parents' rows and compute the target probability
+// of every node's token under its parent's row, and walk.  Work that needs no
+// row statistics comes first, so it overlaps the streaming.
 template <class G>
 __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
   if (n <= 0 || n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
   }
-  constexpr int kOwn = 8;                                  // nodes per thread per pass
-  int bad = 0, late = 0;
-  for (int pass = 0; pass * kOwn * g.size() < n; ++pass) {
-    // every global load of a pass is issued before any result is used
-    int par[kOwn], tok[kOwn];
-    float msv[kOwn], pm[kOwn], ps[kOwn], x[kOwn];
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int i = (pass * kOwn + t) * g.size() + g.rank();
-      par[t] = i < n ? p.parents[lo + i] : -1;
-      tok[t] = i < n ? p.tokens[lo + i] : -1;
-      msv[t] = (p.traversal && i > 0 && i < n) ? p.draft_probs[lo + i] : 1.0f;           // :353
-    }
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int i = (pass * kOwn + t) * g.size() + g.rank();
-      bool use = p.traversal && i > 0 && i < n && par[t] >= 0 && par[t] < i;
-      if (use && !wait_row(p, lo + par[t])) {                  // parents' rows stream first
-        late = 1;
-        use = false;
-      }
-      pm[t] = use ? __ldcg(&p.row_ws[lo + par[t]].m) : 0.0f;
-      ps[t] = use ? __ldcg(&p.row_ws[lo + par[t]].s) : 1.0f;
-      x[t] = (use && tok[t] >= 0 && tok[t] < p.vocab)
-                 ? load_scaled(p, p.logits + (int64_t)(lo + par[t]) * p.row_stride, tok[t])
-                 : -INFINITY;
-    }
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int i = (pass * kOwn + t) * g.size() + g.rank();
-      if (i >= n) continue;
-      if ((i == 0 && par[t] != -1) || (i > 0 && (par[t] < 0 || par[t] >= i))) bad = 1;
-      NodeRec r;
-      r.first_valid = -1;
-      r.sticky_t = i == 0 ? 0 : -1;
-      r.reset_t = -1;
-      r.parent = (int16_t)par[t];
-      r.stored_pa = 1.0f;
-      r.pad = 0;
-      w.token[i] = tok[t];
-      w.valid[i] = 1;
-      if (p.traversal) {
-        const float mb = i == 0 ? 1.0f : (par[t] >= 0 && par[t] < i ? prob_bf16(x[t], pm[t], ps[t]) : 0.0f);   // :349
-        w.mb[i] = mb;
-        w.ms[i] = msv[t];
-      }
-      w.rec[i] = r;
-    }
+  int* cnt = reinterpret_cast<int*>(w.val);               // child counts, then slot bases
+  int* basep = cnt + ((n + 1) & ~1);
+  for (int i = g.rank(); i < n; i += g.size()) cnt[i] = 0;
+  g.sync();
+  int bad = 0;
+  for (int i = g.rank(); i < n; i += g.size()) {
+    const int par = p.parents[lo + i];
+    const int tok = p.tokens[lo + i];
+    const float ms = (p.traversal && i > 0) ? p.draft_probs[lo + i] : 1.0f;   // :353
+    if ((i == 0 && par != -1) || (i > 0 && (par < 0 || par >= i))) bad = 1;
+    NodeRec r;
+    r.first_valid = -1;
+    r.sticky_t = i == 0 ? 0 : -1;
+    r.reset_t = -1;
+    r.parent = (int16_t)par;
+    r.stored_pa = 1.0f;
+    r.ratio = 0.0f;
+    r.slot = r.sib_start = r.sib_cnt = r.child_start = r.child_cnt = 0;
+    r.pad[0] = r.pad[1] = r.pad[2] = 0;
+    w.rec[i] = r;
+    w.token[i] = tok;
+    w.path_pa[i] = ms;
+    if (i > 0 && par >= 0 && par < i) atomicAdd(&cnt[par], 1);
   }
   if (p.traversal)
     for (int k = g.rank(); k < 2 * n + 2; k += g.size())
       w.uni[k] = philox_uniform(p.seed, p.offset, (uint32_t)b, (uint32_t)k);
   bad = g.any(bad != 0, red_sm);
-  late = g.any(late != 0, red_sm);
   g.sync();
-  if (bad || late) {
-    if (g.rank() == 0) write_counts(p, b, bad ? -1 : -3, 0, 0, 0);
+  if (bad) {
+    if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     return;
   }
-  // children in ascending node order: counts and sibling ranks from one pass
-  // over the parents (read by every thread at once), then CSR and linked lists
-  if (n <= kOwn * g.size()) {
-    int cnt[kOwn], rnk[kOwn], px[kOwn];
+  if (g.rank() < 32) {
+    // child runs: exclusive scan of the counts, then a stable scatter of the
+    // nodes in ascending order (ranks within a chunk of 32 from match_any)
+    const int lane = g.rank();
+    int carry = 0;
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      const int c = i < n ? cnt[i] : 0;
+      int incl = c;
 #pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int xi = t * g.size() + g.rank();
-      cnt[t] = 0;
-      rnk[t] = 0;
-      px[t] = xi < n ? w.rec[xi].parent : -2;
-    }
-    const int own = (n + g.size() - 1) / g.size();           // <= kOwn
-    for (int j = 0; j < n; ++j) {
-      const int pj = w.rec[j].parent;
-#pragma unroll
-      for (int t = 0; t < kOwn; ++t) {
-        if (t >= own) break;
-        const int xi = t * g.size() + g.rank();
-        cnt[t] += (pj == xi) ? 1 : 0;
-        rnk[t] += (j < xi && pj == px[t]) ? 1 : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
-    }
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int xi = t * g.size() + g.rank();
-      if (xi < n) w.child_cnt[xi] = (int16_t)cnt[t];
-    }
-    g.sync();
-    if (g.rank() == 0) {
-      int o = 0;
-      for (int i = 0; i < n; ++i) {
-        w.child_start[i] = (int16_t)o;
-        o += w.child_cnt[i];
+      if (i < n) {
+        basep[i] = carry + incl - c;
+        w.rec[i].child_start = (int16_t)(carry + incl - c);
+        w.rec[i].child_cnt = (int16_t)c;
       }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    g.sync();
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int xi = t * g.size() + g.rank();
-      if (xi >= 1 && xi < n) w.sib[w.child_start[px[t]] + rnk[t]] = (int16_t)xi;
-    }
-    g.sync();
-#pragma unroll
-    for (int t = 0; t < kOwn; ++t) {
-      const int xi = t * g.size() + g.rank();
-      if (xi >= n) continue;
-      const int fc = cnt[t] > 0 ? w.sib[w.child_start[xi]] : -1;
-      w.first_child[xi] = (int16_t)fc;
-      w.rec[xi].first_valid = (int16_t)fc;
-      w.next_sib[xi] = (xi >= 1 && rnk[t] + 1 < w.child_cnt[px[t]]) ? w.sib[w.child_start[px[t]] + rnk[t] + 1] : -1;
-    }
-    g.sync();
-  } else if (g.rank() == 0) {
-    for (int i = 0; i < n; ++i) {
-      w.first_child[i] = -1;
-      w.child_cnt[i] = 0;
-    }
-    for (int i = n - 1; i >= 1; --i) {
-      const int par = w.rec[i].parent;
-      w.next_sib[i] = w.first_child[par];
-      w.first_child[par] = (int16_t)i;
-      w.child_cnt[par]++;
-    }
-    w.next_sib[0] = -1;
-    int o = 0;
-    for (int i = 0; i < n; ++i) {
-      w.child_start[i] = (int16_t)o;
-      for (int c = w.first_child[i]; c >= 0; c = w.next_sib[c]) w.sib[o++] = (int16_t)c;
-      w.rec[i].first_valid = w.first_child[i];
+    __syncwarp();
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      const int par = (i >= 1 && i < n) ? (int)w.rec[i].parent : -2 - lane;    // unique key when unused
+      const unsigned same = __match_any_sync(0xffffffffu, par);
+      const int rank = __popc(same & ((1u << lane) - 1u));
+      int slot = n - 1;                                    // the root's slot
+      if (i >= 1 && i < n) slot = basep[par] + rank;
+      __syncwarp();
+      if (i >= 1 && i < n && (same >> lane) == 1u) basep[par] += __popc(same);   // the group's last lane
+      if (i < n) {
+        w.sid[slot] = (int16_t)i;
+        w.rec[i].slot = (int16_t)slot;
+      }
+      __syncwarp();
     }
   }
   g.sync();
-  if (g.rank() == 0) {
-    if (p.traversal) walk_traversal(p, b, lo, n, w);
-    else walk_greedy(p, b, lo, w);
+  for (int i = g.rank(); i < n; i += g.size()) {
+    const NodeRec r = w.rec[i];
+    w.rec[i].first_valid = r.child_cnt > 0 ? w.sid[r.child_start] : (int16_t)-1;
+    w.rec[i].sib_start = i == 0 ? r.slot : w.rec[r.parent].child_start;
+    w.rec[i].sib_cnt = i == 0 ? (int16_t)1 : w.rec[r.parent].child_cnt;
+  }
+  g.sync();                                                // every count and base read: the values may go in
+  for (int i = g.rank(); i < n; i += g.size()) {
+    const int sl = w.rec[i].slot;
+    w.val[sl] = make_float2(1.0f, w.path_pa[i]);           // root: Mb = Ms = 1 (:344-345)
+    w.valid[sl] = 1;
+  }
+  g.sync();
+  if (p.traversal) {
+    // Mb[i] = p[parent(i), token(i)] (:349) once the parent's row is published
+    // (the warps wait with warp-uniform loops and stay converged)
+    int late = 0;
+    for (int i0 = 1 + (g.rank() & ~31); i0 < n; i0 += g.size()) {
+      const int i = i0 + (g.rank() & 31);
+      const NodeRec r = w.rec[i < n ? i : 0];
+      const int pr = lo + r.parent;
+      if (!wait_rows_warp(p, i < n ? pr : -1)) {
+        late = 1;
+        break;
+      }
+      if (i >= n) continue;
+      const float pm = __ldcg(&p.row_ws[pr].m), ps = __ldcg(&p.row_ws[pr].s);
+      const int tk = w.token[i];
+      const float x = (tk >= 0 && tk < p.vocab) ? load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk) : -INFINITY;
+      const float mb = prob_bf16(x, pm, ps);
+      w.val[r.slot].x = mb;
+      w.rec[i].ratio = ratio_of(mb, w.val[r.slot].y);
+    }
+    late = g.any(late != 0, red_sm);
+    g.sync();
+    if (late) {
+      if (g.rank() == 0) write_counts(p, b, -3, 0, 0, 0);
+      return;
+    }
+    if (g.rank() < 32) walk_traversal_warp(p, b, lo, n, w);
+  } else if (g.rank() < 32) {
+    walk_greedy_warp(p, b, lo, w);
   }
   g.sync();
 }
