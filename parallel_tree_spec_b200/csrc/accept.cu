@@ -176,6 +176,10 @@ __device__ __forceinline__ uint32_t scale_pair(uint32_t v, float inv_t) {
   return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
 }
 
+// Index of a partial whose max was not located (its warp skipped values below
+// a larger one found elsewhere): it never wins a tie of the final max.
+constexpr int kNotCandidate = INT_MAX - 1;
+
 // (max, sum of exp(x - max), first index of max) partials.
 struct __align__(16) Part {
   double s;
@@ -917,6 +921,7 @@ struct __align__(16) StreamCtl {
   uint64_t empty[kSSlots];
   uint64_t seg_full[2];       // 16 consumer warps wrote their partials of a segment
   uint64_t seg_empty[2];      // the merger has read them
+  unsigned long long seg_max; // (segment + 1) << 32 | key of the largest value any warp located in it
   Part seg[2][kSConsumerWarps];
 };
 
@@ -959,11 +964,17 @@ struct StreamPlan {
   }
 };
 
+// Requests whose row_indptr the prologue copies into shared memory (larger
+// batches search it in global memory).
+constexpr int kSmemIndptr = 4096;
+
 // Shared-memory bytes of the stream-order tables (internal-row bit mask, the
-// CTA's whole rows, the split rows, scan scratch), placed after the walk state.
-__host__ __device__ inline size_t order_smem_bytes(const StreamPlan& pl) {
+// CTA's whole rows, the split rows, scan scratch, a copy of row_indptr),
+// placed after the walk state.
+__host__ __device__ inline size_t order_smem_bytes(const StreamPlan& pl, int batch) {
   return (size_t)pl.mask_words * 4 + (((size_t)pl.whole_rows_per_cta * 2 + 15) & ~(size_t)15) +
-         (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4;
+         (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4 +
+         (batch < kSmemIndptr ? (size_t)(batch + 1) * 4 : 0);
 }
 
 // First row of the request that holds `row` (binary search over row_indptr).
@@ -971,11 +982,20 @@ __device__ __forceinline__ int request_first_row(const int32_t* indptr, int batc
   int lo = 0, hi = batch - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(indptr + mid) <= row) lo = mid;
+    if (indptr[mid] <= row) lo = mid;
     else hi = mid - 1;
   }
-  return __ldg(indptr + lo);
+  return indptr[lo];
 }
+
+// Order-preserving integer key of a float (for the single-instruction warp
+// max reduction): non-negative values keep their bits, negative ones flip the
+// magnitude bits.  key_float inverts it.
+__device__ __forceinline__ int float_key(float x) {
+  const int b = __float_as_int(x);
+  return b >= 0 ? b : (b ^ 0x7fffffff);
+}
+__device__ __forceinline__ float key_float(int k) { return __int_as_float(k >= 0 ? k : (k ^ 0x7fffffff)); }
 
 __device__ __forceinline__ uint64_t f2(float a, float b) {
   uint64_t r;
@@ -1095,6 +1115,10 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   uint16_t* mine = reinterpret_cast<uint16_t*>(otab + (size_t)plan.mask_words * 4);
   uint16_t* split = mine + ((plan.whole_rows_per_cta + 7) & ~7);
   int* scan = reinterpret_cast<int*>(split + ((plan.num_rows - plan.split_first_row + 7) & ~7));
+  int* sindptr = scan + 32;
+  const int32_t* indptr = p.batch < kSmemIndptr ? sindptr : p.row_indptr;
+  if (p.batch < kSmemIndptr)
+    for (int i = tid; i <= p.batch; i += kSThreads) sindptr[i] = p.row_indptr[i];
 
   if (tid == 0) {
     for (int i = 0; i < kSSlots; ++i) {
@@ -1105,13 +1129,14 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       s_mbar_init(&ctl.seg_full[i], kSConsumerWarps);
       s_mbar_init(&ctl.seg_empty[i], 1);
     }
+    ctl.seg_max = 0ull;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // ---- stream order (every CTA computes it for its own rows) ---------------
   for (int i = tid; i < plan.mask_words; i += kSThreads) imask[i] = 0u;
   __syncthreads();
   for (int j = tid; j < plan.num_rows; j += kSThreads) {
-    const int lo = request_first_row(p.row_indptr, p.batch, j);
+    const int lo = request_first_row(indptr, p.batch, j);
     const int pj = p.parents[j];
     const int r = (j == lo) ? j : ((pj >= 0 && pj < j - lo) ? lo + pj : -1);
     if (r >= 0) atomicOr(&imask[r >> 5], 1u << (r & 31));
@@ -1241,11 +1266,15 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
         }
       }
       // the first index of the warp's max changes only when some lane raises it
-      // (an equal max keeps the earlier, smaller index)
-      if (__any_sync(0xffffffffu, mt > w_m)) {
-        float wm = mt;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+      // (an equal max keeps the earlier, smaller index); a value below the
+      // largest one another warp has located in this segment cannot be the
+      // segment's max, so the warp skips it (the warp that holds the max
+      // always locates it: the shared value never exceeds it)
+      const unsigned long long cm = *reinterpret_cast<volatile unsigned long long*>(&ctl.seg_max);
+      const float cmax = (unsigned)(cm >> 32) == (unsigned)(seg + 1) ? key_float((int)((unsigned)cm ^ 0x80000000u))
+                                                                      : -INFINITY;
+      if (__any_sync(0xffffffffu, mt > w_m && mt >= cmax)) {
+        const float wm = key_float(__reduce_max_sync(0xffffffffu, float_key(mt)));
         // branchless scan from the last value to the first: the smallest index
         // holding wm wins (padding is -inf and never equals the finite wm)
         int fi = INT_MAX;
@@ -1259,20 +1288,22 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
             fi = (__uint_as_float(u << 16) == wm) ? e : fi;
           }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) fi = min(fi, __shfl_xor_sync(0xffffffffu, fi, o));
         w_m = wm;
-        w_idx = fi;
+        w_idx = (int)__reduce_min_sync(0xffffffffu, (unsigned)fi);
+        if (lane == 0)
+          atomicMax(&ctl.seg_max, ((unsigned long long)(unsigned)(seg + 1) << 32) | ((unsigned)float_key(wm) ^ 0x80000000u));
       }
       if (seg_end) {
-        // the warp's partial of the segment: sums relative to the warp max
-        double ws = (m_t == -INFINITY) ? 0.0 : s_t * (double)ex2_approx((m_t - w_m) * kLog2e);
+        // the warp's partial of the segment: sums relative to the warp max; the
+        // index is a candidate only if the warp located that max
+        const float wmax = key_float(__reduce_max_sync(0xffffffffu, float_key(m_t)));
+        double ws = (m_t == -INFINITY) ? 0.0 : s_t * (double)ex2_approx((m_t - wmax) * kLog2e);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
         const int buf = seg & 1;
         if (!s_mbar_wait(&ctl.seg_empty[buf], ((seg >> 1) + 1) & 1, 0)) break;
         if (lane == 0) {
-          ctl.seg[buf][cw] = (w_idx == INT_MAX) ? kNone : Part{ws, w_m, w_idx};
+          ctl.seg[buf][cw] = (wmax == -INFINITY) ? kNone : Part{ws, wmax, w_m == wmax ? w_idx : kNotCandidate};
           s_mbar_arrive(&ctl.seg_full[buf]);
         }
         __syncwarp();
@@ -1415,7 +1446,8 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
     plan.split_items = (p.num_rows - plan.split_first_row) * nchunks;
     plan.num_rows = p.num_rows;
     plan.mask_words = (p.num_rows + 31) / 32;
-    const size_t ssmem = ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan);
+    const size_t ssmem =
+        ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan, p.batch);
     if (ssmem <= kMaxDynSmem) {
       static size_t ssmem_attr[256] = {};
       if (ssmem > ssmem_attr[dev]) {
