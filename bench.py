@@ -65,6 +65,9 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
                     help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor-parallel step (70B-shaped target: 64 query / 8 KV heads split over the ranks, "
+                         "vocabulary split over the ranks, batch 64, prefixes U[512, 8192]); run under torchrun")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
 
@@ -497,10 +500,154 @@ def run_e2e(a, W, step, device):
     return {"value": a.e2e_steps / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
+# ---------------------------------------------------------------- tensor-parallel step
+def run_tp(a):
+    """Tensor-parallel verification step of a 70B-shaped target: every rank
+    holds 8/N of the 8 KV heads (64/N query heads) and 1/N of the vocabulary;
+    attention is local, acceptance exchanges per-row partials and tie indices
+    over NCCL, and every rank walks the same trees.  Batch 64, prefixes drawn
+    uniformly from [512, 8192], 65-row trees, random N(0, 3) logits (no
+    planting: nearly every node is rejected, the longest walks)."""
+    import torch
+    import torch.distributed as dist
+    from parallel_tree_spec_b200 import _lib, kernels as K
+    from parallel_tree_spec_b200 import workload as wl
+    from parallel_tree_spec_b200._lib import check
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if 8 % world:
+        raise ValueError("--tp needs 1, 2, 4 or 8 ranks")
+    L = _lib.lib()
+    B, V, D, pl = 64, a.vocab, 128, 16
+    hq, hkv = 64 // world, 8 // world
+    rng = np.random.default_rng(a.seed + 7)                       # the same on every rank
+    trees = [wl.make_tree(rng, 8, 8, V) for _ in range(B)]
+    n = trees[0].size
+    prefix = rng.integers(512, 8193, size=B)
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    kv_lens = prefix + n
+    npg = (kv_lens + pl - 1) // pl
+    page_indptr = np.concatenate([[0], np.cumsum(npg)]).astype(np.int32)
+    max_pages = int(page_indptr[-1]) + 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 100 + rank)
+    layer = torch.empty(max_pages, 2, pl, hkv, D, dtype=torch.bfloat16, device=dev).normal_(0, 1 / math.sqrt(D),
+                                                                                          generator=g)
+    perm = torch.randperm(max_pages, generator=g, device=dev)[: page_indptr[-1]].to(torch.int32)
+    T = B * n
+    q = torch.randn(T, hq, D, generator=g, device=dev).to(torch.bfloat16)
+    kn = (torch.randn(T, hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    vn = (torch.randn(T, hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    step_v = V // world
+    v0, v1 = rank * step_v, (V if rank == world - 1 else (rank + 1) * step_v)
+    xs = (torch.randn(T, v1 - v0, generator=g, device=dev) * 3.0).to(torch.bfloat16)
+    d = lambda x: torch.as_tensor(np.ascontiguousarray(x), dtype=torch.int32, device=dev)
+    qo, parents, tokens = d(indptr), d(par), d(tok)
+    draft = torch.as_tensor(dp, device=dev)
+    pind, lastp, seqlens, offs = d(page_indptr), d((kv_lens - 1) % pl + 1), d(kv_lens), d(prefix)
+    mw = K.mask_words_for(n)
+    bits = torch.empty(T, mw, dtype=torch.int64, device=dev)
+    bi = torch.empty(T, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    attn_ws = K.workspace(dev, "attn", 256)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    pool = layer.view(1, *layer.shape)
+
+    def gather(t):
+        if world == 1:
+            return t.unsqueeze(0)
+        o = torch.empty(world, *t.shape, dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(o, t)
+        return o
+
+    res = {}
+
+    def one(ev=None):
+        check(L.pts_tree_mask_from_parents(parents.data_ptr(), qo.data_ptr(), B, T, mw, bits.data_ptr(), s), "mask")
+        check(L.pts_batch_positions(qo.data_ptr(), seqlens.data_ptr(), B, T, bi.data_ptr(), pos.data_ptr(), s), "pos")
+        check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), hkv * D, hkv * D, layer.data_ptr(), bi.data_ptr(),
+                              pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, hkv, D, pl, max_pages, 2, s), "app")
+        if ev is not None:
+            ev[0].record()
+        check(L.pts_tree_attn_run(q.data_ptr(), layer.data_ptr(), qo.data_ptr(), pind.data_ptr(), perm.data_ptr(),
+                                  lastp.data_ptr(), bits.data_ptr(), mw, out.data_ptr(), B, T, n, int(kv_lens.max()),
+                                  hq, hkv, D, pl, max_pages, 1 / math.sqrt(D), attn_ws.data_ptr(), attn_ws.numel(),
+                                  s), "attention")
+        if ev is not None:
+            ev[1].record()
+        parts, tk = K.accept_shard_partials(xs, v0, qo, parents, tokens)
+        stats, tkm = K.accept_merge_shards(gather(parts), gather(tk))
+        ties = gather(K.accept_shard_ties(xs, v0, stats))
+        ot, oh, oc = K.accept_walk_merged(stats, tkm, ties, V, qo, parents, tokens, draft, seed=5, offset=0,
+                                          max_nodes=n)
+        if ev is not None:
+            ev[2].record()
+        K.kv_compact(pool, pind, perm, oh, oc, offs)
+        res["oc"] = oc
+
+    for _ in range(max(3, a.warmup)):
+        one()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local).start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start.record()
+    for i in range(a.steps):
+        one(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    sampler.stop()
+    el = start.elapsed_time(end)
+    attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
+    acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    if world > 1:
+        t = torch.tensor([el, attn, acc], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el, attn, acc = (float(x) for x in t.tolist())
+        counts = gather(res["oc"])
+        same = bool(all(torch.equal(counts[0], counts[k]) for k in range(world)))
+    else:
+        same = True
+    rec = {
+        "metric": "tree-verify steps/s, tensor-parallel (vocabulary and KV heads split over the ranks)",
+        "value": a.steps / (el / 1e3), "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": el / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "tensor-parallel tree-verify step: B=64 requests, prefixes U[512, 8192], tree rows "
+                               "65, Hq=64, Hkv=8, D=128, page 16, vocab 128256, traversal T=1.0, one layer",
+                   "parallelism": f"tp{world} (KV heads and vocabulary)"},
+        "tokens_per_s": a.steps / (el / 1e3) * B * n,
+        "kernels_us": {"tree_attn": attn, "accept_with_exchange": acc},
+        "ranks_agree": same,
+        "clocks": sampler.summary(t0, t1),
+    }
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if same else 1
+
+
 def main(argv=None):
     a = parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.tp:
+        return run_tp(a)
     return run_b200(a)
 
 

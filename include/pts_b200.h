@@ -80,6 +80,48 @@ int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32
                          int32_t* out_counts, int out_stride, void* workspace,
                          size_t workspace_bytes, pts_stream_t stream);
 
+/* ------------------------------------------------------ vocabulary-sharded acceptance
+ * Tensor-parallel acceptance: each rank holds the logits of one vocabulary
+ * shard (columns [vocab_offset, vocab_offset + shard_vocab) of the rows the
+ * reference softmaxes whole, verification.py:55,212-213,310-311).  The
+ * reference has no tensor parallelism; this is the exchange step of the
+ * 8-way vocabulary split:
+ *   1. pts_accept_shard_partials on every rank: per row a 16-byte partial
+ *      {f64 sum of exp(x - m), f32 max m, i32 first (global) index of m}
+ *      and per node the scaled logit of its token under its parent's row if
+ *      this shard holds the token (else -inf);
+ *   2. all-gather both arrays (shard order);
+ *   3. pts_accept_merge_shards on every rank: 16-byte row statistics
+ *      {f32 m, f32 s, i32 argmax, i32 flags}, flags bit 0 = a rounding tie
+ *      decides the argmax of the rounded probabilities, plus merged token
+ *      logits;
+ *   4. pts_accept_shard_ties on every rank: per tied row the first index of
+ *      this shard with the largest rounded probability (INT_MAX otherwise);
+ *   5. all-gather those indices;
+ *   6. pts_accept_walk_merged on every rank: the walks of verify_tree_exact
+ *      (draft_probs == NULL) or verify_tree_traversal (Philox stream as in
+ *      pts_accept_traversal) from the merged statistics; it rewrites the
+ *      argmax of tied rows in row_stats.
+ * Every rank obtains the same accepted paths. */
+int pts_accept_shard_partials(const uint16_t* logits_shard, int64_t row_stride,
+                              const int32_t* row_indptr, const int32_t* parents,
+                              const int32_t* tokens, int batch, int num_rows, int shard_vocab,
+                              int vocab_offset, float temperature, void* out_partials,
+                              float* out_token_logit, void* workspace, size_t workspace_bytes,
+                              pts_stream_t stream);
+int pts_accept_merge_shards(const void* partials_all, const float* token_logit_all, int num_shards,
+                            int num_rows, void* out_row_stats, float* out_token_logit,
+                            pts_stream_t stream);
+int pts_accept_shard_ties(const uint16_t* logits_shard, int64_t row_stride, int num_rows,
+                          int shard_vocab, int vocab_offset, float temperature,
+                          const void* row_stats, int32_t* out_first, pts_stream_t stream);
+int pts_accept_walk_merged(void* row_stats, const float* token_logit, const int32_t* ties_all,
+                           int num_shards, const int32_t* row_indptr, const int32_t* parents,
+                           const int32_t* tokens, const float* draft_probs, int batch, int num_rows,
+                           int vocab, int max_nodes, int64_t eos_token_id, uint64_t philox_seed,
+                           uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                           int32_t* out_counts, int out_stride, pts_stream_t stream);
+
 /* pts_accept_traversal without a workspace argument.  No counterpart in the
  * reference: it is for callers that cannot allocate device memory (a host
  * program holding only device pointers handed over by another runtime, or a

@@ -36,6 +36,12 @@ SIGNATURES = {
                                        C.c_int, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
     "pts_accept_traversal_noalloc": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64,
                                                f32, f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp]),
+    "pts_accept_shard_partials": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,
+                                            vp, sz, vp]),
+    "pts_accept_merge_shards": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
+    "pts_accept_shard_ties": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, f32, vp, vp, vp]),
+    "pts_accept_walk_merged": (C.c_int, [vp, vp, vp, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         i64, u64, u64, vp, vp, vp, C.c_int, vp]),
     "pts_batch_positions": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_kv_append": (C.c_int, [vp, vp, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, vp]),

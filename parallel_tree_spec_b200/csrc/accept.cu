@@ -86,6 +86,12 @@ struct AcceptParams {
   unsigned* req_ctr;
   unsigned* walk_ctr;      // [1]: requests claimed by the persistent kernel's walkers
   unsigned* row_done;      // per row: 1 once its statistics are in row_ws (release/acquire)
+  // vocabulary-sharded (tensor-parallel) acceptance
+  struct Part* parts_out;  // shard partials mode: per row the merged (sum, max, first index), no walks
+  float* tok_logit_out;    // shard partials mode: per node its token's (scaled) logit if this shard holds it
+  int vocab_offset;        // first vocabulary column of this shard
+  const float* tok_logit;  // merged mode: per node its token's scaled logit (instead of reading logits)
+  int stats_ready;         // merged mode: row_ws is complete, no waiting
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -96,6 +102,7 @@ __device__ __forceinline__ void publish_row(const AcceptParams& p, int row) {
 }
 
 __device__ __forceinline__ bool row_published(const AcceptParams& p, int row) {
+  if (p.stats_ready) return true;
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.row_done + row) : "memory");
   return v != 0;
@@ -118,6 +125,7 @@ __device__ __forceinline__ bool wait_rows_warp(const AcceptParams& p, int row) {
 
 // Bounded wait until row `row`'s statistics are published; false on timeout.
 __device__ __forceinline__ bool wait_row(const AcceptParams& p, int row) {
+  if (p.stats_ready) return true;
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.row_done + row) : "memory");
   if (v) return true;
@@ -714,7 +722,9 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
       if (i >= n) continue;
       const float pm = __ldcg(&p.row_ws[pr].m), ps = __ldcg(&p.row_ws[pr].s);
       const int tk = w.token[i];
-      const float x = (tk >= 0 && tk < p.vocab) ? load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk) : -INFINITY;
+      const float x = (tk < 0 || tk >= p.vocab) ? -INFINITY
+                      : p.tok_logit ? p.tok_logit[lo + i]
+                                    : load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk);
       const float mb = prob_bf16(x, pm, ps);
       w.val[r.slot].x = mb;
       w.rec[i].ratio = ratio_of(mb, w.val[r.slot].y);
@@ -843,8 +853,26 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
     // a smaller value can only tie with the max after rounding if the
     // largest bf16 value below m already does
     s_tie = (r.m > -INFINITY) && (prob_bf16(prev_bf16(r.m), r.m, sf) == qmax);
+    s_warp[0] = r;
   }
   __syncthreads();
+  if (p.parts_out) {
+    // shard partials mode: the row's partial and node `row`'s token logit
+    if (warp == 0) {
+      const int b = find_request(p.row_indptr, p.batch, row);
+      if (lane == 0) {
+        Part r = s_warp[0];
+        if (r.idx < kNotCandidate) r.idx += p.vocab_offset;
+        p.parts_out[row] = r;
+        const int lo = p.row_indptr[b], pj = p.parents[row], tk = p.tokens[row] - p.vocab_offset;
+        float xv = -INFINITY;
+        if (row > lo && pj >= 0 && pj < row - lo && tk >= 0 && tk < p.vocab)
+          xv = load_scaled(p, p.logits + (int64_t)(lo + pj) * p.row_stride, tk);
+        p.tok_logit_out[row] = xv;
+      }
+    }
+    return;
+  }
   if (s_tie) {
     int best = INT_MAX;
     for (int e = tid; e < p.vocab; e += kThreads) {
@@ -1351,6 +1379,14 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
         }
       }
       if (!row_done) continue;
+      if (p.parts_out) {
+        if (lane == 0) {
+          if (x.idx < kNotCandidate) x.idx += p.vocab_offset;
+          p.parts_out[row] = x;
+        }
+        __syncwarp();
+        continue;
+      }
       finish_row_warp(p, row, x);
     }
   } else {
@@ -1358,6 +1394,18 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     // Claims the next request and walks it, waiting for each row it reads
     // (parents' rows, the bonus row) to be published: the walks of different
     // requests run on different SMs while the leaf rows still stream.
+    if (p.parts_out) {
+      // shard partials mode: each node's token logit, if this shard holds the token
+      for (int r = c * 32 + lane; r < p.num_rows; r += plan.G * 32) {
+        const int lo = request_first_row(indptr, p.batch, r);
+        const int pj = p.parents[r], tk = p.tokens[r] - p.vocab_offset;
+        float xv = -INFINITY;
+        if (r > lo && pj >= 0 && pj < r - lo && tk >= 0 && tk < p.vocab)
+          xv = load_scaled(p, p.logits + (int64_t)(lo + pj) * p.row_stride, tk);
+        p.tok_logit_out[r] = xv;
+      }
+      return;
+    }
     const WalkSmem w = walk_smem(sm + kSWalkOff, p.max_nodes);
     for (;;) {
       unsigned t = 0;
@@ -1403,7 +1451,8 @@ size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, s
 int accept_launch(AcceptParams p, int traversal, float temperature, void* workspace, size_t ws_bytes,
                   cudaStream_t stream) {
   PTS_CHECK_ARG(p.logits && p.row_indptr && p.parents && p.tokens, "null input pointer");
-  PTS_CHECK_ARG(p.out_tokens && p.out_hidden && p.out_counts, "null output pointer");
+  PTS_CHECK_ARG(p.parts_out ? (p.tok_logit_out != nullptr) : (p.out_tokens && p.out_hidden && p.out_counts),
+                "null output pointer");
   PTS_CHECK_ARG(p.batch > 0 && p.num_rows >= p.batch, "need batch > 0 and num_rows >= batch");
   PTS_CHECK_ARG(p.vocab > 0 && p.row_stride >= p.vocab, "need vocab > 0 and row_stride >= vocab");
   PTS_CHECK_ARG(p.max_nodes > 0, "max_nodes must be positive");
@@ -1412,7 +1461,7 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
                      PTS_MAX_TREE_NODES);
   if (p.vocab > kMaxChunks * kChunk)
     return set_error(PTS_ERR_UNSUPPORTED, "vocab %d above %d", p.vocab, kMaxChunks * kChunk);
-  PTS_CHECK_ARG(p.out_stride >= 1, "out_stride must be positive");
+  PTS_CHECK_ARG(p.parts_out || p.out_stride >= 1, "out_stride must be positive");
   PTS_CHECK_ARG(temperature > 0.0f, "temperature must be positive");
   if (p.num_rows > 65535) return set_error(PTS_ERR_CAPACITY, "num_rows %d above 65535", p.num_rows);
   size_t opt, orw, orc, oqc, owk;
@@ -1469,6 +1518,75 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   }
   accept_kernel<<<dim3(nchunks, p.num_rows), kThreads, smem, stream>>>(p);
   return launch_status("accept_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded (tensor-parallel) acceptance.  Each rank holds the logits
+// of a vocabulary shard; pts_accept_shard_partials reduces them to per-row
+// partials (the persistent streaming kernel in partials mode), the ranks
+// all-gather the partials, and every rank then merges them in shard order
+// (merge_shards_kernel), resolves rounding ties of the argmax with one more
+// all-gather of per-shard first indices (shard_ties_kernel), and walks the
+// trees from the merged statistics (walk_merged_kernel), so every rank gets
+// the same accepted paths.
+
+__global__ void merge_shards_kernel(const Part* parts, const float* tok_in, int shards, int rows, RowStat* out,
+                                    float* tok_out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  Part acc = parts[r];
+  float t = tok_in[r];
+  for (int k = 1; k < shards; ++k) {
+    acc = merge(acc, parts[(int64_t)k * rows + r]);
+    t = fmaxf(t, tok_in[(int64_t)k * rows + r]);
+  }
+  RowStat rs;
+  rs.m = acc.m;
+  rs.s = (float)acc.s;
+  rs.argmax = acc.idx;
+  const float qmax = round_to_bf16(__fdiv_rn(1.0f, rs.s));
+  // as in finish_row_warp: a value below the max can only take the argmax of
+  // the rounded probabilities if the largest bf16 value below the max does
+  rs.flags = (acc.m > -INFINITY) && (prob_bf16(prev_bf16(acc.m), acc.m, rs.s) == qmax);
+  out[r] = rs;
+  tok_out[r] = t;
+}
+
+// One warp per row: for rows flagged with a rounding tie, the first index of
+// this shard whose rounded probability equals the row's largest one.
+__global__ void shard_ties_kernel(const AcceptParams p, const RowStat* rows, int* out_first) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= p.num_rows) return;
+  const RowStat rs = rows[warp];
+  int best = INT_MAX;
+  if (rs.flags & 1) {
+    const float qmax = round_to_bf16(__fdiv_rn(1.0f, rs.s));
+    const uint16_t* rp = p.logits + (int64_t)warp * p.row_stride;
+    for (int e = lane; e < p.vocab; e += 32)
+      if (prob_bf16(load_scaled(p, rp, e), rs.m, rs.s) == qmax) {
+        best = e + p.vocab_offset;
+        break;
+      }
+    best = (int)__reduce_min_sync(0xffffffffu, (unsigned)best);
+  }
+  if (lane == 0) out_first[warp] = best;
+}
+
+// One warp per request: settle the argmax of tied rows (smallest index over
+// all shards), then walk from the merged statistics.
+__global__ void walk_merged_kernel(const AcceptParams p, const int* ties, int shards) {
+  extern __shared__ __align__(128) uint8_t wsm[];
+  const int b = blockIdx.x, lane = threadIdx.x & 31;
+  const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
+  for (int r = lo + lane; r < lo + n; r += 32) {
+    if (p.row_ws[r].flags & 1) {
+      int best = INT_MAX;
+      for (int k = 0; k < shards; ++k) best = min(best, ties[(int64_t)k * p.num_rows + r]);
+      p.row_ws[r].argmax = best;
+    }
+  }
+  __syncwarp();
+  walk_request(p, b, lo, n, walk_smem(wsm, p.max_nodes), WarpGroup{}, nullptr);
 }
 
 }  // namespace
@@ -1536,6 +1654,105 @@ extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, 
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
   return accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded acceptance (tensor parallelism): C ABI.
+
+extern "C" int pts_accept_shard_partials(const uint16_t* logits_shard, int64_t row_stride, const int32_t* row_indptr,
+                                         const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                                         int shard_vocab, int vocab_offset, float temperature, void* out_partials,
+                                         float* out_token_logit, void* workspace, size_t workspace_bytes,
+                                         pts_stream_t stream) {
+  PTS_CHECK_ARG(out_partials && out_token_logit, "null output pointer");
+  PTS_CHECK_ARG(vocab_offset >= 0, "vocab_offset must be non-negative");
+  AcceptParams p{};
+  p.logits = logits_shard;
+  p.row_stride = row_stride;
+  p.row_indptr = row_indptr;
+  p.parents = parents;
+  p.tokens = tokens;
+  p.batch = batch;
+  p.num_rows = num_rows;
+  p.vocab = shard_vocab;
+  p.max_nodes = 1;
+  p.eos = -1;
+  p.parts_out = (Part*)out_partials;
+  p.tok_logit_out = out_token_logit;
+  p.vocab_offset = vocab_offset;
+  return accept_launch(p, 0, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int pts_accept_merge_shards(const void* partials_all, const float* token_logit_all, int num_shards,
+                                       int num_rows, void* out_row_stats, float* out_token_logit,
+                                       pts_stream_t stream) {
+  PTS_CHECK_ARG(partials_all && token_logit_all && out_row_stats && out_token_logit, "null pointer");
+  PTS_CHECK_ARG(num_shards >= 1 && num_rows >= 1, "need num_shards >= 1 and num_rows >= 1");
+  merge_shards_kernel<<<(num_rows + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
+      (const Part*)partials_all, token_logit_all, num_shards, num_rows, (RowStat*)out_row_stats, out_token_logit);
+  return launch_status("merge_shards_kernel");
+}
+
+extern "C" int pts_accept_shard_ties(const uint16_t* logits_shard, int64_t row_stride, int num_rows, int shard_vocab,
+                                     int vocab_offset, float temperature, const void* row_stats, int32_t* out_first,
+                                     pts_stream_t stream) {
+  PTS_CHECK_ARG(logits_shard && row_stats && out_first, "null pointer");
+  PTS_CHECK_ARG(num_rows >= 1 && shard_vocab >= 1 && row_stride >= shard_vocab, "bad sizes");
+  PTS_CHECK_ARG(temperature > 0.0f, "temperature must be positive");
+  AcceptParams p{};
+  p.logits = logits_shard;
+  p.row_stride = row_stride;
+  p.num_rows = num_rows;
+  p.vocab = shard_vocab;
+  p.vocab_offset = vocab_offset;
+  p.use_temp = (temperature != 1.0f);
+  p.inv_temp = 1.0f / temperature;
+  shard_ties_kernel<<<(num_rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>(p, (const RowStat*)row_stats, out_first);
+  return launch_status("shard_ties_kernel");
+}
+
+extern "C" int pts_accept_walk_merged(void* row_stats, const float* token_logit, const int32_t* ties_all,
+                                      int num_shards, const int32_t* row_indptr, const int32_t* parents,
+                                      const int32_t* tokens, const float* draft_probs, int batch, int num_rows,
+                                      int vocab, int max_nodes, int64_t eos_token_id, uint64_t philox_seed,
+                                      uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                                      int32_t* out_counts, int out_stride, pts_stream_t stream) {
+  PTS_CHECK_ARG(row_stats && token_logit && ties_all && row_indptr && parents && tokens, "null input pointer");
+  PTS_CHECK_ARG(out_tokens && out_hidden && out_counts && out_stride >= 1, "bad outputs");
+  PTS_CHECK_ARG(batch > 0 && num_rows >= batch && num_shards >= 1 && vocab > 0 && max_nodes > 0, "bad sizes");
+  if (max_nodes > PTS_MAX_TREE_NODES)
+    return set_error(PTS_ERR_CAPACITY, "max_nodes %d above PTS_MAX_TREE_NODES %d", max_nodes, PTS_MAX_TREE_NODES);
+  AcceptParams p{};
+  p.row_indptr = row_indptr;
+  p.parents = parents;
+  p.tokens = tokens;
+  p.draft_probs = draft_probs;
+  p.batch = batch;
+  p.num_rows = num_rows;
+  p.vocab = vocab;
+  p.max_nodes = max_nodes;
+  p.out_stride = out_stride;
+  p.eos = eos_token_id;
+  p.traversal = draft_probs != nullptr;
+  p.seed = philox_seed;
+  p.offset = philox_offset;
+  p.out_tokens = out_tokens;
+  p.out_hidden = out_hidden;
+  p.out_counts = out_counts;
+  p.row_ws = (RowStat*)row_stats;
+  p.tok_logit = token_logit;
+  p.stats_ready = 1;
+  const size_t smem = walk_smem_bytes(max_nodes);
+  if (smem > 232448) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
+  int dev = 0;
+  PTS_CUDA_TRY(cudaGetDevice(&dev));
+  static size_t attr[256] = {};
+  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
+    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[dev] = smem;
+  }
+  walk_merged_kernel<<<batch, 32, smem, (cudaStream_t)stream>>>(p, ties_all, num_shards);
+  return launch_status("walk_merged_kernel");
 }
 
 // ---------------------------------------------------------------------------

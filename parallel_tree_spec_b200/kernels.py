@@ -118,6 +118,97 @@ def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
     return ot, oh, oc
 
 
+# ------------------------------------------------- vocabulary-sharded acceptance
+def accept_shard_partials(logits_shard: torch.Tensor, vocab_offset: int, row_indptr: torch.Tensor,
+                          parents: torch.Tensor, tokens: torch.Tensor, temperature: float = 1.0):
+    """Step 1 of the sharded acceptance: ``logits_shard`` [rows, Vs] bf16 is
+    this rank's vocabulary columns (any row stride).  Returns (partials
+    [rows, 2] int64 holding 16-byte records, token logits [rows] f32)."""
+    if logits_shard.dtype != torch.bfloat16 or logits_shard.dim() != 2 or logits_shard.stride(1) != 1:
+        raise ValueError("logits_shard must be a 2-D bf16 tensor with contiguous rows")
+    dev, row_indptr, parents, tokens = _accept_common(logits_shard, row_indptr, parents, tokens)
+    R, Vs = logits_shard.shape
+    parts = torch.empty(R, 2, dtype=torch.int64, device=dev)
+    tok = torch.empty(R, dtype=torch.float32, device=dev)
+    ws = workspace(dev, "accept_shard", _lib.lib().pts_accept_workspace_size(R, Vs))
+    _lib.call("pts_accept_shard_partials", logits_shard.data_ptr(), logits_shard.stride(0), row_indptr.data_ptr(),
+              parents.data_ptr(), tokens.data_ptr(), row_indptr.numel() - 1, R, Vs, int(vocab_offset),
+              float(temperature), parts.data_ptr(), tok.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+    return parts, tok
+
+
+def accept_merge_shards(parts_all: torch.Tensor, tok_all: torch.Tensor):
+    """Step 3: ``parts_all`` [shards, rows, 2] int64, ``tok_all`` [shards, rows]
+    f32 (all-gathered in shard order) -> (row statistics [rows, 4] int32
+    holding 16-byte records, merged token logits [rows] f32)."""
+    dev = _need_cuda(parts_all, tok_all)
+    K, R = tok_all.shape
+    stats = torch.empty(R, 4, dtype=torch.int32, device=dev)
+    tok = torch.empty(R, dtype=torch.float32, device=dev)
+    _lib.call("pts_accept_merge_shards", parts_all.contiguous().data_ptr(), tok_all.contiguous().data_ptr(), K, R,
+              stats.data_ptr(), tok.data_ptr(), _stream(dev))
+    return stats, tok
+
+
+def accept_shard_ties(logits_shard: torch.Tensor, vocab_offset: int, stats: torch.Tensor,
+                      temperature: float = 1.0) -> torch.Tensor:
+    """Step 4: per tied row the first index of this shard holding the row's
+    largest rounded probability (INT_MAX elsewhere), [rows] int32."""
+    dev = _need_cuda(logits_shard, stats)
+    R, Vs = logits_shard.shape
+    first = torch.empty(R, dtype=torch.int32, device=dev)
+    _lib.call("pts_accept_shard_ties", logits_shard.data_ptr(), logits_shard.stride(0), R, Vs, int(vocab_offset),
+              float(temperature), stats.data_ptr(), first.data_ptr(), _stream(dev))
+    return first
+
+
+def accept_walk_merged(stats: torch.Tensor, tok: torch.Tensor, ties_all: torch.Tensor, vocab: int,
+                       row_indptr: torch.Tensor, parents: torch.Tensor, tokens: torch.Tensor,
+                       draft_probs: Optional[torch.Tensor] = None, eos_token_id: Optional[int] = None,
+                       seed: int = 0, offset: int = 0, max_nodes: Optional[int] = None):
+    """Step 6: greedy (``draft_probs`` None) or traversal walks from merged
+    statistics; same outputs as ``accept_greedy`` / ``accept_traversal``."""
+    dev = _need_cuda(stats, tok, ties_all, row_indptr, parents, tokens)
+    row_indptr, parents, tokens = _i32(row_indptr, "a"), _i32(parents, "b"), _i32(tokens, "c")
+    B = row_indptr.numel() - 1
+    R = tok.numel()
+    mn = min(int(max_nodes) if max_nodes is not None else R, _lib.PTS_MAX_TREE_NODES)
+    ot = torch.empty(B, mn, dtype=torch.int32, device=dev)
+    oh = torch.empty(B, mn, dtype=torch.int32, device=dev)
+    oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    dp = None
+    if draft_probs is not None:
+        dp = draft_probs.to(torch.float32).contiguous()
+    _lib.call("pts_accept_walk_merged", stats.data_ptr(), tok.data_ptr(), ties_all.contiguous().data_ptr(),
+              ties_all.shape[0], row_indptr.data_ptr(), parents.data_ptr(), tokens.data_ptr(),
+              dp.data_ptr() if dp is not None else None, B, R, int(vocab), mn,
+              -1 if eos_token_id is None else int(eos_token_id), int(seed) & (2 ** 64 - 1),
+              int(offset) & (2 ** 64 - 1), ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), mn, _stream(dev))
+    return ot, oh, oc
+
+
+def accept_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab: int, row_indptr: torch.Tensor,
+                   parents: torch.Tensor, tokens: torch.Tensor, draft_probs: Optional[torch.Tensor] = None,
+                   group=None, eos_token_id: Optional[int] = None, temperature: float = 1.0, seed: int = 0,
+                   offset: int = 0, max_nodes: Optional[int] = None):
+    """Tensor-parallel acceptance on one rank of ``group`` (torch.distributed,
+    NCCL): the shard partials and the tie indices are all-gathered, every
+    rank merges in shard order and walks; all ranks return the same paths."""
+    import torch.distributed as dist
+    K = dist.get_world_size(group)
+    parts, tok = accept_shard_partials(logits_shard, vocab_offset, row_indptr, parents, tokens, temperature)
+    parts_all = torch.empty(K, *parts.shape, dtype=parts.dtype, device=parts.device)
+    tok_all = torch.empty(K, *tok.shape, dtype=tok.dtype, device=tok.device)
+    dist.all_gather_into_tensor(parts_all, parts, group=group)
+    dist.all_gather_into_tensor(tok_all, tok, group=group)
+    stats, tokm = accept_merge_shards(parts_all, tok_all)
+    first = accept_shard_ties(logits_shard, vocab_offset, stats, temperature)
+    ties_all = torch.empty(K, *first.shape, dtype=first.dtype, device=first.device)
+    dist.all_gather_into_tensor(ties_all, first, group=group)
+    return accept_walk_merged(stats, tokm, ties_all, vocab, row_indptr, parents, tokens, draft_probs,
+                              eos_token_id, seed, offset, max_nodes)
+
+
 # ------------------------------------------------------------------ paged KV
 def batch_positions(append_indptr: torch.Tensor, seq_lens: torch.Tensor, num_tokens: int):
     dev = _need_cuda(append_indptr, seq_lens)
