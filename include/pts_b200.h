@@ -140,6 +140,35 @@ int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride,
                                  int32_t* out_hidden, int32_t* out_counts, int out_stride,
                                  pts_stream_t stream);
 
+/* ------------------------------------------------------------- sparse page sets
+ * Long-prefix requests restricted to a page subset per KV head.  The
+ * reference selects important pages (q . k scores aggregated per page, top-k
+ * plus a recent window) only for the draft's decode and with one set for all
+ * heads (sparse_attention/pillar.py:83-216); these entry points select a set
+ * per (request, KV head) for the verification attention.
+ *
+ * pts_page_key_sums: out[i, h, :] = fp32 sum of the page_len keys of page
+ * page_ids[i], head h (a page summary kept beside the cache, [n, Hkv, D]).
+ *
+ * pts_select_pages: key_sums aligned with page_indices ([entries, Hkv, 128]);
+ * per (request b, KV head h), in position order: the first n_first and last
+ * n_last full prefix pages, the n_top middle pages of highest score
+ * qbar . key_sum (qbar = the root query row qo_indptr[b] averaged over h's
+ * GQA group; ties to the earlier page), then every page from the first one
+ * holding a tree token.  Outputs per-head tables for
+ * pts_tree_attn_run_head_pages: out_head_indptr [B*Hkv+1],
+ * out_head_indices (capacity Hkv * entries of page_indices),
+ * out_head_last_page_len [B*Hkv].  max_prefix_pages bounds the pages of any
+ * request (at most 8192). */
+int pts_page_key_sums(const void* kv_layer, const int32_t* page_ids, int num_pages, int num_kv_heads,
+                      int head_dim, int page_len, float* out, pts_stream_t stream);
+int pts_select_pages(const float* key_sums, const int32_t* page_indptr, const int32_t* page_indices,
+                     const int32_t* last_page_len, const void* q, const int32_t* qo_indptr, int batch,
+                     int num_qo_heads, int num_kv_heads, int head_dim, int page_len, int n_first,
+                     int n_top, int n_last, int max_prefix_pages, int32_t* out_head_indptr,
+                     int32_t* out_head_indices, int32_t* out_head_last_page_len,
+                     pts_stream_t stream);
+
 /* ------------------------------------------------------------------ paged KV
  * Per appended token t: batch_indices[t] = b and positions[t] = seq_lens[b] -
  * (append_indptr[b+1] - append_indptr[b]) + (t - append_indptr[b]).
@@ -210,6 +239,20 @@ int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_ind
                       int num_qo_heads, int num_kv_heads, int head_dim, int page_len,
                       int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
                       pts_stream_t stream);
+
+/* pts_tree_attn_run with page tables per (request, KV head): head_page_indptr
+ * [B*Hkv+1] and head_last_page_len [B*Hkv] indexed b * Hkv + h, every list
+ * ending with the request's tree (its last N slots), for example the sparse
+ * sets of pts_select_pages.  Replaces the same FlashInfer paged prefill
+ * (attention_wrapper.py:131-144, 250-252) when each KV head attends its own
+ * page subset. */
+int pts_tree_attn_run_head_pages(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                                 const int32_t* head_page_indptr, const int32_t* head_page_indices,
+                                 const int32_t* head_last_page_len, const uint64_t* mask_bits,
+                                 int mask_words, void* out, int batch, int total_q, int max_qo_len,
+                                 int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
+                                 int page_len, int max_pages, float sm_scale, void* workspace,
+                                 size_t workspace_bytes, pts_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,10 @@ for the tree-verification path of parallel_tree_spec:
   ``tree.py:167-194``).
 * ``philox``    -- Philox4x32-10 (Salmon et al., SC'11) and the uniform
   stream that replaces ``torch.rand(1)`` inside the traversal loop.
+* ``pages``     -- page key sums, per-KV-head sparse page selection and tree
+  attention over per-head page tables (long-prefix requests; parity
+  unpinned: the reference selects pages for the draft only, one set for all
+  heads, ``sparse_attention/pillar.py:83-216``).
 
 It is the checker, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import it.

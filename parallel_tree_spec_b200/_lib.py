@@ -49,6 +49,12 @@ SIGNATURES = {
                                  vp, C.c_int, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_tree_mask_from_parents": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "pts_tree_mask_from_bool": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
+    "pts_tree_attn_run_head_pages": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, sz,
+                                               vp]),
+    "pts_page_key_sums": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]),
+    "pts_select_pages": (C.c_int, [vp, vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                   C.c_int, C.c_int, C.c_int, vp, vp, vp, vp]),
     "pts_tree_attn_workspace_size": (sz, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "pts_tree_attn_run": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, sz, vp]),

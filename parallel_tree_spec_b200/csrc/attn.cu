@@ -96,6 +96,7 @@ struct AttnParams {
   int mask_words;
   uint16_t* out;
   int Hq, Hkv, g;
+  int head_pages;          // page tables per (request, KV head) instead of per request
   int max_pages;
   float scale_log2;
   int* err;
@@ -161,10 +162,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tensor_rows = min(kTensorRows, rows_here);
   const int n_tiles = (tensor_rows + 127) / 128;
   const int sync_rows = rows_here - tensor_rows;
-  const int p0 = p.page_indptr[b];
-  const int n_pages = p.page_indptr[b + 1] - p0;
+  const int pt = p.head_pages ? b * p.Hkv + h : b;     // this CTA's page table
+  const int p0 = p.page_indptr[pt];
+  const int n_pages = p.page_indptr[pt + 1] - p0;
   if (n_pages <= 0) return;
-  const int kv_len = (n_pages - 1) * kPage + p.last_page_len[b];
+  const int kv_len = (n_pages - 1) * kPage + p.last_page_len[pt];
   const int prefix = kv_len - n_nodes;
   const int n_blocks = (kv_len + kBlockN - 1) / kBlockN;
 
@@ -678,12 +680,12 @@ using namespace pts;
 
 extern "C" size_t pts_tree_attn_workspace_size(int, int, int, int, int) { return 256; }
 
-extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_indptr,
-                                 const int32_t* page_indptr, const int32_t* page_indices, const int32_t* last_page_len,
-                                 const uint64_t* mask_bits, int mask_words, void* out, int batch, int total_q,
-                                 int max_qo_len, int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
-                                 int page_len, int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
-                                 pts_stream_t stream) {
+static int tree_attn_launch(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                            const int32_t* page_indptr, const int32_t* page_indices, const int32_t* last_page_len,
+                            const uint64_t* mask_bits, int mask_words, void* out, int batch, int total_q,
+                            int max_qo_len, int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
+                            int page_len, int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
+                            pts_stream_t stream, int head_pages) {
   PTS_CHECK_ARG(q && kv_layer && qo_indptr && page_indptr && page_indices && last_page_len && out, "null pointer");
   PTS_CHECK_ARG(batch > 0 && total_q > 0 && max_qo_len > 0 && max_kv_len > 0, "bad sizes");
   PTS_CHECK_ARG(num_qo_heads > 0 && num_kv_heads > 0 && num_qo_heads % num_kv_heads == 0, "bad head counts");
@@ -724,6 +726,7 @@ extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int3
   p.Hq = num_qo_heads;
   p.Hkv = num_kv_heads;
   p.g = g;
+  p.head_pages = head_pages;
   p.max_pages = max_pages;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.err = (int*)workspace;
@@ -737,4 +740,27 @@ extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int3
   dim3 grid(num_kv_heads, batch, groups);
   tree_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(p, kv_map);
   return launch_status("tree_attn_kernel");
+}
+
+extern "C" int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                                 const int32_t* page_indptr, const int32_t* page_indices, const int32_t* last_page_len,
+                                 const uint64_t* mask_bits, int mask_words, void* out, int batch, int total_q,
+                                 int max_qo_len, int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
+                                 int page_len, int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
+                                 pts_stream_t stream) {
+  return tree_attn_launch(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len, mask_bits, mask_words,
+                          out, batch, total_q, max_qo_len, max_kv_len, num_qo_heads, num_kv_heads, head_dim, page_len,
+                          max_pages, sm_scale, workspace, workspace_bytes, stream, 0);
+}
+
+extern "C" int pts_tree_attn_run_head_pages(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                                            const int32_t* head_page_indptr, const int32_t* head_page_indices,
+                                            const int32_t* head_last_page_len, const uint64_t* mask_bits,
+                                            int mask_words, void* out, int batch, int total_q, int max_qo_len,
+                                            int max_kv_len, int num_qo_heads, int num_kv_heads, int head_dim,
+                                            int page_len, int max_pages, float sm_scale, void* workspace,
+                                            size_t workspace_bytes, pts_stream_t stream) {
+  return tree_attn_launch(q, kv_layer, qo_indptr, head_page_indptr, head_page_indices, head_last_page_len, mask_bits,
+                          mask_words, out, batch, total_q, max_qo_len, max_kv_len, num_qo_heads, num_kv_heads,
+                          head_dim, page_len, max_pages, sm_scale, workspace, workspace_bytes, stream, 1);
 }

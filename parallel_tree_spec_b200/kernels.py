@@ -330,3 +330,63 @@ def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Ten
               mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T,
               int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
     return out
+
+
+# ------------------------------------------------------------ sparse page sets
+def page_key_sums(kv_layer: torch.Tensor, page_ids: torch.Tensor) -> torch.Tensor:
+    """Per page and KV head the fp32 sum of its keys: [n, Hkv, D] float32
+    (a page summary computed once, when the page is full)."""
+    dev = _need_cuda(kv_layer, page_ids)
+    P, _, pl, H, D = kv_layer.shape
+    ids = _i32(page_ids, "page_ids")
+    out = torch.empty(ids.numel(), H, D, dtype=torch.float32, device=dev)
+    _lib.call("pts_page_key_sums", kv_layer.data_ptr(), ids.data_ptr(), ids.numel(), H, D, pl, out.data_ptr(),
+              _stream(dev))
+    return out
+
+
+def select_pages(key_sums: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor,
+                 last_page_len: torch.Tensor, q: torch.Tensor, qo_indptr: torch.Tensor, num_kv_heads: int,
+                 n_first: int = 4, n_top: int = 64, n_last: int = 8, page_len: int = 16,
+                 max_prefix_pages: Optional[int] = None):
+    """Per-(request, KV head) sparse page tables for pts_tree_attn_run_head_pages:
+    the first ``n_first`` and last ``n_last`` full prefix pages, the ``n_top``
+    middle pages of highest root-query . key-sum score, and the pages that
+    hold the tree.  ``key_sums`` is aligned with ``page_indices``.  Returns
+    (head_indptr [B*Hkv+1], head_indices, head_last_page_len [B*Hkv])."""
+    dev = _need_cuda(key_sums, page_indptr, page_indices, last_page_len, q, qo_indptr)
+    page_indptr, page_indices = _i32(page_indptr, "a"), _i32(page_indices, "b")
+    B = page_indptr.numel() - 1
+    T, Hq, D = q.shape
+    if max_prefix_pages is None:
+        max_prefix_pages = int((page_indptr[1:] - page_indptr[:-1]).max().item())
+    indptr = torch.empty(B * num_kv_heads + 1, dtype=torch.int32, device=dev)
+    indices = torch.empty(num_kv_heads * page_indices.numel(), dtype=torch.int32, device=dev)
+    last = torch.empty(B * num_kv_heads, dtype=torch.int32, device=dev)
+    _lib.call("pts_select_pages", key_sums.data_ptr(), page_indptr.data_ptr(), page_indices.data_ptr(),
+              _i32(last_page_len, "c").data_ptr(), q.data_ptr(), _i32(qo_indptr, "d").data_ptr(), B, Hq,
+              num_kv_heads, D, page_len, n_first, n_top, n_last, int(max_prefix_pages), indptr.data_ptr(),
+              indices.data_ptr(), last.data_ptr(), _stream(dev))
+    return indptr, indices, last
+
+
+def tree_attention_head_pages(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Tensor,
+                              head_indptr: torch.Tensor, head_indices: torch.Tensor, head_last: torch.Tensor,
+                              mask_bits: Optional[torch.Tensor], max_qo_len: int, max_kv_len: int,
+                              sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Tree attention where KV head h of request b reads its own page list
+    (index b * Hkv + h); the tree occupies the last N slots of every list."""
+    dev = _need_cuda(q, kv_layer, qo_indptr, head_indptr, head_indices, head_last)
+    T, Hq, D = q.shape
+    P, _, pl, Hkv, _ = kv_layer.shape
+    B = qo_indptr.numel() - 1
+    if out is None:
+        out = torch.empty_like(q)
+    scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(D)
+    ws = workspace(dev, "attn", 256)
+    _lib.call("pts_tree_attn_run_head_pages", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
+              _i32(head_indptr, "hi").data_ptr(), _i32(head_indices, "hx").data_ptr(),
+              _i32(head_last, "hl").data_ptr(), mask_bits.data_ptr() if mask_bits is not None else None,
+              mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T, int(max_qo_len),
+              int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
+    return out
