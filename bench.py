@@ -65,6 +65,9 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
                     help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sparse", action="store_true",
+                    help="long-context sparse step (batch 8, 32768-token prefixes, 129-row trees, attention over "
+                         "per-KV-head sets of 4 first + 64 top-scored + 8 last prefix pages, greedy)")
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel step (70B-shaped target: 64 query / 8 KV heads split over the ranks, "
                          "vocabulary split over the ranks, batch 64, prefixes U[512, 8192]); run under torchrun")
@@ -642,10 +645,134 @@ def run_tp(a):
     return 0 if same else 1
 
 
+# ---------------------------------------------------------------- long-context sparse step
+def run_sparse(a):
+    """Long-context verification step: 8 requests with 32768-token prefixes
+    and 129-row trees (width 16, depth 8), Hq=32 / Hkv=8.  The per-KV-head
+    page sets (first 4 + 64 highest root-query . key-sum scores + last 8
+    prefix pages, plus the tree's pages) are selected once after the prefill
+    from page key sums (timed separately); each step packs masks, appends the
+    tree K/V, runs attention over the per-head page tables, greedy acceptance
+    over [1032, 128256] bf16 logits and compaction."""
+    import torch
+    from parallel_tree_spec_b200 import _lib, kernels as K
+    from parallel_tree_spec_b200 import workload as wl
+    from parallel_tree_spec_b200._lib import check
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L = _lib.lib()
+    B, P, Hq, Hkv, D, pl, V = 8, 32768, 32, 8, 128, 16, a.vocab
+    rng = np.random.default_rng(a.seed + 11)
+    trees = [wl.make_tree(rng, 16, 8, V) for _ in range(B)]
+    n = trees[0].size
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    kv_len = P + n
+    npg = (kv_len + pl - 1) // pl
+    max_pages = B * npg + 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 21)
+    layer = torch.empty(max_pages, 2, pl, Hkv, D, dtype=torch.bfloat16, device=dev).normal_(0, 1 / math.sqrt(D),
+                                                                                          generator=g)
+    perm = torch.randperm(max_pages, generator=g, device=dev)[: B * npg].to(torch.int32)
+    T = B * n
+    q = torch.randn(T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    kn = (torch.randn(T, Hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    vn = (torch.randn(T, Hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    x = (torch.randn(T, V, generator=g, device=dev) * 3.0).to(torch.bfloat16)
+    d = lambda v: torch.as_tensor(np.ascontiguousarray(v), dtype=torch.int32, device=dev)
+    qo, parents, tokens = d(indptr), d(par), d(tok)
+    pind = d(np.arange(B + 1) * npg)
+    lastp, seqlens, offs = d(np.full(B, (kv_len - 1) % pl + 1)), d(np.full(B, kv_len)), d(np.full(B, P))
+    # page sets, once after the prefill
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        e0.record()
+        ks = K.page_key_sums(layer, perm)
+        hi, hx, hl = K.select_pages(ks, pind, perm, lastp, q, qo, Hkv, n_first=4, n_top=64, n_last=8,
+                                    max_prefix_pages=npg)
+        e1.record()
+        torch.cuda.synchronize()
+    select_us = e0.elapsed_time(e1) * 1e3
+    sel_pages = int(hi[1].item() - hi[0].item())
+    mw = K.mask_words_for(n)
+    bits = torch.empty(T, mw, dtype=torch.int64, device=dev)
+    bi = torch.empty(T, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    attn_ws = K.workspace(dev, "attn", 256)
+    acc_ws = K.workspace(dev, "accept", L.pts_accept_workspace_size(T, V))
+    ot = torch.empty(B, n, dtype=torch.int32, device=dev)
+    oh = torch.empty(B, n, dtype=torch.int32, device=dev)
+    oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    pool = layer.view(1, *layer.shape)
+    s = torch.cuda.current_stream(dev).cuda_stream
+
+    def one(ev=None):
+        check(L.pts_tree_mask_from_parents(parents.data_ptr(), qo.data_ptr(), B, T, mw, bits.data_ptr(), s), "mask")
+        check(L.pts_batch_positions(qo.data_ptr(), seqlens.data_ptr(), B, T, bi.data_ptr(), pos.data_ptr(), s), "pos")
+        check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), Hkv * D, Hkv * D, layer.data_ptr(), bi.data_ptr(),
+                              pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, Hkv, D, pl, max_pages, 2, s), "app")
+        if ev is not None:
+            ev[0].record()
+        check(L.pts_tree_attn_run_head_pages(q.data_ptr(), layer.data_ptr(), qo.data_ptr(), hi.data_ptr(),
+                                             hx.data_ptr(), hl.data_ptr(), bits.data_ptr(), mw, out.data_ptr(), B, T,
+                                             n, sel_pages * pl, Hq, Hkv, D, pl, max_pages, 1 / math.sqrt(D),
+                                             attn_ws.data_ptr(), attn_ws.numel(), s), "attention")
+        if ev is not None:
+            ev[1].record()
+        check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), qo.data_ptr(), parents.data_ptr(), tokens.data_ptr(),
+                                  B, T, V, n, -1, ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), n,
+                                  acc_ws.data_ptr(), acc_ws.numel(), s), "accept")
+        if ev is not None:
+            ev[2].record()
+        check(L.pts_kv_compact(pool.data_ptr(), 1, max_pages, pl, Hkv, D, 2, pind.data_ptr(), perm.data_ptr(),
+                               oh.data_ptr(), n, oc.data_ptr(), 4, offs.data_ptr(), B, n, None, None, s), "compact")
+
+    for _ in range(max(3, a.warmup)):
+        one()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local).start()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start.record()
+    for i in range(a.steps):
+        one(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    sampler.stop()
+    el = start.elapsed_time(end)
+    attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
+    acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    groups = (n * (Hq // Hkv) + 263) // 264
+    kv_bytes = B * Hkv * groups * sel_pages * pl * D * 2 * 2
+    rec = {
+        "metric": "tree-verify steps/s, long-context sparse (per-KV-head page sets)",
+        "value": a.steps / (el / 1e3), "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": el / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": f"long-context sparse tree-verify step: B={B} requests, prefix {P}, tree rows {n} "
+                               f"(width 16, depth 8), Hq={Hq}, Hkv={Hkv}, D=128, page 16, {sel_pages} pages per KV "
+                               f"head (4 first + 64 top + 8 last + tree pages), vocab {V}, greedy, one layer"},
+        "tokens_per_s": a.steps / (el / 1e3) * B * n,
+        "kernels_us": {"tree_attn_head_pages": attn, "accept": acc, "select_once": select_us},
+        "attention_kv_gbs": kv_bytes / (attn * 1e-6) / 1e9,
+        "clocks": sampler.summary(t0, t1),
+    }
+    print(json.dumps(rec), flush=True)
+    return 0
+
+
 def main(argv=None):
     a = parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.sparse:
+        return run_sparse(a)
     if a.tp:
         return run_tp(a)
     return run_b200(a)
