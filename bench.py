@@ -60,6 +60,7 @@ def parse_args(argv=None):
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--top-p", type=float, default=1.0, help="nucleus target distribution for traversal (extension)")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-sample-requests", type=int, default=1)
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
@@ -77,6 +78,8 @@ def parse_args(argv=None):
 
 def workload_name(a):
     mode = f"traversal T={a.temperature}" if a.mode == "traversal" else "greedy"
+    if a.mode == "traversal" and a.top_p < 1.0:
+        mode += f" top-p {a.top_p}"
     n = 1 + a.width * a.depth
     return (f"tree-verify step: B={a.batch} requests, prefix={a.prefix}, tree rows={n} (width {a.width}, depth "
             f"{a.depth}), Hq={a.hq}, Hkv={a.hkv}, D=128, page=16, vocab={a.vocab}, {mode}")
@@ -268,7 +271,7 @@ class Step:
         if a.mode == "traversal":
             check(L.pts_accept_traversal(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
                                          W["tokens"].data_ptr(), W["draft_probs"].data_ptr(), B, B * n, a.vocab, n,
-                                         -1, a.temperature, 1.0, 0, self.philox_seed, self.step_index,
+                                         -1, a.temperature, a.top_p, 0, self.philox_seed, self.step_index,
                                          W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
                                          self.acc_ws.data_ptr(), self.acc_ws.numel(), s), "accept")
         else:

@@ -68,10 +68,17 @@ int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t*
  * Philox4x32-10 stream u(b, k) = (philox(key = seed, ctr = (k>>2, b,
  * offset_lo, offset_hi))[k&3] >> 8) * 2^-24.  draft_probs[r] is node r's
  * cumulative_probability (tree.py:30).  top_p < 1 restricts the target
- * distribution to its nucleus (no counterpart in the reference);
- * do_sample != 0 draws the bonus token from the accepted row's distribution
- * with draw index 2*PTS_MAX_TREE_NODES instead of taking its argmax
- * (verification.py:508-511). */
+ * distribution to its nucleus (no counterpart in the reference): the tokens
+ * whose scaled logit is >= t*, t* the largest logit value whose cumulative
+ * mass from the top (fp64 sum of count(v) * expf(v - m) over the distinct
+ * values v >= t*) reaches top_p * s; inside it p'(x) = bf16(expf(x - m) /
+ * s_N), s_N that mass in fp32.  do_sample != 0 draws the bonus token from
+ * the accepted row's distribution (p' under top-p) instead of taking its
+ * argmax (verification.py:508-511), by inverse CDF with the Philox draw
+ * 2*PTS_MAX_TREE_NODES: the row's rounded probabilities summed in fp64 over
+ * 1024 consecutive segments, the segment sums accumulated in order, the
+ * first index whose running sum exceeds u * total.  Both run the walks in a
+ * second launch after the row statistics (and the nuclei). */
 int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
                          const int32_t* parents, const int32_t* tokens, const float* draft_probs,
                          int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,

@@ -330,3 +330,64 @@ def verify_batch(logits_bits: np.ndarray, row_indptr: Sequence[int], parents, to
         else:
             raise ValueError(f"Unknown verification method: {method!r} (expected 'traversal' or 'exact')")
     return out
+
+
+# ------------------------------------------- top-p target and sampled bonus
+# Neither exists in the reference's acceptance (it takes softmax rows as they
+# are and the bonus by argmax unless do_sample draws it with torch.multinomial,
+# verification.py:508-511); these restate the rules the library states in
+# include/pts_b200.h (pts_accept_traversal), so their parity is unpinned.
+def _expf(d: np.ndarray) -> np.ndarray:
+    return np.exp(np.asarray(d, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def nucleus(row_bits: np.ndarray, temperature: float, top_p: float, m: float, s: float):
+    """(t*, s_N): the smallest logit value of the nucleus and its fp32 mass.
+    Cumulative mass from the top over distinct values: count * expf(v - m)
+    summed in float64, until it reaches top_p * s."""
+    x = scale_logits(row_bits, temperature)
+    vals, counts = np.unique(x, return_counts=True)
+    target = float(np.float32(top_p)) * float(np.float32(s))
+    cum = 0.0
+    for v, c in zip(vals[::-1], counts[::-1]):
+        cum += float(c) * float(_expf(np.float32(v) - np.float32(m)))
+        if cum >= target:
+            return np.float32(v), np.float32(cum)
+    return np.float32(-np.inf), np.float32(cum)
+
+
+def nucleus_probs(row_bits: np.ndarray, temperature: float, m: float, t: float, s_n: float) -> np.ndarray:
+    """p'(x) = bf16(expf(x - m) / s_N) inside the nucleus (x >= t*), else 0."""
+    x = scale_logits(row_bits, temperature)
+    p = round_bf16((_expf(x - np.float32(m)) / np.float32(s_n)).astype(np.float32))
+    return np.where(x >= t, p, np.float32(0.0)).astype(np.float32)
+
+
+def sample_inverse_cdf(p: np.ndarray, u: float, segments: int = 1024) -> int:
+    """First index whose running fp64 sum exceeds u * total; the sums run over
+    ``segments`` consecutive segments (sequential inside each), then over the
+    segment sums in order."""
+    V = p.shape[0]
+    per = (V + segments - 1) // segments
+    p64 = p.astype(np.float64)
+    local = np.zeros(segments, dtype=np.float64)
+    for i in range(segments):
+        seg = p64[min(i * per, V):min((i + 1) * per, V)]
+        if seg.size:
+            local[i] = np.cumsum(seg)[-1]
+    excl = np.zeros(segments, dtype=np.float64)
+    total = 0.0
+    for i in range(segments):
+        excl[i] = total
+        total += local[i]
+    target = float(np.float32(u)) * total
+    for i in range(segments):
+        if excl[i] <= target < excl[i] + local[i]:
+            cum = excl[i]
+            for e in range(min(i * per, V), min((i + 1) * per, V)):
+                if p[e] > 0:
+                    cum += float(p64[e])
+                    if cum > target:
+                        return e
+    nz = np.nonzero(p > 0)[0]
+    return int(nz[-1]) if nz.size else -1

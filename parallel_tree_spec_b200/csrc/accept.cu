@@ -92,6 +92,10 @@ struct AcceptParams {
   int vocab_offset;        // first vocabulary column of this shard
   const float* tok_logit;  // merged mode: per node its token's scaled logit (instead of reading logits)
   int stats_ready;         // merged mode: row_ws is complete, no waiting
+  // top-p (nucleus) target distribution
+  int no_walk;             // row statistics only (the walks run in a later launch)
+  const float* topp_thresh;  // per row: smallest (scaled) logit value inside the nucleus
+  const float* topp_mass;    // per row: sum of exp(x - m) over the nucleus
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -725,7 +729,9 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
       const float x = (tk < 0 || tk >= p.vocab) ? -INFINITY
                       : p.tok_logit ? p.tok_logit[lo + i]
                                     : load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk);
-      const float mb = prob_bf16(x, pm, ps);
+      // nucleus rows: tokens below the threshold get 0, the rest renormalise
+      const float mb = p.topp_mass ? (x >= p.topp_thresh[pr] ? prob_bf16(x, pm, p.topp_mass[pr]) : 0.0f)
+                                   : prob_bf16(x, pm, ps);
       w.val[r.slot].x = mb;
       w.rec[i].ratio = ratio_of(mb, w.val[r.slot].y);
     }
@@ -903,7 +909,7 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
     }
   }
   __syncthreads();
-  if (!s_flag) return;
+  if (!s_flag || p.no_walk) return;
 
   // ---- 3. tree walk (last row CTA of the request) ----------------------------
   walk_request(p, s_b, s_lo, s_n, walk_smem(dyn_smem, p.max_nodes), CtaGroup{}, s_red_i);
@@ -1394,6 +1400,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     // Claims the next request and walks it, waiting for each row it reads
     // (parents' rows, the bonus row) to be published: the walks of different
     // requests run on different SMs while the leaf rows still stream.
+    if (p.no_walk) return;
     if (p.parts_out) {
       // shard partials mode: each node's token logit, if this shard holds the token
       for (int r = c * 32 + lane; r < p.num_rows; r += plan.G * 32) {
@@ -1521,6 +1528,163 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
 }
 
 // ---------------------------------------------------------------------------
+// Top-p (nucleus) target distribution and sampled bonus tokens.  Neither has a
+// counterpart in the reference's acceptance (it renormalises nothing and takes
+// the bonus by argmax unless do_sample, verification.py:508-511), so the rules
+// are stated here and restated exactly by the oracle:
+//   nucleus of a row   all tokens whose (scaled) logit is >= t*, where t* is
+//                      the largest logit value whose cumulative mass from the
+//                      top, sum over values v >= t* of count(v) * expf(v - m)
+//                      (fp64, values in descending order), reaches
+//                      top_p * s (s = the row's fp32 sum of exp(x - m));
+//                      that cumulative mass, rounded to fp32, is the
+//                      nucleus mass s_N; p'(x) = bf16(expf(x - m) / s_N);
+//   sampled bonus      inverse CDF over the accepted row's bf16-rounded
+//                      probabilities (p' under top-p): 1024 consecutive
+//                      segments summed in fp64, their sums accumulated in
+//                      order, target = u * total with u the Philox draw
+//                      2 * PTS_MAX_TREE_NODES of the request's stream; the
+//                      first index whose running sum exceeds the target.
+
+constexpr int kToppThreads = 512;
+constexpr int kToppWindow = 4;           // coarse bins (256 values each) counted per pass
+
+// Order-preserving 16-bit key of a bf16 value (-0 folded onto +0).
+__device__ __forceinline__ uint32_t bf16_key(uint32_t bits) {
+  if (bits == 0x8000u) bits = 0u;
+  return (bits & 0x8000u) ? (~bits & 0xffffu) : (bits | 0x8000u);
+}
+__device__ __forceinline__ float key_bf16(uint32_t key) {
+  const uint32_t bits = (key & 0x8000u) ? (key & 0x7fffu) : (~key & 0xffffu);
+  return __uint_as_float(bits << 16);
+}
+
+__device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uint16_t* row, int e) {
+  return __float_as_uint(load_scaled(p, row, e)) >> 16;
+}
+
+// One CTA per row: counts of every distinct value in a window of kToppWindow
+// coarse bins below the row max, then the cumulative mass from the top; the
+// window moves down until the mass reaches top_p * s.
+__global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p, float top_p, float* thresh,
+                                                             float* mass) {
+  __shared__ uint32_t cnt[kToppWindow * 256];
+  __shared__ int s_done;
+  __shared__ float s_t, s_m;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const RowStat rs = p.row_ws[row];
+  const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
+  const double target = (double)top_p * (double)rs.s;
+  const int top_coarse = (int)(bf16_key(__float_as_uint(rs.m) >> 16) >> 8);
+  double cum = 0.0;                       // thread 0's running mass over the windows
+  if (tid == 0) s_done = 0;
+  for (int hi_c = top_coarse; hi_c >= 0; hi_c -= kToppWindow) {
+    const int lo_c = max(0, hi_c - kToppWindow + 1);
+    const uint32_t lo_key = (uint32_t)lo_c << 8, hi_key = ((uint32_t)hi_c << 8) | 0xffu;
+    for (int i = tid; i < kToppWindow * 256; i += kToppThreads) cnt[i] = 0u;
+    __syncthreads();
+    for (int e = tid; e < p.vocab; e += kToppThreads) {
+      const uint32_t k = bf16_key(scaled_bits(p, rp, e));
+      if (k >= lo_key && k <= hi_key) atomicAdd(&cnt[k - lo_key], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int k = (int)hi_key; k >= (int)lo_key; --k) {
+        const uint32_t c = cnt[k - (int)lo_key];
+        if (!c) continue;
+        const float v = key_bf16((uint32_t)k);
+        cum += (double)c * (double)expf(v - rs.m);
+        if (cum >= target) {
+          s_done = 1;
+          s_t = v;
+          break;
+        }
+      }
+      s_m = (float)cum;
+    }
+    __syncthreads();
+    if (s_done) break;
+  }
+  if (tid == 0) {
+    thresh[row] = s_done ? s_t : -INFINITY;   // the whole row when rounding keeps the mass below the target
+    mass[row] = s_m;
+  }
+}
+
+// One CTA per request: replace the bonus token (the last output, present when
+// the output is one longer than the accepted node's depth) by a draw from the
+// accepted row's distribution.
+__global__ void __launch_bounds__(1024) sample_bonus_kernel(const AcceptParams p) {
+  __shared__ double seg[1024];
+  __shared__ double s_target;
+  __shared__ int s_row, s_skip, s_pick;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  if (tid == 0) {
+    const int32_t* c = p.out_counts + (int64_t)b * 4;
+    const int n_out = c[0], node = c[3];
+    const int lo = p.row_indptr[b];
+    int depth = 0;
+    for (int u = node; u > 0; u = p.parents[lo + u]) ++depth;
+    s_skip = !(n_out > 0 && n_out == depth + 1 && n_out <= p.out_stride);
+    s_row = lo + node;
+    s_pick = -1;
+  }
+  __syncthreads();
+  if (s_skip) return;
+  const int row = s_row;
+  const RowStat rs = p.row_ws[row];
+  const float t = p.topp_thresh ? p.topp_thresh[row] : -INFINITY;
+  const float sn = p.topp_mass ? p.topp_mass[row] : rs.s;
+  const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
+  const int per = (p.vocab + 1023) / 1024;
+  const int e0 = min(tid * per, p.vocab), e1 = min(e0 + per, p.vocab);
+  double local = 0.0;
+  for (int e = e0; e < e1; ++e) {
+    const float x = load_scaled(p, rp, e);
+    if (x >= t) local += (double)prob_bf16(x, rs.m, sn);
+  }
+  seg[tid] = local;
+  __syncthreads();
+  if (tid == 0) {
+    double total = 0.0;
+    for (int i = 0; i < 1024; ++i) {
+      const double v = seg[i];
+      seg[i] = total;                       // exclusive prefix
+      total += v;
+    }
+    s_target = (double)philox_uniform(p.seed, p.offset, (uint32_t)b, 2u * PTS_MAX_TREE_NODES) * total;
+  }
+  __syncthreads();
+  const double target = s_target;
+  if (seg[tid] <= target && target < seg[tid] + local) {
+    double cum = seg[tid];
+    for (int e = e0; e < e1; ++e) {
+      const float x = load_scaled(p, rp, e);
+      if (x < t) continue;
+      cum += (double)prob_bf16(x, rs.m, sn);
+      if (cum > target) {
+        atomicMax(&s_pick, e);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int pick = s_pick;
+    if (pick < 0) {                         // target at the very end: the last token with mass
+      for (int e = p.vocab - 1; e >= 0; --e) {
+        const float x = load_scaled(p, rp, e);
+        if (x >= t && prob_bf16(x, rs.m, sn) > 0.0f) {
+          pick = e;
+          break;
+        }
+      }
+    }
+    if (pick >= 0) p.out_tokens[(int64_t)b * p.out_stride + p.out_counts[(int64_t)b * 4] - 1] = pick;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Vocabulary-sharded (tensor-parallel) acceptance.  Each rank holds the logits
 // of a vocabulary shard; pts_accept_shard_partials reduces them to per-row
 // partials (the persistent streaming kernel in partials mode), the ranks
@@ -1578,7 +1742,7 @@ __global__ void walk_merged_kernel(const AcceptParams p, const int* ties, int sh
   extern __shared__ __align__(128) uint8_t wsm[];
   const int b = blockIdx.x, lane = threadIdx.x & 31;
   const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
-  for (int r = lo + lane; r < lo + n; r += 32) {
+  for (int r = lo + lane; shards > 0 && r < lo + n; r += 32) {
     if (p.row_ws[r].flags & 1) {
       int best = INT_MAX;
       for (int k = 0; k < shards; ++k) best = min(best, ties[(int64_t)k * p.num_rows + r]);
@@ -1589,6 +1753,62 @@ __global__ void walk_merged_kernel(const AcceptParams p, const int* ties, int sh
   walk_request(p, b, lo, n, walk_smem(wsm, p.max_nodes), WarpGroup{}, nullptr);
 }
 
+// Traversal with a top-p target and/or a sampled bonus: row statistics first
+// (no walks), then the nuclei, then the walks from the finished statistics,
+// then the bonus draws.  The nucleus thresholds and masses follow the main
+// workspace.
+size_t topp_ws_bytes(int num_rows) { return align_up((size_t)num_rows * 8, 256); }
+
+int accept_traversal_extended(AcceptParams p, float temperature, float top_p, int do_sample, void* workspace,
+                              size_t ws_bytes, cudaStream_t stream) {
+  size_t opt, orw, orc, oqc, owk;
+  const size_t need = ws_layout(p.num_rows, p.vocab, &opt, &orw, &orc, &oqc, &owk);
+  const bool topp = top_p < 1.0f;
+  if (!workspace || ws_bytes < need + (topp ? topp_ws_bytes(p.num_rows) : 0))
+    return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu (top-p adds %zu)", ws_bytes, need,
+                     topp_ws_bytes(p.num_rows));
+  AcceptParams stats = p;
+  stats.no_walk = 1;
+  int rc = accept_launch(stats, 1, temperature, workspace, ws_bytes, stream);
+  if (rc) return rc;
+  // the launch above filled in the workspace pointers and the scaling
+  AcceptParams q = p;
+  char* ws = (char*)workspace;
+  q.part_ws = (Part*)(ws + opt);
+  q.row_ws = (RowStat*)(ws + orw);
+  q.row_ctr = (unsigned*)(ws + orc);
+  q.req_ctr = (unsigned*)(ws + oqc);
+  q.walk_ctr = (unsigned*)(ws + owk);
+  q.row_done = (unsigned*)(ws + owk + 2 * sizeof(unsigned));
+  q.traversal = 1;
+  q.use_temp = (temperature != 1.0f);
+  q.inv_temp = 1.0f / temperature;
+  q.stats_ready = 1;
+  if (topp) {
+    float* th = (float*)(ws + need);
+    float* ms = th + p.num_rows;
+    topp_kernel<<<p.num_rows, kToppThreads, 0, stream>>>(q, top_p, th, ms);
+    rc = launch_status("topp_kernel");
+    if (rc) return rc;
+    q.topp_thresh = th;
+    q.topp_mass = ms;
+  }
+  const size_t smem = walk_smem_bytes(p.max_nodes);
+  if (smem > kMaxDynSmem) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
+  int dev = 0;
+  PTS_CUDA_TRY(cudaGetDevice(&dev));
+  static size_t attr[256] = {};
+  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
+    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[dev] = smem;
+  }
+  walk_merged_kernel<<<p.batch, 32, smem, stream>>>(q, nullptr, 0);
+  rc = launch_status("walk_merged_kernel");
+  if (rc || !do_sample) return rc;
+  sample_bonus_kernel<<<p.batch, 1024, 0, stream>>>(q);
+  return launch_status("sample_bonus_kernel");
+}
+
 }  // namespace
 }  // namespace pts
 
@@ -1597,7 +1817,7 @@ using namespace pts;
 extern "C" size_t pts_accept_workspace_size(int num_rows, int vocab) {
   size_t a, b, c, d;
   if (num_rows <= 0 || vocab <= 0) return 0;
-  return ws_layout(num_rows, vocab, &a, &b, &c, &d);
+  return ws_layout(num_rows, vocab, &a, &b, &c, &d) + topp_ws_bytes(num_rows);
 }
 
 extern "C" int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
@@ -1633,8 +1853,6 @@ extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, 
                                     size_t workspace_bytes, pts_stream_t stream) {
   if (!draft_probs) return set_error(PTS_ERR_INVALID, "null draft_probs");
   if (!(top_p > 0.0f && top_p <= 1.0f)) return set_error(PTS_ERR_INVALID, "top_p must be in (0, 1]");
-  if (top_p < 1.0f) return set_error(PTS_ERR_UNSUPPORTED, "top_p < 1 is not implemented");
-  if (do_sample) return set_error(PTS_ERR_UNSUPPORTED, "do_sample is not implemented");
   AcceptParams p{};
   p.logits = logits;
   p.row_stride = row_stride;
@@ -1653,7 +1871,8 @@ extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, 
   p.out_tokens = out_tokens;
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
-  return accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
+  if (top_p >= 1.0f && !do_sample) return accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
+  return accept_traversal_extended(p, temperature, top_p, do_sample, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -1810,7 +2029,7 @@ extern "C" int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_
                                             int32_t* out_counts, int out_stride, pts_stream_t stream) {
   if (num_rows <= 0 || vocab <= 0) return set_error(PTS_ERR_INVALID, "need num_rows > 0 and vocab > 0");
   size_t a, b, c, d;
-  const size_t need = ws_layout(num_rows, vocab, &a, &b, &c, &d);
+  const size_t need = ws_layout(num_rows, vocab, &a, &b, &c, &d) + topp_ws_bytes(num_rows);
   if (need > kNoAllocScratchBytes)
     return set_error(PTS_ERR_CAPACITY,
                      "pts_accept_traversal_noalloc: %d rows at vocab %d need %zu bytes of scratch, above the fixed %zu",
