@@ -87,6 +87,26 @@ int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32
                          int32_t* out_counts, int out_stride, void* workspace,
                          size_t workspace_bytes, pts_stream_t stream);
 
+/* verify_tree_exact / verify_tree_traversal over fp32 logits (small fp32
+ * models, for example the reference's 2-layer configuration): the
+ * probabilities stay fp32 as torch's softmax of fp32 logits does
+ * (verification.py:46-55, 310-311), p = expf(x - m) / s; the greedy argmax is
+ * the first index of the largest fp32 probability.  Same outputs as the bf16
+ * entry points; the walks run in a second launch after the row statistics.
+ * Workspace: pts_accept_workspace_size. */
+int pts_accept_greedy_f32(const float* logits, int64_t row_stride, const int32_t* row_indptr,
+                          const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                          int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
+                          int32_t* out_hidden, int32_t* out_counts, int out_stride, void* workspace,
+                          size_t workspace_bytes, pts_stream_t stream);
+int pts_accept_traversal_f32(const float* logits, int64_t row_stride, const int32_t* row_indptr,
+                             const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                             int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                             float temperature, uint64_t philox_seed, uint64_t philox_offset,
+                             int32_t* out_tokens, int32_t* out_hidden, int32_t* out_counts,
+                             int out_stride, void* workspace, size_t workspace_bytes,
+                             pts_stream_t stream);
+
 /* ------------------------------------------------------ vocabulary-sharded acceptance
  * Tensor-parallel acceptance: each rank holds the logits of one vocabulary
  * shard (columns [vocab_offset, vocab_offset + shard_vocab) of the rows the
@@ -246,6 +266,20 @@ int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_ind
                       int num_qo_heads, int num_kv_heads, int head_dim, int page_len,
                       int max_pages, float sm_scale, void* workspace, size_t workspace_bytes,
                       pts_stream_t stream);
+
+/* pts_tree_attn_run for any supported element type and shape: elem_bytes 2
+ * (bf16) or 4 (fp32), head_dim a multiple of 32 up to 256, any page_len.
+ * bf16 / head_dim 128 / page_len 16 / GQA group <= 16 takes the tensor-core
+ * kernel, everything else a SIMT kernel (a correctness path for small fp32
+ * models such as the reference's 2-layer, head_dim-64 configuration).  Same
+ * reference interface as pts_tree_attn_run. */
+int pts_tree_attn_run_any(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                          const int32_t* page_indptr, const int32_t* page_indices,
+                          const int32_t* last_page_len, const uint64_t* mask_bits, int mask_words,
+                          void* out, int batch, int total_q, int max_qo_len, int max_kv_len,
+                          int num_qo_heads, int num_kv_heads, int head_dim, int page_len, int max_pages,
+                          float sm_scale, int elem_bytes, void* workspace, size_t workspace_bytes,
+                          pts_stream_t stream);
 
 /* pts_tree_attn_run with page tables per (request, KV head): head_page_indptr
  * [B*Hkv+1] and head_last_page_len [B*Hkv] indexed b * Hkv + h, every list

@@ -391,3 +391,25 @@ def sample_inverse_cdf(p: np.ndarray, u: float, segments: int = 1024) -> int:
                         return e
     nz = np.nonzero(p > 0)[0]
     return int(nz[-1]) if nz.size else -1
+
+
+# --------------------------------------------------------------- fp32 logits
+def scale_logits_f32(x: np.ndarray, temperature: float) -> np.ndarray:
+    """``logits / temperature`` for fp32 logits as the device computes it
+    (multiply by the fp32 reciprocal; ``verification.py:310``)."""
+    x = np.asarray(x, dtype=np.float32)
+    if temperature == 1.0:
+        return x
+    return (x * (np.float32(1.0) / np.float32(temperature))).astype(np.float32)
+
+
+def row_stats_f32(x: np.ndarray, temperature: float = 1.0):
+    """fp32 softmax rows (``verification.py:46-55`` on fp32 logits): exp in
+    float64 rounded to fp32, row sum in float64 rounded to fp32, p = e / s in
+    fp32; argmax = first index of the largest p.  Returns (argmax, probs)."""
+    x = scale_logits_f32(x, temperature)
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp((x - m).astype(np.float32).astype(np.float64)).astype(np.float32)
+    s = e.astype(np.float64).sum(axis=-1, keepdims=True).astype(np.float32)
+    p = (e / s).astype(np.float32)
+    return np.argmax(p, axis=-1).astype(np.int64), p

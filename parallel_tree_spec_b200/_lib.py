@@ -42,6 +42,10 @@ SIGNATURES = {
     "pts_accept_shard_ties": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, f32, vp, vp, vp]),
     "pts_accept_walk_merged": (C.c_int, [vp, vp, vp, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                          i64, u64, u64, vp, vp, vp, C.c_int, vp]),
+    "pts_accept_greedy_f32": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, vp, vp, vp,
+                                        C.c_int, vp, sz, vp]),
+    "pts_accept_traversal_f32": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, f32,
+                                           u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
     "pts_batch_positions": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_kv_append": (C.c_int, [vp, vp, i64, i64, vp, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_int, vp]),
@@ -49,6 +53,8 @@ SIGNATURES = {
                                  vp, C.c_int, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_tree_mask_from_parents": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "pts_tree_mask_from_bool": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
+    "pts_tree_attn_run_any": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, C.c_int, vp, sz, vp]),
     "pts_tree_attn_run_head_pages": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int,
                                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, sz,
                                                vp]),

@@ -10,10 +10,11 @@ the paged cache + attention over it.  Behind it:
   bitmasks (``pts_tree_mask_from_bool``); a mask whose prefix columns are not
   all true is rejected with ``ValueError``;
 * mode "tree"/"prefill" without a mask and mode "decode": causal rows;
-* append: ``pts_kv_append``; attention: ``pts_tree_attn_run`` (tcgen05).
+* append: ``pts_kv_append``; attention: ``pts_tree_attn_run_any``.
 
-No FlashInfer, no CPU path.  This build's kernel takes bf16, head_dim 128,
-page_len 16 and Hq/Hkv dividing 128.
+No FlashInfer, no CPU path.  bf16 caches with head_dim 128, 16-token pages
+and GQA groups up to 16 run on the tcgen05 kernel; fp32 caches and other
+head dims (multiples of 32 up to 256) on the SIMT kernel.
 """
 from __future__ import annotations
 

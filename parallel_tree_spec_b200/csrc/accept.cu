@@ -96,6 +96,7 @@ struct AcceptParams {
   int no_walk;             // row statistics only (the walks run in a later launch)
   const float* topp_thresh;  // per row: smallest (scaled) logit value inside the nucleus
   const float* topp_mass;    // per row: sum of exp(x - m) over the nucleus
+  const float* logits_f32;   // fp32 logits (instead of bf16): probabilities stay fp32
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -726,6 +727,17 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
       if (i >= n) continue;
       const float pm = __ldcg(&p.row_ws[pr].m), ps = __ldcg(&p.row_ws[pr].s);
       const int tk = w.token[i];
+      if (p.logits_f32) {                                      // fp32 rows: fp32 probabilities
+        float xf = -INFINITY;
+        if (tk >= 0 && tk < p.vocab) {
+          xf = p.logits_f32[(int64_t)pr * p.row_stride + tk];
+          if (p.use_temp) xf = __fmul_rn(xf, p.inv_temp);
+        }
+        const float mbf = __fdiv_rn(expf(xf - pm), ps);
+        w.val[r.slot].x = mbf;
+        w.rec[i].ratio = ratio_of(mbf, w.val[r.slot].y);
+        continue;
+      }
       const float x = (tk < 0 || tk >= p.vocab) ? -INFINITY
                       : p.tok_logit ? p.tok_logit[lo + i]
                                     : load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk);
@@ -1685,6 +1697,101 @@ __global__ void __launch_bounds__(1024) sample_bonus_kernel(const AcceptParams p
 }
 
 // ---------------------------------------------------------------------------
+// fp32 logits (small fp32 models, for example the reference's 2-layer
+// configuration): the probabilities stay fp32, as torch's softmax of fp32
+// logits does (verification.py:46-55).  One CTA per row computes the max, the
+// sum of expf(x - m) (fp64 per thread, combined in thread order) and the
+// argmax of the fp32 probabilities: the first index whose probability
+// expf(x - m) / s equals the max's 1 / s (values just below the max can round
+// to it).  The walks then run from these statistics.
+constexpr int kF32Threads = 512;
+
+__global__ void walk_merged_kernel(const AcceptParams p, const int* ties, int shards);
+
+__device__ __forceinline__ float load_f32(const AcceptParams& p, const float* row, int e) {
+  const float x = row[e];
+  return p.use_temp ? __fmul_rn(x, p.inv_temp) : x;
+}
+
+__global__ void __launch_bounds__(kF32Threads) f32_row_stats_kernel(const AcceptParams p) {
+  __shared__ float s_max[kF32Threads / 32];
+  __shared__ double s_sum[kF32Threads];
+  __shared__ int s_first[kF32Threads / 32];
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* rp = p.logits_f32 + (int64_t)row * p.row_stride;
+  float m = -INFINITY;
+  for (int e = tid; e < p.vocab; e += kF32Threads) m = fmaxf(m, load_f32(p, rp, e));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) s_max[warp] = m;
+  __syncthreads();
+  m = s_max[0];
+  for (int i = 1; i < kF32Threads / 32; ++i) m = fmaxf(m, s_max[i]);
+  double acc = 0.0;
+  for (int e = tid; e < p.vocab; e += kF32Threads) acc += (double)expf(load_f32(p, rp, e) - m);
+  s_sum[tid] = acc;
+  __syncthreads();
+  __shared__ float s_s;
+  if (tid == 0) {
+    double t = 0.0;
+    for (int i = 0; i < kF32Threads; ++i) t += s_sum[i];
+    s_s = (float)t;
+  }
+  __syncthreads();
+  const float sf = s_s;
+  const float pmax = __fdiv_rn(1.0f, sf);
+  int first = INT_MAX;
+  for (int e = tid; e < p.vocab; e += kF32Threads)
+    if (__fdiv_rn(expf(load_f32(p, rp, e) - m), sf) == pmax) {
+      first = e;
+      break;
+    }
+  first = (int)__reduce_min_sync(0xffffffffu, (unsigned)first);
+  if (lane == 0) s_first[warp] = first;
+  __syncthreads();
+  if (tid == 0) {
+    int f = INT_MAX;
+    for (int i = 0; i < kF32Threads / 32; ++i) f = min(f, s_first[i]);
+    RowStat rs;
+    rs.m = m;
+    rs.s = sf;
+    rs.argmax = f;
+    rs.flags = 0;
+    p.row_ws[row] = rs;
+  }
+}
+
+int accept_f32_launch(AcceptParams p, float temperature, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  PTS_CHECK_ARG(p.logits_f32 && p.row_indptr && p.parents && p.tokens, "null input pointer");
+  PTS_CHECK_ARG(p.out_tokens && p.out_hidden && p.out_counts && p.out_stride >= 1, "bad outputs");
+  PTS_CHECK_ARG(p.batch > 0 && p.num_rows >= p.batch && p.vocab > 0 && p.row_stride >= p.vocab, "bad sizes");
+  PTS_CHECK_ARG(p.max_nodes > 0 && temperature > 0.0f, "bad max_nodes or temperature");
+  if (p.max_nodes > PTS_MAX_TREE_NODES)
+    return set_error(PTS_ERR_CAPACITY, "max_nodes %d above PTS_MAX_TREE_NODES %d", p.max_nodes, PTS_MAX_TREE_NODES);
+  size_t opt, orw, orc, oqc, owk;
+  const size_t need = ws_layout(p.num_rows, p.vocab, &opt, &orw, &orc, &oqc, &owk);
+  if (!workspace || ws_bytes < need) return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", ws_bytes, need);
+  p.row_ws = (RowStat*)((char*)workspace + orw);
+  p.use_temp = (temperature != 1.0f);
+  p.inv_temp = 1.0f / temperature;
+  p.stats_ready = 1;
+  f32_row_stats_kernel<<<p.num_rows, kF32Threads, 0, stream>>>(p);
+  int rc = launch_status("f32_row_stats_kernel");
+  if (rc) return rc;
+  const size_t smem = walk_smem_bytes(p.max_nodes);
+  if (smem > kMaxDynSmem) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
+  int dev = 0;
+  PTS_CUDA_TRY(cudaGetDevice(&dev));
+  static size_t attr[256] = {};
+  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
+    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr[dev] = smem;
+  }
+  walk_merged_kernel<<<p.batch, 32, smem, stream>>>(p, nullptr, 0);
+  return launch_status("walk_merged_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // Vocabulary-sharded (tensor-parallel) acceptance.  Each rank holds the logits
 // of a vocabulary shard; pts_accept_shard_partials reduces them to per-row
 // partials (the persistent streaming kernel in partials mode), the ranks
@@ -1972,6 +2079,62 @@ extern "C" int pts_accept_walk_merged(void* row_stats, const float* token_logit,
   }
   walk_merged_kernel<<<batch, 32, smem, (cudaStream_t)stream>>>(p, ties_all, num_shards);
   return launch_status("walk_merged_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// fp32 logits: C ABI.
+
+extern "C" int pts_accept_greedy_f32(const float* logits, int64_t row_stride, const int32_t* row_indptr,
+                                     const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                                     int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
+                                     int32_t* out_hidden, int32_t* out_counts, int out_stride, void* workspace,
+                                     size_t workspace_bytes, pts_stream_t stream) {
+  AcceptParams p{};
+  p.logits_f32 = logits;
+  p.row_stride = row_stride;
+  p.row_indptr = row_indptr;
+  p.parents = parents;
+  p.tokens = tokens;
+  p.batch = batch;
+  p.num_rows = num_rows;
+  p.vocab = vocab;
+  p.max_nodes = max_nodes;
+  p.out_stride = out_stride;
+  p.eos = eos_token_id;
+  p.out_tokens = out_tokens;
+  p.out_hidden = out_hidden;
+  p.out_counts = out_counts;
+  return accept_f32_launch(p, 1.0f, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int pts_accept_traversal_f32(const float* logits, int64_t row_stride, const int32_t* row_indptr,
+                                        const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                                        int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                                        float temperature, uint64_t philox_seed, uint64_t philox_offset,
+                                        int32_t* out_tokens, int32_t* out_hidden, int32_t* out_counts,
+                                        int out_stride, void* workspace, size_t workspace_bytes,
+                                        pts_stream_t stream) {
+  if (!draft_probs) return set_error(PTS_ERR_INVALID, "null draft_probs");
+  AcceptParams p{};
+  p.logits_f32 = logits;
+  p.row_stride = row_stride;
+  p.row_indptr = row_indptr;
+  p.parents = parents;
+  p.tokens = tokens;
+  p.draft_probs = draft_probs;
+  p.batch = batch;
+  p.num_rows = num_rows;
+  p.vocab = vocab;
+  p.max_nodes = max_nodes;
+  p.out_stride = out_stride;
+  p.eos = eos_token_id;
+  p.traversal = 1;
+  p.seed = philox_seed;
+  p.offset = philox_offset;
+  p.out_tokens = out_tokens;
+  p.out_hidden = out_hidden;
+  p.out_counts = out_counts;
+  return accept_f32_launch(p, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

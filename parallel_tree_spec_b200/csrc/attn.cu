@@ -764,3 +764,37 @@ extern "C" int pts_tree_attn_run_head_pages(const void* q, const void* kv_layer,
                           mask_words, out, batch, total_q, max_qo_len, max_kv_len, num_qo_heads, num_kv_heads,
                           head_dim, page_len, max_pages, sm_scale, workspace, workspace_bytes, stream, 1);
 }
+
+namespace pts {
+int tree_attn_simt_launch(const void* q, const void* kv_layer, const int32_t* qo_indptr, const int32_t* page_indptr,
+                          const int32_t* page_indices, const int32_t* last_page_len, const uint64_t* mask_bits,
+                          int mask_words, void* out, int batch, int max_qo_len, int num_qo_heads, int num_kv_heads,
+                          int head_dim, int page_len, int max_pages, float sm_scale, int elem_bytes, int head_pages,
+                          cudaStream_t stream);
+}
+
+extern "C" int pts_tree_attn_run_any(const void* q, const void* kv_layer, const int32_t* qo_indptr,
+                                     const int32_t* page_indptr, const int32_t* page_indices,
+                                     const int32_t* last_page_len, const uint64_t* mask_bits, int mask_words,
+                                     void* out, int batch, int total_q, int max_qo_len, int max_kv_len,
+                                     int num_qo_heads, int num_kv_heads, int head_dim, int page_len, int max_pages,
+                                     float sm_scale, int elem_bytes, void* workspace, size_t workspace_bytes,
+                                     pts_stream_t stream) {
+  PTS_CHECK_ARG(q && kv_layer && qo_indptr && page_indptr && page_indices && last_page_len && out, "null pointer");
+  PTS_CHECK_ARG(batch > 0 && total_q > 0 && max_qo_len > 0, "bad sizes");
+  PTS_CHECK_ARG(num_qo_heads > 0 && num_kv_heads > 0 && num_qo_heads % num_kv_heads == 0, "bad head counts");
+  PTS_CHECK_ARG(page_len > 0 && max_pages > 0, "bad page sizes");
+  if (mask_bits) {
+    if (max_qo_len > PTS_MAX_TREE_NODES)
+      return set_error(PTS_ERR_CAPACITY, "tree of %d rows above %d", max_qo_len, PTS_MAX_TREE_NODES);
+    PTS_CHECK_ARG(mask_words >= (max_qo_len + 63) / 64, "mask_words %d too small for %d rows", mask_words,
+                  max_qo_len);
+  }
+  if (elem_bytes == 2 && head_dim == kD && page_len == kPage && num_qo_heads / num_kv_heads <= 16)
+    return tree_attn_launch(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len, mask_bits, mask_words,
+                            out, batch, total_q, max_qo_len, max_kv_len, num_qo_heads, num_kv_heads, head_dim,
+                            page_len, max_pages, sm_scale, workspace, workspace_bytes, stream, 0);
+  return tree_attn_simt_launch(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len, mask_bits,
+                               mask_words, out, batch, max_qo_len, num_qo_heads, num_kv_heads, head_dim, page_len,
+                               max_pages, sm_scale, elem_bytes, 0, (cudaStream_t)stream);
+}

@@ -51,8 +51,8 @@ def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
 
 # ------------------------------------------------------------------ acceptance
 def _accept_common(logits, row_indptr, parents, tokens):
-    if logits.dtype != torch.bfloat16 or logits.dim() != 2:
-        raise ValueError("logits must be a 2-D bf16 tensor [rows, vocab]")
+    if logits.dtype not in (torch.bfloat16, torch.float32) or logits.dim() != 2:
+        raise ValueError("logits must be a 2-D bf16 or fp32 tensor [rows, vocab]")
     if logits.stride(1) != 1:
         raise ValueError("logits rows must be contiguous")
     dev = _need_cuda(logits, row_indptr, parents, tokens)
@@ -80,7 +80,8 @@ def accept_greedy(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch
         ot, oh, oc = out
     wsz = _lib.lib().pts_accept_workspace_size(R, V)
     ws = workspace(dev, "accept", wsz)
-    _lib.call("pts_accept_greedy", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(), parents.data_ptr(),
+    fn = "pts_accept_greedy_f32" if logits.dtype == torch.float32 else "pts_accept_greedy"
+    _lib.call(fn, logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(), parents.data_ptr(),
               tokens.data_ptr(), B, R, V, mn, -1 if eos_token_id is None else int(eos_token_id), ot.data_ptr(),
               oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
     return ot, oh, oc
@@ -110,6 +111,15 @@ def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
         ot, oh, oc = out
     wsz = _lib.lib().pts_accept_workspace_size(R, V)
     ws = workspace(dev, "accept", wsz)
+    if logits.dtype == torch.float32:
+        if top_p < 1.0 or do_sample:
+            raise ValueError("top_p < 1 and do_sample take bf16 logits in this build")
+        _lib.call("pts_accept_traversal_f32", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
+                  parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr(), B, R, V, mn,
+                  -1 if eos_token_id is None else int(eos_token_id), float(temperature), int(seed) & (2 ** 64 - 1),
+                  int(offset) & (2 ** 64 - 1), ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), ot.shape[1],
+                  ws.data_ptr(), ws.numel(), _stream(dev))
+        return ot, oh, oc
     _lib.call("pts_accept_traversal", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
               parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr(), B, R, V, mn,
               -1 if eos_token_id is None else int(eos_token_id), float(temperature), float(top_p),
@@ -306,12 +316,14 @@ def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Ten
                    page_indices: torch.Tensor, last_page_len: torch.Tensor, mask_bits: Optional[torch.Tensor],
                    max_qo_len: int, max_kv_len: int, sm_scale: Optional[float] = None,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Tree-masked paged attention: q [T, Hq, D] bf16, kv_layer [P, 2, 16, Hkv, D]
-    bf16; ``mask_bits`` None means causal rows."""
+    """Tree-masked paged attention: q [T, Hq, D], kv_layer [P, 2, page_len, Hkv, D],
+    both bf16 or both fp32; ``mask_bits`` None means causal rows.  bf16 with
+    head_dim 128 and 16-token pages runs on the tensor cores, other shapes
+    on the SIMT kernel."""
     dev = _need_cuda(q, kv_layer, qo_indptr, page_indptr, page_indices, last_page_len,
                      *([mask_bits] if mask_bits is not None else []))
-    if q.dtype != torch.bfloat16 or kv_layer.dtype != torch.bfloat16:
-        raise ValueError("tree attention takes bf16 queries and cache")
+    if q.dtype not in (torch.bfloat16, torch.float32) or kv_layer.dtype != q.dtype:
+        raise ValueError("tree attention takes bf16 or fp32 queries and a cache of the same type")
     if not q.is_contiguous() or not kv_layer.is_contiguous():
         raise ValueError("q and kv_layer must be contiguous")
     T, Hq, D = q.shape
@@ -324,11 +336,12 @@ def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Ten
     scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(D)
     wsz = _lib.lib().pts_tree_attn_workspace_size(B, T, Hq, D, int(max_kv_len))
     ws = workspace(dev, "attn", max(wsz, 256))
-    _lib.call("pts_tree_attn_run", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
+    _lib.call("pts_tree_attn_run_any", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
               _i32(page_indptr, "pi").data_ptr(), _i32(page_indices, "px").data_ptr(),
               _i32(last_page_len, "lp").data_ptr(), mask_bits.data_ptr() if mask_bits is not None else None,
               mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T,
-              int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
+              int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, q.element_size(), ws.data_ptr(),
+              ws.numel(), _stream(dev))
     return out
 
 

@@ -15,7 +15,8 @@ stream of (seed, offset, request): ``set_traversal_seed`` fixes the seed
 successive calls draw fresh uniforms.  Given the same uniforms the accepted
 path is the reference's, bit for bit.
 
-Limits of this build: bf16 logits on a CUDA device, ``root_ind == 0`` and
+Limits of this build: bf16 or fp32 logits on a CUDA device (top-p and
+sampled bonuses with bf16), ``root_ind == 0`` and
 ``skip_nodes == 0`` (the only values the reference's own caller passes,
 ``verification.py:569-576``), sibling tokens distinct (the reference's greedy
 walk fails on duplicates, ``verification.py:245-246``).
@@ -107,8 +108,8 @@ def _rows(logits: torch.Tensor) -> torch.Tensor:
     x = logits.reshape(-1, logits.shape[-1])
     if x.device.type != "cuda":
         raise ValueError("logits must be on a CUDA device (this path has no CPU implementation)")
-    if x.dtype != torch.bfloat16:
-        raise ValueError(f"logits must be bf16 (got {x.dtype})")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"logits must be bf16 or fp32 (got {x.dtype})")
     if x.stride(-1) != 1:
         x = x.contiguous()
     return x

@@ -18,6 +18,10 @@ reference's outputs:
 * ``RequestKvCache.reorder_cache_with_offset`` / ``KvCachePool.reorder_cache_with_offset``
   (``cache_manager.py:103-140,196-213``) on small CPU pools
 * ``Tree.create_attention_mask`` (``tree.py:167-194``)
+* the same acceptance functions on fp32 logits (``accept_f32.json``; the
+  logits are the bf16 generator's values plus a seeded fp32 perturbation)
+
+``--f32-only`` writes ``accept_f32.json`` alone.
 """
 from __future__ import annotations
 
@@ -67,6 +71,10 @@ def case_inputs(c):
     x = wl.make_logits(rng, t, c["vocab"], sigma=c["sigma"], plant=c["plant"], soft=c.get("soft", False))
     if c.get("const_rows"):
         x[: c["const_rows"]] = wl._bf16_bits(np.zeros((1, c["vocab"]), np.float32))
+    if c.get("dtype") == "f32":
+        x = (wl._bf16_f32(x) + rng.standard_normal(x.shape).astype(np.float32) * np.float32(1e-3)).astype(np.float32)
+        if c.get("const_rows"):
+            x[: c["const_rows"]] = 0.0
     return t, x
 
 
@@ -74,7 +82,7 @@ def run_accept_case(mods, c):
     Tree, verification = mods
     t, x = case_inputs(c)
     tree = ref_tree(Tree, t)
-    logits = bits_to_torch_bf16(x).unsqueeze(0)
+    logits = (torch.from_numpy(x.copy()) if c.get("dtype") == "f32" else bits_to_torch_bf16(x)).unsqueeze(0)
     eos = c.get("eos")
     if eos == "planted":
         # an accepted-path token when the tree is planted: the root's first child
@@ -155,6 +163,29 @@ def accept_cases():
     return cases
 
 
+def accept_f32_cases():
+    cases = []
+    seed = 5000
+    shapes = [
+        dict(width=2, depth=4, vocab=1024, full=True),     # the 15-node binary tree of the small fp32 model
+        dict(width=4, depth=4, vocab=1024),
+        dict(width=8, depth=8, vocab=1024),
+        dict(width=1, depth=6, vocab=4096),
+    ]
+    for method in ("exact", "traversal"):
+        for sh in shapes:
+            for plant, soft in ((0.0, False), (1.0, True)):
+                for T in ((1.0,) if method == "exact" else (1.0, 0.8)):
+                    cases.append(dict(sh, method=method, seed=seed, sigma=3.0, plant=plant, soft=soft, eos=None,
+                                      temperature=T, philox_seed=11 + seed, philox_offset=seed % 3,
+                                      request=seed % 4, dtype="f32"))
+                    seed += 1
+    cases.append(dict(width=4, depth=3, vocab=1024, method="exact", seed=seed, sigma=3.0, plant=0.0, soft=False,
+                      eos=None, temperature=1.0, philox_seed=3, philox_offset=0, request=0, const_rows=3,
+                      dtype="f32"))
+    return cases
+
+
 def reorder_cases(cache_manager):
     out = []
     rng = np.random.default_rng(7)
@@ -212,6 +243,7 @@ def mask_cases(Tree):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference/src")
+    ap.add_argument("--f32-only", action="store_true")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from parallel_tree_spec.tree import Tree
@@ -219,6 +251,12 @@ def main():
     from parallel_tree_spec.flashinfer import cache_manager
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    acc32 = [run_accept_case((Tree, verification), c) for c in accept_f32_cases()]
+    with open(os.path.join(HERE, "accept_f32.json"), "w") as f:
+        json.dump(acc32, f)
+    print(f"{len(acc32)} fp32 acceptance cases written")
+    if args.f32_only:
+        return
     acc = [run_accept_case((Tree, verification), c) for c in accept_cases()]
     with open(os.path.join(HERE, "accept.json"), "w") as f:
         json.dump(acc, f)

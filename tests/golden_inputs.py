@@ -19,6 +19,10 @@ def case_inputs(c):
     x = wl.make_logits(rng, t, c["vocab"], sigma=c["sigma"], plant=c["plant"], soft=c.get("soft", False))
     if c.get("const_rows"):
         x[: c["const_rows"]] = wl._bf16_bits(np.zeros((1, c["vocab"]), np.float32))
+    if c.get("dtype") == "f32":
+        x = (wl._bf16_f32(x) + rng.standard_normal(x.shape).astype(np.float32) * np.float32(1e-3)).astype(np.float32)
+        if c.get("const_rows"):
+            x[: c["const_rows"]] = 0.0
     return t, x
 
 
