@@ -309,8 +309,20 @@ __device__ void write_counts(const AcceptParams& p, int b, int n_out, int total,
   c[3] = node;
 }
 
+// Correctly rounded a / b for a >= 0 and b > 0 normal, without sending a zero
+// dividend into the division: zero operands leave the division's fast path,
+// and one lane on the slow path holds up the whole warp.
+__device__ __forceinline__ float div_nn(float a, float b) {
+  const float q = __fdiv_rn(a == 0.0f ? 1.0f : a, b);
+  return a == 0.0f ? 0.0f : q;
+}
+__device__ __forceinline__ double ddiv_nn(double a, double b) {
+  const double q = __ddiv_rn(a == 0.0 ? 1.0 : a, b);
+  return a == 0.0 ? 0.0 : q;
+}
+
 __device__ __forceinline__ float ratio_of(float mb, float ms) {
-  return ms > kEps32 ? __fdiv_rn(mb, ms) : 0.0f;
+  return ms > kEps32 ? div_nn(mb, ms) : 0.0f;
 }
 
 // First child of `node` whose token is `tok` (-1: none), by one warp.
@@ -524,11 +536,11 @@ __device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n,
       const double p_old = (double)p_old32;
       const double num = lane == 1 ? fmax(__dsub_rn(__dmul_rn(p_old, (double)old_mb32), (double)old_ms32), 0.0) : S;
       const double den = lane == 1 ? S : __dsub_rn(__dadd_rn(S, 1.0), p_old);
-      q = __ddiv_rn(num, den);
+      q = ddiv_nn(num, den);
       // every lane divides (no divergent branch); valid siblings store (:443-448)
-      const float ms_new = __fdiv_rn(msk, ms_denom32);
-      const float mb_new = __fdiv_rn(tk, S32);
-      const float ratio = __fdiv_rn(mb_new, ms_new > kEps32 ? ms_new : 1.0f);
+      const float ms_new = div_nn(msk, ms_denom32);
+      const float mb_new = div_nn(tk, S32);
+      const float ratio = div_nn(mb_new, ms_new > kEps32 ? ms_new : 1.0f);
       if (vk) {
         w.val[sl] = make_float2(mb_new, ms_new);
         w.rec[ck].ratio = ms_new > kEps32 ? ratio : 0.0f;
@@ -568,15 +580,15 @@ __device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n,
       const double p_old = (double)p_old32;
       const double num = lane == 1 ? fmax(__dsub_rn(__dmul_rn(p_old, (double)old_mb32), (double)old_ms32), 0.0) : S;
       const double den = lane == 1 ? S : __dsub_rn(__dadd_rn(S, 1.0), p_old);
-      q = __ddiv_rn(num, den);
+      q = ddiv_nn(num, den);
       __syncwarp();
       for (int base = 0; base < nc; base += 32) {
         const int sl = s0 + base + lane;
         if (base + lane >= nc || sl == cslot || !w.valid[sl]) continue;
         const float2 v = w.val[sl];
         const float t = fmaxf(__fsub_rn(__fmul_rn(p_old32, v.x), v.y), 0.0f);
-        const float ms_new = __fdiv_rn(v.y, ms_denom32);
-        const float mb_new = __fdiv_rn(t, S32);
+        const float ms_new = div_nn(v.y, ms_denom32);
+        const float mb_new = div_nn(t, S32);
         w.val[sl] = make_float2(mb_new, ms_new);
         w.rec[w.sid[sl]].ratio = ratio_of(mb_new, ms_new);
       }
