@@ -4,12 +4,11 @@
 One step = the verification of one batch of draft trees against the target's
 paged KV cache, for one attention layer, on one GPU:
 
-  1. tree-mask packing from the parent arrays          (pts_tree_mask_from_parents)
-  2. append positions of the tree tokens                (pts_batch_positions)
-  3. append of the tree tokens' K/V into the pages      (pts_kv_append)
-  4. tree-masked paged attention                        (pts_tree_attn_run)
-  5. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
-  6. compaction of each accepted path's KV              (pts_kv_compact)
+  1. tree masks and append positions (one launch)     (pts_tree_prepare)
+  2. append of the tree tokens' K/V into the pages      (pts_kv_append)
+  3. tree-masked paged attention                        (pts_tree_attn_run)
+  4. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
+  5. compaction of each accepted path's KV              (pts_kv_compact)
 
 Workload (default): 16 requests, 4096-token prefix, 65-row trees (root + 8
 levels of 8), 32 query / 8 KV heads, head_dim 128, 16-token pages, logits
@@ -208,20 +207,30 @@ def build_workload(a, device, seed):
     logits[parent_row.to(device), ctok.to(device)] = (rmax[parent_row.to(device)] + boost.to(device)).to(torch.bfloat16)
 
     dev_i32 = lambda x: torch.as_tensor(np.ascontiguousarray(x), dtype=torch.int32, device=device)
+    # the per-step tree inputs in one buffer (parents | tokens | draft probabilities), so a step's
+    # host-to-device transfer is one copy
+    T = B * n
+    tree_in = torch.empty(3 * T, dtype=torch.int32, device=device)
+    tree_in[:T] = dev_i32(par)
+    tree_in[T:2 * T] = dev_i32(tok)
+    tree_in[2 * T:] = torch.as_tensor(dp, dtype=torch.float32, device=device).view(torch.int32)
     W = dict(
         trees=trees, n=n, kv_len=kv_len, layer=layer, pool=layer.view(1, *layer.shape), q=q, k_new=k_new,
-        v_new=v_new, logits=logits,
-        qo_indptr=dev_i32(indptr), parents=dev_i32(par), tokens=dev_i32(tok),
-        draft_probs=torch.as_tensor(dp, dtype=torch.float32, device=device),
+        v_new=v_new, logits=logits, tree_in=tree_in,
+        qo_indptr=dev_i32(indptr), parents=tree_in[:T], tokens=tree_in[T:2 * T],
+        draft_probs=tree_in[2 * T:].view(torch.float32),
         page_indptr=dev_i32(np.arange(B + 1) * pages_per), page_indices=perm.contiguous(),
         last_page_len=dev_i32(np.full(B, (kv_len - 1) % pl + 1)), seq_lens=dev_i32(np.full(B, kv_len)),
         offsets=dev_i32(np.full(B, P)), mask_words=K.mask_words_for(n),
         host=dict(parents=par, tokens=tok, draft_probs=dp, indptr=indptr),
     )
     W["out"] = torch.empty_like(q)
-    W["ot"] = torch.empty(B, n, dtype=torch.int32, device=device)
-    W["oh"] = torch.empty(B, n, dtype=torch.int32, device=device)
-    W["oc"] = torch.empty(B, 4, dtype=torch.int32, device=device)
+    # the per-step results in one buffer (tokens | hidden indices | counts): one device-to-host copy
+    res = torch.empty(2 * B * n + 4 * B, dtype=torch.int32, device=device)
+    W["res"] = res
+    W["ot"] = res[:B * n].view(B, n)
+    W["oh"] = res[B * n:2 * B * n].view(B, n)
+    W["oc"] = res[2 * B * n:].view(B, 4)
     W["bits"] = torch.empty(B * n, W["mask_words"], dtype=torch.int64, device=device)
     W["bi"] = torch.empty(B * n, dtype=torch.int32, device=device)
     W["pos"] = torch.empty(B * n, dtype=torch.int32, device=device)
@@ -243,17 +252,16 @@ class Step:
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
-        self.launches_per_step = 6
+        self.launches_per_step = 5
 
     def run(self, ev=None):
         from parallel_tree_spec_b200._lib import check
         a, W, L, s = self.a, self.W, self.L, self.stream
         B, n = a.batch, W["n"]
         P = W["page_indptr"]
-        check(L.pts_tree_mask_from_parents(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), B, B * n,
-                                           W["mask_words"], W["bits"].data_ptr(), s), "mask")
-        check(L.pts_batch_positions(W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(), B, B * n,
-                                    W["bi"].data_ptr(), W["pos"].data_ptr(), s), "positions")
+        check(L.pts_tree_prepare(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(), B,
+                                 W["mask_words"], W["bits"].data_ptr(), W["bi"].data_ptr(), W["pos"].data_ptr(), s),
+              "prepare")
         lay = W["layer"]
         check(L.pts_kv_append(W["k_new"].data_ptr(), W["v_new"].data_ptr(), a.hkv * 128, a.hkv * 128, lay.data_ptr(),
                               W["bi"].data_ptr(), W["pos"].data_ptr(), P.data_ptr(), W["page_indices"].data_ptr(),
@@ -478,23 +486,16 @@ def run_e2e(a, W, step, device):
     tokens / hidden indices / counts are read back every step."""
     import torch
     h = W["host"]
-    hp = torch.from_numpy(h["parents"]).pin_memory()
-    ht = torch.from_numpy(h["tokens"]).pin_memory()
-    hd = torch.from_numpy(h["draft_probs"]).pin_memory()
-    ot = torch.empty_like(W["ot"], device="cpu").pin_memory()
-    oh = torch.empty_like(W["oh"], device="cpu").pin_memory()
-    oc = torch.empty_like(W["oc"], device="cpu").pin_memory()
-    h2d = hp.numel() * 4 + ht.numel() * 4 + hd.numel() * 4
-    d2h = ot.numel() * 4 + oh.numel() * 4 + oc.numel() * 4
+    hin = torch.cat([torch.from_numpy(h["parents"].astype(np.int32)), torch.from_numpy(h["tokens"].astype(np.int32)),
+                     torch.from_numpy(h["draft_probs"].astype(np.float32)).view(torch.int32)]).pin_memory()
+    hres = torch.empty_like(W["res"], device="cpu").pin_memory()
+    h2d = hin.numel() * 4
+    d2h = hres.numel() * 4
 
     def one():
-        W["parents"].copy_(hp, non_blocking=True)
-        W["tokens"].copy_(ht, non_blocking=True)
-        W["draft_probs"].copy_(hd, non_blocking=True)
+        W["tree_in"].copy_(hin, non_blocking=True)
         step.run()
-        ot.copy_(W["ot"], non_blocking=True)
-        oh.copy_(W["oh"], non_blocking=True)
-        oc.copy_(W["oc"], non_blocking=True)
+        hres.copy_(W["res"], non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
 
     for _ in range(3):
@@ -577,8 +578,8 @@ def run_tp(a):
     res = {}
 
     def one(ev=None):
-        check(L.pts_tree_mask_from_parents(parents.data_ptr(), qo.data_ptr(), B, T, mw, bits.data_ptr(), s), "mask")
-        check(L.pts_batch_positions(qo.data_ptr(), seqlens.data_ptr(), B, T, bi.data_ptr(), pos.data_ptr(), s), "pos")
+        check(L.pts_tree_prepare(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw, bits.data_ptr(),
+                                 bi.data_ptr(), pos.data_ptr(), s), "prepare")
         check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), hkv * D, hkv * D, layer.data_ptr(), bi.data_ptr(),
                               pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, hkv, D, pl, max_pages, 2, s), "app")
         if ev is not None:
@@ -713,8 +714,8 @@ def run_sparse(a):
     s = torch.cuda.current_stream(dev).cuda_stream
 
     def one(ev=None):
-        check(L.pts_tree_mask_from_parents(parents.data_ptr(), qo.data_ptr(), B, T, mw, bits.data_ptr(), s), "mask")
-        check(L.pts_batch_positions(qo.data_ptr(), seqlens.data_ptr(), B, T, bi.data_ptr(), pos.data_ptr(), s), "pos")
+        check(L.pts_tree_prepare(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw, bits.data_ptr(),
+                                 bi.data_ptr(), pos.data_ptr(), s), "prepare")
         check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), Hkv * D, Hkv * D, layer.data_ptr(), bi.data_ptr(),
                               pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, Hkv, D, pl, max_pages, 2, s), "app")
         if ev is not None:

@@ -241,6 +241,17 @@ int pts_tree_mask_from_parents(const int32_t* parents, const int32_t* qo_indptr,
                                int total_q, int mask_words, uint64_t* mask_bits,
                                pts_stream_t stream);
 
+/* Once per tree step, in one launch: the ancestor bitmasks of every row
+ * (pts_tree_mask_from_parents) and, when batch_indices / positions are
+ * given, the append batch index and position of every tree token
+ * (pts_batch_positions with one segment per request, seq_lens including the
+ * tree).  Replaces Tree.create_attention_mask + the mask packing of
+ * prepareAttention (tree.py:167-194, attention_wrapper.py:141) and
+ * flashinfer.get_batch_indices_positions (cache_manager.py:263-271). */
+int pts_tree_prepare(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens, int batch,
+                     int mask_words, uint64_t* mask_bits, int32_t* batch_indices, int32_t* positions,
+                     pts_stream_t stream);
+
 /* Pack a boolean custom mask [sum_b N_b * kv_len_b] (FlashInfer's flattened
  * custom_mask, flashinfer/attention_wrapper.py:141) into tree bitmasks.
  * Columns before kv_len_b - N_b must all be true; *bad_rows (device int,

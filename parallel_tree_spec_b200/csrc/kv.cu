@@ -130,6 +130,47 @@ __global__ void mask_from_parents_kernel(const int32_t* __restrict__ parents, co
   }
 }
 
+// One CTA per request: the tree's parents staged in shared memory, then per
+// row the ancestor bitmask (each word from one walk up the chain) and, when
+// asked, the append batch index and position of the row's token.
+__global__ void tree_prepare_kernel(const int32_t* __restrict__ parents, const int32_t* __restrict__ qo_indptr,
+                                    const int32_t* __restrict__ seq_lens, int words, uint64_t* __restrict__ bits,
+                                    int32_t* __restrict__ batch_indices, int32_t* __restrict__ positions) {
+  __shared__ int16_t sp[PTS_MAX_TREE_NODES];
+  const int b = blockIdx.x;
+  const int base = qo_indptr[b], n = qo_indptr[b + 1] - base;
+  const bool staged = n <= PTS_MAX_TREE_NODES;
+  if (staged)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int p = parents[base + i];
+      sp[i] = (int16_t)((p >= 0 && p < i) ? p : -1);
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    uint64_t* out = bits + (int64_t)(base + i) * words;
+    for (int w = 0; w < words; ++w) {
+      uint64_t acc = 0ull;
+      int node = i;
+      for (int guard = 0; node >= 0 && guard <= PTS_MAX_TREE_NODES; ++guard) {
+        if ((node >> 6) == w) acc |= 1ull << (node & 63);
+        int p;
+        if (staged) {
+          p = sp[node];
+        } else {
+          p = parents[base + node];
+          p = (p >= 0 && p < node) ? p : -1;
+        }
+        node = p;
+      }
+      out[w] = acc;
+    }
+    if (positions) {
+      batch_indices[base + i] = b;
+      positions[base + i] = seq_lens[b] - n + i;
+    }
+  }
+}
+
 // One warp per row of the flattened boolean custom mask.
 __global__ void mask_from_bool_kernel(const uint8_t* __restrict__ mask, const int32_t* __restrict__ qo_indptr,
                                       const int32_t* __restrict__ mask_indptr, const int32_t* __restrict__ kv_lens,
@@ -261,4 +302,16 @@ extern "C" int pts_tree_mask_from_bool(const uint8_t* mask, const int32_t* qo_in
   mask_from_bool_kernel<<<(total_q + 3) / 4, 128, 0, (cudaStream_t)stream>>>(
       mask, qo_indptr, mask_indptr, kv_lens, batch, total_q, mask_words, mask_bits, bad_rows);
   return launch_status("mask_from_bool_kernel");
+}
+
+extern "C" int pts_tree_prepare(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens, int batch,
+                                int mask_words, uint64_t* mask_bits, int32_t* batch_indices, int32_t* positions,
+                                pts_stream_t stream) {
+  PTS_CHECK_ARG(parents && qo_indptr && mask_bits, "null pointer");
+  PTS_CHECK_ARG(batch > 0 && mask_words > 0, "bad sizes");
+  PTS_CHECK_ARG((batch_indices == nullptr) == (positions == nullptr) && (!positions || seq_lens),
+                "batch_indices, positions and seq_lens go together");
+  tree_prepare_kernel<<<batch, 128, 0, (cudaStream_t)stream>>>(parents, qo_indptr, seq_lens, mask_words, mask_bits,
+                                                              batch_indices, positions);
+  return launch_status("tree_prepare_kernel");
 }

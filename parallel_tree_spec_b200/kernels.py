@@ -289,6 +289,25 @@ def tree_mask_from_parents(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_
     return bits
 
 
+def tree_prepare(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_words: int,
+                 seq_lens: Optional[torch.Tensor] = None):
+    """One launch per tree step: ancestor bitmasks [T, mask_words] and, with
+    ``seq_lens``, the append batch indices and positions of the tree tokens."""
+    dev = _need_cuda(parents, qo_indptr)
+    parents, qo_indptr = _i32(parents, "parents"), _i32(qo_indptr, "qo_indptr")
+    T = parents.numel()
+    bits = torch.empty(T, mask_words, dtype=torch.int64, device=dev)
+    bi = pos = None
+    if seq_lens is not None:
+        bi = torch.empty(T, dtype=torch.int32, device=dev)
+        pos = torch.empty(T, dtype=torch.int32, device=dev)
+    _lib.call("pts_tree_prepare", parents.data_ptr(), qo_indptr.data_ptr(),
+              _i32(seq_lens, "seq_lens").data_ptr() if seq_lens is not None else None, qo_indptr.numel() - 1,
+              mask_words, bits.data_ptr(), bi.data_ptr() if bi is not None else None,
+              pos.data_ptr() if pos is not None else None, _stream(dev))
+    return bits, bi, pos
+
+
 def tree_mask_from_bool(mask: torch.Tensor, qo_indptr: torch.Tensor, mask_indptr: torch.Tensor,
                         kv_lens: torch.Tensor, mask_words: int, total_q: Optional[int] = None,
                         check: bool = True) -> torch.Tensor:

@@ -146,3 +146,22 @@ def test_tree_masks_vs_oracle():
         K.tree_mask_from_bool(torch.from_numpy(bad).to(DEV), torch.from_numpy(indptr).to(DEV),
                               torch.tensor(mind, dtype=torch.int32, device=DEV),
                               torch.tensor(kvl, dtype=torch.int32, device=DEV), words)
+
+
+def test_tree_prepare_matches_masks_and_positions():
+    """pts_tree_prepare (one launch) = pts_tree_mask_from_parents + pts_batch_positions,
+    including a 1024-node chain (words = 16) and a root-only tree."""
+    rng = np.random.default_rng(12)
+    trees = [wl.make_tree(rng, w, d, 500) for (w, d) in [(8, 8), (0, 0), (16, 8), (1, 1023), (3, 5)]]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    T = int(indptr[-1])
+    words = K.mask_words_for(max(t.size for t in trees))
+    dpar, dind = torch.from_numpy(par).to(DEV), torch.from_numpy(indptr).to(DEV)
+    seq = torch.tensor([t.size + int(rng.integers(0, 300)) for t in trees], dtype=torch.int32, device=DEV)
+    bits, bi, pos = K.tree_prepare(dpar, dind, words, seq)
+    ref_bits = K.tree_mask_from_parents(dpar, dind, words)
+    rbi, rpos = K.batch_positions(dind, seq, T)
+    assert torch.equal(bits, ref_bits)
+    assert torch.equal(bi, rbi) and torch.equal(pos, rpos)
+    bits2, none_bi, none_pos = K.tree_prepare(dpar, dind, words)
+    assert torch.equal(bits2, ref_bits) and none_bi is None and none_pos is None
