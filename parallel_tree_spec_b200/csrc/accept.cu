@@ -273,11 +273,13 @@ struct WalkSmem {
   int16_t* path_rmax;
   float* path_pa;          // during set-up: the nodes' Ms
   float* uni;              // 2 * cap + 2 uniforms
+  float* xtok;             // by node (lazy walks): its token's scaled logit under its parent's row
+  uint8_t* expanded;       // by node (lazy walks): its children's Mb are in place
 };
 
 __host__ __device__ inline size_t walk_smem_bytes(int cap) {
   cap = (cap + 15) & ~15;
-  return (size_t)cap * (32 + 4 + 8 + 2 + 1 + 2 + 2 + 4) + (size_t)(2 * cap + 2) * 4 + 160;
+  return (size_t)cap * (32 + 4 + 8 + 2 + 1 + 2 + 2 + 4 + 4 + 1) + (size_t)(2 * cap + 2) * 4 + 192;
 }
 
 __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
@@ -298,6 +300,8 @@ __device__ inline WalkSmem walk_smem(uint8_t* base, int cap) {
   w.path = (int16_t*)take((size_t)cap * 2);
   w.path_rmax = (int16_t*)take((size_t)cap * 2);
   w.valid = (uint8_t*)take((size_t)cap);
+  w.xtok = (float*)take((size_t)cap * 4);
+  w.expanded = (uint8_t*)take((size_t)cap);
   return w;
 }
 
@@ -422,6 +426,100 @@ __device__ void traversal_output(const AcceptParams& p, int b, int lo, int accep
   write_counts(p, b, n_out > p.out_stride ? -2 : n_out, n_out, n_out > 0 ? n_out - 1 : 0, accepted);
 }
 
+// ---- lazy walks (persistent kernel) ------------------------------------------
+// The walker warp starts a traversal walk as soon as the request's tree is
+// loaded; an expander warp of the same CTA fills in each internal node's
+// children's Mb when the node's row is published, and the walker waits (in
+// shared memory) only when it descends through a node not yet expanded.  The
+// stream order hands every request its internal rows in walk order, so the
+// walk overlaps the streaming instead of following it.
+
+// Target probability of a node's token (scaled logit x) under its parent's
+// row (m, s): the softmax entry (verification.py:349), renormalised over the
+// nucleus under top-p, fp32 for fp32 logits.
+__device__ __forceinline__ float node_mb(const AcceptParams& p, float x, int prow, float m, float s) {
+  if (p.logits_f32) return __fdiv_rn(expf(x - m), s);
+  if (p.topp_mass) return x >= p.topp_thresh[prow] ? prob_bf16(x, m, p.topp_mass[prow]) : 0.0f;
+  return prob_bf16(x, m, s);
+}
+
+// One thread: node v's children's Mb and Mb/Ms from v's published row.
+__device__ void expand_node(const AcceptParams& p, int lo, const WalkSmem& w, int v) {
+  const float m = __ldcg(&p.row_ws[lo + v].m), s = __ldcg(&p.row_ws[lo + v].s);
+  const NodeRec rv = w.rec[v];
+  for (int k = 0; k < rv.child_cnt; ++k) {
+    const int sl = rv.child_start + k;
+    const int c = w.sid[sl];
+    const float mb = node_mb(p, w.xtok[c], lo + v, m, s);
+    w.val[sl].x = mb;
+    w.rec[c].ratio = ratio_of(mb, w.val[sl].y);
+  }
+}
+
+// Walker (whole warp, one node): bounded wait until node u is expanded; the
+// fence after the flag orders the expander's stores before the walker's loads.
+__device__ __forceinline__ bool wait_expanded(const WalkSmem& w, int u) {
+  const volatile uint8_t* f = w.expanded + u;
+  if (*f) {
+    __threadfence_block();
+    return true;
+  }
+  const long long t0 = clock64();
+  for (;;) {
+    __nanosleep(32);
+    if (__all_sync(0xffffffffu, *f != 0)) {
+      __threadfence_block();
+      return true;
+    }
+    if (__any_sync(0xffffffffu, clock64() - t0 > kRowWaitLimit)) return false;
+  }
+}
+
+// Expander (whole warp): expands request b's internal nodes as their rows are
+// published.  Lane l owns nodes l, l + 32, ...; each pass polls the owned
+// pending nodes' publication flags with independent relaxed loads (the fence
+// after a set flag makes the row's statistics visible), expands the
+// published ones and sets their flags.  Returns when no node is pending, the
+// walk has ended (*walk_done) or the wait limit passed.
+__device__ void expand_request(const AcceptParams& p, int lo, int n, const WalkSmem& w, const volatile int* walk_done) {
+  const int lane = threadIdx.x & 31;
+  uint32_t pending = 0;                                    // bit j: node lane + 32 j
+  for (int j = 0; lane + 32 * j < n; ++j)
+    if (w.rec[lane + 32 * j].child_cnt > 0) pending |= 1u << j;
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ready = 0;
+    if (p.stats_ready) {
+      ready = pending;
+    } else {
+      for (int j0 = 0; j0 < 32 && (pending >> j0); j0 += 4) {
+        unsigned f[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          f[q] = 0;
+          if ((pending >> (j0 + q)) & 1u)
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];"
+                         : "=r"(f[q]) : "l"(p.row_done + lo + lane + 32 * (j0 + q)) : "memory");
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (f[q]) ready |= 1u << (j0 + q);
+      }
+      if (ready) __threadfence();
+    }
+    for (uint32_t r = ready; r; r &= r - 1) {
+      const int v = lane + 32 * (__ffs(r) - 1);
+      expand_node(p, lo, w, v);
+      __threadfence_block();
+      *(volatile uint8_t*)(w.expanded + v) = 1;
+    }
+    pending &= ~ready;
+    if (!__any_sync(0xffffffffu, pending != 0u)) return;
+    if (__any_sync(0xffffffffu, *walk_done != 0 || clock64() - t0 > kRowWaitLimit)) return;
+    __nanosleep(64);
+  }
+}
+
 // Traversal verification (verify_tree_traversal, verification.py:377-524) by
 // one warp.  The loop is sequential (each iteration depends on the last), so
 // the warp keeps its dependent chain short: every lane computes the same
@@ -435,6 +533,7 @@ __device__ void traversal_output(const AcceptParams& p, int b, int lo, int accep
 // division (lanes 0 and 1).  Fp32 tensor and fp64 scalar operations are
 // replayed with explicitly rounded operations in the reference's order.  See
 // the file comment for the lazily evaluated p_alpha.
+template <bool kLazy = false>
 __device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w) {
   const int lane = threadIdx.x & 31;
   constexpr unsigned kFull = 0xffffffffu;
@@ -456,7 +555,12 @@ __device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n,
     NodeRec ru = w.rec[u];
     float pa_u = w.path_pa[depth];
     int rmax_u = w.path_rmax[depth];
+    bool late = false;
     while (ru.first_valid >= 0) {
+      if (kLazy && !wait_expanded(w, u)) {             // u's children's Mb come from u's row
+        late = true;
+        break;
+      }
       const int c = ru.first_valid;
       const NodeRec rc = w.rec[c];
       const int rmax = max(rmax_u, (int)ru.reset_t);
@@ -471,6 +575,10 @@ __device__ void walk_traversal_warp(const AcceptParams& p, int b, int lo, int n,
       ru = rc;
       pa_u = pa;
       rmax_u = rmax;
+    }
+    if (late) {
+      if (lane == 0) write_counts(p, b, -3, 0, 0, 0);
+      return;
     }
     const int cand = u;
     if (eta < pa_u) {                                                 // :395-400
@@ -633,11 +741,15 @@ struct WarpGroup {
 // (traversal) wait for the parents' rows and compute the target probability
 // of every node's token under its parent's row, and walk.  Work that needs no
 // row statistics comes first, so it overlaps the streaming.
-template <class G>
-__device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
+//
+// kLazy (the persistent kernel's traversal walker): the set-up only, with each
+// node's token logit read and every expansion flag cleared; returns whether
+// the walk is to run (the caller runs it against its expander warp).
+template <bool kLazy = false, class G>
+__device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
   if (n <= 0 || n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
-    return;
+    return false;
   }
   int* cnt = reinterpret_cast<int*>(w.val);               // child counts, then slot bases
   int* basep = cnt + ((n + 1) & ~1);
@@ -670,7 +782,7 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
   g.sync();
   if (bad) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
-    return;
+    return false;
   }
   if (g.rank() < 32) {
     // child runs: exclusive scan of the counts, then a stable scatter of the
@@ -724,6 +836,25 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
     w.valid[sl] = 1;
   }
   g.sync();
+  if (kLazy && p.traversal) {
+    for (int i = g.rank(); i < n; i += g.size()) {
+      float x = -INFINITY;
+      const int tk = w.token[i];
+      if (i > 0 && tk >= 0 && tk < p.vocab) {
+        const int pr = lo + w.rec[i].parent;
+        if (p.logits_f32) {
+          x = p.logits_f32[(int64_t)pr * p.row_stride + tk];
+          if (p.use_temp) x = __fmul_rn(x, p.inv_temp);
+        } else {
+          x = p.tok_logit ? p.tok_logit[lo + i] : load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk);
+        }
+      }
+      w.xtok[i] = x;
+      w.expanded[i] = 0;
+    }
+    g.sync();
+    return true;
+  }
   if (p.traversal) {
     // Mb[i] = p[parent(i), token(i)] (:349) once the parent's row is published
     // (the warps wait with warp-uniform loops and stay converged)
@@ -763,13 +894,14 @@ __device__ void walk_request(const AcceptParams& p, int b, int lo, int n, const 
     g.sync();
     if (late) {
       if (g.rank() == 0) write_counts(p, b, -3, 0, 0, 0);
-      return;
+      return false;
     }
     if (g.rank() < 32) walk_traversal_warp(p, b, lo, n, w);
   } else if (g.rank() < 32) {
     walk_greedy_warp(p, b, lo, w);
   }
   g.sync();
+  return false;
 }
 
 // Request of `row`: the warp finds the last request whose first row is <= row
@@ -960,17 +1092,21 @@ __global__ void __launch_bounds__(kThreads, 4) accept_kernel(const AcceptParams 
 //   warp 17       merger: combines the 16 warp partials of a row (or of a chunk
 //                 of a split row), derives the row statistics with the tie
 //                 rescan, and counts the request's finished rows;
-//   warp 18       walker: claims the next slot of the workspace's publication
-//                 list and runs the tree walk of the request the mergers publish
-//                 there (the walks of different requests run on different SMs,
-//                 each as soon as the request's last row is done, while the
-//                 other warps stream the following rows).
+//   warp 18       walker: claims the next request (a grid-wide counter) and
+//                 runs its tree walk (the walks of different requests run on
+//                 different SMs while the other warps stream); a traversal
+//                 walk starts as soon as the tree is loaded and waits only for
+//                 nodes whose rows have not streamed yet;
+//   warp 19       expander (traversal): fills in the walked request's
+//                 children's target probabilities row by row as the rows are
+//                 published (named barriers 1 and 2 pair it with the walker).
 constexpr int kSChunk = 16384;                 // elements per item (32 KB)
 constexpr int kSSlots = 5;
 constexpr int kSConsumerWarps = 16;
 constexpr int kSConsumers = kSConsumerWarps * 32;
-constexpr int kSThreads = kSConsumers + 96;    // + producer, merger and walker warps
+constexpr int kSThreads = kSConsumers + 128;   // + producer, merger, walker and expander warps
 constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (4)
+constexpr int kSPolyPairs = 0;                     // of the 16 value pairs per chunk, exponentials by ex2_poly2
 constexpr long long kSpinLimit = 4000000000ll;     // clock cycles, about 2 s
 constexpr size_t kMaxDynSmem = 232448;             // 227 KB per CTA
 
@@ -981,6 +1117,8 @@ struct __align__(16) StreamCtl {
   uint64_t seg_empty[2];      // the merger has read them
   unsigned long long seg_max; // (segment + 1) << 32 | key of the largest value any warp located in it
   Part seg[2][kSConsumerWarps];
+  int walk_b;                 // the walker's request for the expander (-1: no more, -2: skip)
+  int walk_done;              // the walker has finished the request's walk
 };
 
 constexpr size_t kSRingBytes = (size_t)kSSlots * kSChunk * 2;
@@ -989,24 +1127,31 @@ constexpr size_t kSWalkOff = (kSCtlOff + sizeof(StreamCtl) + 127) & ~(size_t)127
 
 // The work of CTA c.  Rows are taken in "stream order": the internal rows
 // (every request's root and every row with children) of all requests first,
-// then the leaf rows, each group in row order.  Position q of the stream order
-// is a whole row of CTA q % G while q < split_first_row; the remaining
-// num_rows % G positions are split by chunk over all CTAs.  A traversal walk
-// needs the statistics of internal rows only (its target probabilities come
-// from the parents' rows) and one leaf row at most (the bonus token), so the
-// walks start while the leaf rows still stream.
+// then the leaf rows in row order.  Internal rows go in row order, or (dfs)
+// ordered by their rank in the depth-first preorder of their tree, the
+// requests interleaved at each rank: the order in which traversal walks
+// descend through them, so every walk receives its rows while it runs.
+// Position q of the stream order is a whole row of CTA q % G while
+// q < split_first_row; when every CTA streams fewer than four rows, the
+// remaining num_rows % G positions are split by chunk over all CTAs.  A
+// traversal walk needs the statistics of internal rows only (its target
+// probabilities come from the parents' rows) and one leaf row at most (the
+// bonus token), so the walks start while the leaf rows still stream.
 struct StreamPlan {
-  int G, nchunks, whole_rows_per_cta, split_first_row, split_items;
+  int G, nchunks, whole_rows_per_cta, split_first_row, split_items;   // whole_rows_per_cta: the most of any CTA
   int num_rows, mask_words;
+  int dfs, key_bits;          // depth-first order of the internal rows; bits per level of its keys
+  int walkers;                // CTAs G .. G + walkers - 1 only walk (0: every CTA streams and walks)
+  __device__ int whole_rows(int c) const { return c < split_first_row ? (split_first_row - c + G - 1) / G : 0; }
   __device__ int items(int c) const {
     const int extra = split_items > c ? (split_items - c + G - 1) / G : 0;
-    return whole_rows_per_cta * nchunks + extra;
+    return whole_rows(c) * nchunks + extra;
   }
   // row, chunk and whether item k ends a segment (a whole row, or one split
   // chunk); `mine` lists the CTA's whole rows, `split` the split rows
   __device__ void item(int c, int k, const uint16_t* mine, const uint16_t* split, int& row, int& chunk,
                        bool& seg_end, bool& whole) const {
-    const int n1 = whole_rows_per_cta * nchunks;
+    const int n1 = whole_rows(c) * nchunks;
     if (k < n1) {
       row = mine[k / nchunks];
       chunk = k % nchunks;
@@ -1026,24 +1171,41 @@ struct StreamPlan {
 // batches search it in global memory).
 constexpr int kSmemIndptr = 4096;
 
+// Largest launch whose internal rows go in depth-first order (the prologue's
+// rank search is O(rows * (tree + batch)) per CTA).
+constexpr int kDfsMaxRows = 4096, kDfsMaxBatch = 256, kDfsMaxNodes = 256;
+
 // Shared-memory bytes of the stream-order tables (internal-row bit mask, the
-// CTA's whole rows, the split rows, scan scratch, a copy of row_indptr),
-// placed after the walk state.
+// CTA's whole rows, the split rows, scan scratch, a copy of row_indptr; dfs:
+// the rows' preorder keys and the requests' internal-row counts), placed after
+// the walk state.
 __host__ __device__ inline size_t order_smem_bytes(const StreamPlan& pl, int batch) {
-  return (size_t)pl.mask_words * 4 + (((size_t)pl.whole_rows_per_cta * 2 + 15) & ~(size_t)15) +
-         (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4 +
-         (batch < kSmemIndptr ? (size_t)(batch + 1) * 4 : 0);
+  const size_t base = (size_t)pl.mask_words * 4 + (((size_t)pl.whole_rows_per_cta * 2 + 15) & ~(size_t)15) +
+                      (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4 +
+                      (batch < kSmemIndptr ? (size_t)(batch + 1) * 4 : 0);
+  return pl.dfs ? ((base + 7) & ~(size_t)7) + (size_t)pl.num_rows * 12 + (size_t)batch * 4 +
+                       (size_t)(kDfsMaxNodes + 1) * 4 + 16
+                 : base;
 }
 
 // First row of the request that holds `row` (binary search over row_indptr).
-__device__ __forceinline__ int request_first_row(const int32_t* indptr, int batch, int row) {
+// Barrier `id` over `count` threads (whole warps) of the CTA.
+__device__ __forceinline__ void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ int request_index(const int32_t* indptr, int batch, int row) {
   int lo = 0, hi = batch - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (indptr[mid] <= row) lo = mid;
     else hi = mid - 1;
   }
-  return indptr[lo];
+  return lo;
+}
+
+__device__ __forceinline__ int request_first_row(const int32_t* indptr, int batch, int row) {
+  return indptr[request_index(indptr, batch, row)];
 }
 
 // Order-preserving integer key of a float (for the single-instruction warp
@@ -1074,6 +1236,33 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// 2^a and 2^b for a, b <= 0 on the FMA pipe (the consumers' exponentials are
+// bound by the MUFU pipe; a share of them is computed here instead).  Range
+// reduction a = j + f with j = round(a) (adding 1.5 * 2^23 rounds to an
+// integer, which lands in the sum's low mantissa bits) and |f| <= 1/2; 2^f
+// from a degree-5 polynomial with the constant term 1, fitted here to the
+// relative error of 2^f on [-1/2, 1/2] by weighted least squares with Lawson
+// reweighting (max 1.8e-7 relative in fp32, 2^0 = 1 exactly); 2^j is added to
+// the exponent field.  Arguments below -125 are taken as -125 (2^-125 next to
+// a partial sum that holds a term 1).
+__device__ __forceinline__ uint64_t ex2_poly2(float a, float b) {
+  constexpr float kRound = 12582912.0f;
+  const uint64_t x = f2(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
+  const uint64_t t = fadd2(x, f2(kRound, kRound));
+  const uint64_t j = fadd2(t, f2(-kRound, -kRound));
+  const uint64_t f = ffma2(j, f2(-1.0f, -1.0f), x);
+  uint64_t q = ffma2(f, f2(1.3308824e-3f, 1.3308824e-3f), f2(9.6715167e-3f, 9.6715167e-3f));
+  q = ffma2(q, f, f2(5.5505823e-2f, 5.5505823e-2f));
+  q = ffma2(q, f, f2(2.4022242e-1f, 2.4022242e-1f));
+  q = ffma2(q, f, f2(6.9314706e-1f, 6.9314706e-1f));
+  q = ffma2(q, f, f2(1.0f, 1.0f));
+  float q0, q1, t0, t1;
+  f2_split(q, q0, q1);
+  f2_split(t, t0, t1);
+  return f2(__uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)),
+            __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)));
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    su32(dst)),
@@ -1164,7 +1353,8 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   StreamCtl& ctl = *reinterpret_cast<StreamCtl*>(sm + kSCtlOff);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
-  const int n_items = plan.items(c);
+  const bool streams = c < plan.G;      // CTAs past G (dedicated walkers) stream nothing
+  const int n_items = streams ? plan.items(c) : 0;
   const Part kNone{0.0, -INFINITY, INT_MAX};
 
   // stream-order tables after the walk state
@@ -1177,6 +1367,14 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   const int32_t* indptr = p.batch < kSmemIndptr ? sindptr : p.row_indptr;
   if (p.batch < kSmemIndptr)
     for (int i = tid; i <= p.batch; i += kSThreads) sindptr[i] = p.row_indptr[i];
+  // dfs tables (plan.dfs implies batch < kSmemIndptr)
+  unsigned long long* okeys = reinterpret_cast<unsigned long long*>(
+      (reinterpret_cast<uintptr_t>(sindptr + (p.batch < kSmemIndptr ? p.batch + 1 : 0)) + 7) & ~(uintptr_t)7);
+  int* nint = reinterpret_cast<int*>(okeys + plan.num_rows);
+  int16_t* spar = reinterpret_cast<int16_t*>(nint + p.batch);   // request-local parents (-1: none)
+  int16_t* orank = spar + plan.num_rows;                         // internal rows: preorder rank
+  int* rank_base = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(orank + plan.num_rows) + 3) & ~(uintptr_t)3);
+  // rank_base[k]: the internal rows of rank below k over all requests (sum of min(nint, k))
 
   if (tid == 0) {
     for (int i = 0; i < kSSlots; ++i) {
@@ -1190,17 +1388,79 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     ctl.seg_max = 0ull;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // ---- stream order (every CTA computes it for its own rows) ---------------
-  for (int i = tid; i < plan.mask_words; i += kSThreads) imask[i] = 0u;
-  __syncthreads();
-  for (int j = tid; j < plan.num_rows; j += kSThreads) {
-    const int lo = request_first_row(indptr, p.batch, j);
-    const int pj = p.parents[j];
-    const int r = (j == lo) ? j : ((pj >= 0 && pj < j - lo) ? lo + pj : -1);
-    if (r >= 0) atomicOr(&imask[r >> 5], 1u << (r & 31));
-  }
-  __syncthreads();
-  {
+  // ---- stream order (every streaming CTA computes it for its own rows) -------
+  if (streams) {
+    for (int i = tid; i < plan.mask_words; i += kSThreads) imask[i] = 0u;
+    __syncthreads();
+    for (int j = tid; j < plan.num_rows; j += kSThreads) {
+      const int lo = request_first_row(indptr, p.batch, j);
+      const int pj = p.parents[j];
+      const bool has = j > lo && pj >= 0 && pj < j - lo;
+      const int r = (j == lo) ? j : (has ? lo + pj : -1);
+      if (r >= 0) atomicOr(&imask[r >> 5], 1u << (r & 31));
+      if (plan.dfs) spar[j] = (int16_t)(has ? pj : -1);
+    }
+    __syncthreads();
+    if (plan.dfs) {
+      // One warp per request.  Preorder key of every internal row: its
+      // ancestors' node indices below the root (and its own), key_bits each,
+      // the shallowest in the top bits and zeros below the node's depth, so a
+      // node sorts before its subtree and siblings by index; the low 8 bits
+      // hold the node's own index instead (unique keys; a request has at most
+      // kDfsMaxNodes = 256 nodes here).  A chain longer than the key keeps its
+      // top levels, one longer than the climb limit sorts last.  The keys of
+      // the request's internal rows are packed at okeys[lo ..], then each
+      // one's rank is the number of smaller keys: a permutation whatever the
+      // tree.
+      const int levels = 64 / plan.key_bits;
+      for (int b = warp; b < p.batch; b += kSThreads / 32) {
+        const int lo = indptr[b], n = indptr[b + 1] - lo;
+        int m = 0;
+        for (int i0 = 0; i0 < n; i0 += 32) {
+          const int i = i0 + lane, j = lo + i;
+          const bool in = i < n && ((imask[j >> 5] >> (j & 31)) & 1u);
+          unsigned long long key = 0ull;
+          if (in) {
+            int v = i;
+            for (int d = 0; v > 0 && d <= levels + 8; ++d) {   // parents precede children: v decreases
+              key = (key >> plan.key_bits) | ((unsigned long long)v << (64 - plan.key_bits));
+              v = max((int)spar[lo + v], 0);
+            }
+            key = ((v > 0 ? ~0ull : key) & ~0xffull) | (unsigned long long)i;
+          }
+          const unsigned bal = __ballot_sync(0xffffffffu, in);
+          const int slot = m + __popc(bal & ((1u << lane) - 1u));
+          if (in) {
+            okeys[lo + slot] = key;
+            if (n > kDfsMaxNodes) orank[j] = (int16_t)slot;     // (invalid sizes) row order
+          }
+          m += __popc(bal);
+        }
+        if (lane == 0) nint[b] = m;
+        __syncwarp();
+        for (int s0 = 0; n <= kDfsMaxNodes && s0 < m; s0 += 32) {
+          const int sidx = s0 + lane;
+          const unsigned long long kr = sidx < m ? okeys[lo + sidx] : ~0ull;
+          int k = 0, t = 0;
+          for (; t + 8 <= m; t += 8) {
+            unsigned long long kk[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) kk[q] = okeys[lo + t + q];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) k += kk[q] < kr ? 1 : 0;
+          }
+          for (; t < m; ++t) k += okeys[lo + t] < kr ? 1 : 0;
+          if (sidx < m) orank[lo + (int)(kr & 0xffull)] = (int16_t)k;
+        }
+      }
+      __syncthreads();
+      for (int k = tid; k <= kDfsMaxNodes; k += kSThreads) {
+        int sum = 0;
+        for (int b2 = 0; b2 < p.batch; ++b2) sum += min(nint[b2], k);
+        rank_base[k] = sum;
+      }
+      __syncthreads();
+    }
     const int per = (plan.num_rows + kSThreads - 1) / kSThreads;
     const int r0 = min(tid * per, plan.num_rows), r1 = min(r0 + per, plan.num_rows);
     int cnt = 0;
@@ -1227,7 +1487,19 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     int ib = (warp ? scan[warp - 1] : 0) + incl - cnt;       // internal rows before r0
     for (int r = r0; r < r1; ++r) {
       const int in = (imask[r >> 5] >> (r & 31)) & 1;
-      const int q = in ? ib : n_int + (r - ib);
+      int q = in ? ib : n_int + (r - ib);
+      if (in && plan.dfs) {
+        // the internal rows go rank by rank, requests in order within a rank
+        const int b = request_index(indptr, p.batch, r);
+        const int k = orank[r];
+        if (k <= kDfsMaxNodes) {
+          q = rank_base[k];
+        } else {
+          q = 0;
+          for (int b2 = 0; b2 < p.batch; ++b2) q += min(nint[b2], k);
+        }
+        for (int b2 = 0; b2 < b; ++b2) q += nint[b2] > k ? 1 : 0;
+      }
       ib += in;
       if (q < plan.split_first_row) {
         if (q % plan.G == c) mine[q / plan.G] = (uint16_t)r;
@@ -1307,7 +1579,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
         for (int i = 0; i < kSVec * 4; ++i) {
           float a, b;
           f2_split(ffma2(f2(__uint_as_float(v[i] << 16), __uint_as_float(v[i] & 0xffff0000u)), sc2, nm2), a, b);
-          const uint64_t e = f2(ex2_approx(a), ex2_approx(b));
+          const uint64_t e = i >= kSVec * 4 - kSPolyPairs ? ex2_poly2(a, b) : f2(ex2_approx(a), ex2_approx(b));
           if (i & 1) acc_b = fadd2(acc_b, e);
           else acc_a = fadd2(acc_a, e);
         }
@@ -1419,12 +1691,12 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       }
       finish_row_warp(p, row, x);
     }
-  } else {
+  } else if (warp == kSConsumerWarps + 2) {
     // ---------------------------------------------------------------- walker
     // Claims the next request and walks it, waiting for each row it reads
     // (parents' rows, the bonus row) to be published: the walks of different
     // requests run on different SMs while the leaf rows still stream.
-    if (p.no_walk) return;
+    if (p.no_walk || (plan.walkers && streams)) return;
     if (p.parts_out) {
       // shard partials mode: each node's token logit, if this shard holds the token
       for (int r = c * 32 + lane; r < p.num_rows; r += plan.G * 32) {
@@ -1442,10 +1714,44 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       unsigned t = 0;
       if (lane == 0) t = atomicAdd(&p.walk_ctr[1], 1u);
       t = __shfl_sync(0xffffffffu, t, 0);
-      if (t >= (unsigned)p.batch) break;
-      const int b = (int)t;
-      const int lo = p.row_indptr[b];
-      walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr);
+      const int b = t < (unsigned)p.batch ? (int)t : -1;
+      if (!p.traversal) {
+        if (b < 0) break;
+        const int lo = p.row_indptr[b];
+        walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr);
+        continue;
+      }
+      // traversal: set-up, hand the request to the expander, walk lazily
+      int lo = 0, n = 0;
+      bool go = false;
+      if (b >= 0) {
+        lo = p.row_indptr[b];
+        n = p.row_indptr[b + 1] - lo;
+        go = walk_request<true>(p, b, lo, n, w, WarpGroup{}, nullptr);
+      }
+      if (lane == 0) {
+        ctl.walk_b = b < 0 ? -1 : go ? b : -2;
+        ctl.walk_done = 0;
+      }
+      named_barrier(1, 64);
+      if (b < 0) break;
+      if (go) walk_traversal_warp<true>(p, b, lo, n, w);
+      if (lane == 0) *(volatile int*)&ctl.walk_done = 1;
+      named_barrier(2, 64);
+    }
+  } else {
+    // -------------------------------------------------------------- expander
+    if (p.no_walk || p.parts_out || !p.traversal || (plan.walkers && streams)) return;
+    const WalkSmem w = walk_smem(sm + kSWalkOff, p.max_nodes);
+    for (;;) {
+      named_barrier(1, 64);
+      const int b = *(volatile int*)&ctl.walk_b;
+      if (b == -1) break;
+      if (b >= 0) {
+        const int lo = p.row_indptr[b];
+        expand_request(p, lo, p.row_indptr[b + 1] - lo, w, &ctl.walk_done);
+      }
+      named_barrier(2, 64);
     }
   }
 }
@@ -1519,13 +1825,22 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   if (dev < 0 || dev >= 256) return set_error(PTS_ERR_UNSUPPORTED, "device ordinal %d", dev);
   if (p.vec_ok && p.vocab % 8 == 0 && sms > 0) {
     StreamPlan plan;
-    plan.G = min(sms, p.num_rows * nchunks);
+    // small traversal batches: one CTA per walk that streams nothing, so the
+    // walk's dependent chain does not share issue slots with the consumers
+    plan.walkers = (p.traversal && !p.parts_out && !p.no_walk && p.batch <= sms / 8) ? p.batch : 0;
+    plan.G = min(sms - plan.walkers, p.num_rows * nchunks);
     plan.nchunks = nchunks;
-    plan.whole_rows_per_cta = p.num_rows / plan.G;
-    plan.split_first_row = plan.whole_rows_per_cta * plan.G;
+    // the rows past the last full round of G are split by chunk over all CTAs
+    // only when every CTA streams few rows: a split chunk costs its merger a
+    // global atomic and, for the last chunk, the row's merge
+    const int rounds = p.num_rows / plan.G;
+    plan.split_first_row = rounds >= 4 ? p.num_rows : rounds * plan.G;
+    plan.whole_rows_per_cta = (plan.split_first_row + plan.G - 1) / plan.G;
     plan.split_items = (p.num_rows - plan.split_first_row) * nchunks;
     plan.num_rows = p.num_rows;
     plan.mask_words = (p.num_rows + 31) / 32;
+    plan.dfs = p.traversal && p.num_rows <= kDfsMaxRows && p.batch <= kDfsMaxBatch && p.max_nodes <= kDfsMaxNodes;
+    plan.key_bits = p.max_nodes > 1 ? 32 - __builtin_clz((unsigned)(p.max_nodes - 1)) : 1;
     const size_t ssmem =
         ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan, p.batch);
     if (ssmem <= kMaxDynSmem) {
@@ -1535,7 +1850,7 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
             cudaFuncSetAttribute(accept_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
         ssmem_attr[dev] = ssmem;
       }
-      accept_stream_kernel<<<plan.G, kSThreads, ssmem, stream>>>(p, plan);
+      accept_stream_kernel<<<plan.G + plan.walkers, kSThreads, ssmem, stream>>>(p, plan);
       return launch_status("accept_stream_kernel");
     }
   }
