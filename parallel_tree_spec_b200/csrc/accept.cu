@@ -1106,7 +1106,6 @@ constexpr int kSConsumerWarps = 16;
 constexpr int kSConsumers = kSConsumerWarps * 32;
 constexpr int kSThreads = kSConsumers + 128;   // + producer, merger, walker and expander warps
 constexpr int kSVec = kSChunk / 8 / kSConsumers;   // 16-byte vectors per consumer thread (4)
-constexpr int kSPolyPairs = 0;                     // of the 16 value pairs per chunk, exponentials by ex2_poly2
 constexpr long long kSpinLimit = 4000000000ll;     // clock cycles, about 2 s
 constexpr size_t kMaxDynSmem = 232448;             // 227 KB per CTA
 
@@ -1132,8 +1131,8 @@ constexpr size_t kSWalkOff = (kSCtlOff + sizeof(StreamCtl) + 127) & ~(size_t)127
 // requests interleaved at each rank: the order in which traversal walks
 // descend through them, so every walk receives its rows while it runs.
 // Position q of the stream order is a whole row of CTA q % G while
-// q < split_first_row; when every CTA streams fewer than four rows, the
-// remaining num_rows % G positions are split by chunk over all CTAs.  A
+// q < split_first_row; the remaining num_rows % G positions are split by
+// chunk over all CTAs when they are few or every CTA streams few rows.  A
 // traversal walk needs the statistics of internal rows only (its target
 // probabilities come from the parents' rows) and one leaf row at most (the
 // bonus token), so the walks start while the leaf rows still stream.
@@ -1236,33 +1235,6 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-// 2^a and 2^b for a, b <= 0 on the FMA pipe (the consumers' exponentials are
-// bound by the MUFU pipe; a share of them is computed here instead).  Range
-// reduction a = j + f with j = round(a) (adding 1.5 * 2^23 rounds to an
-// integer, which lands in the sum's low mantissa bits) and |f| <= 1/2; 2^f
-// from a degree-5 polynomial with the constant term 1, fitted here to the
-// relative error of 2^f on [-1/2, 1/2] by weighted least squares with Lawson
-// reweighting (max 1.8e-7 relative in fp32, 2^0 = 1 exactly); 2^j is added to
-// the exponent field.  Arguments below -125 are taken as -125 (2^-125 next to
-// a partial sum that holds a term 1).
-__device__ __forceinline__ uint64_t ex2_poly2(float a, float b) {
-  constexpr float kRound = 12582912.0f;
-  const uint64_t x = f2(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
-  const uint64_t t = fadd2(x, f2(kRound, kRound));
-  const uint64_t j = fadd2(t, f2(-kRound, -kRound));
-  const uint64_t f = ffma2(j, f2(-1.0f, -1.0f), x);
-  uint64_t q = ffma2(f, f2(1.3308824e-3f, 1.3308824e-3f), f2(9.6715167e-3f, 9.6715167e-3f));
-  q = ffma2(q, f, f2(5.5505823e-2f, 5.5505823e-2f));
-  q = ffma2(q, f, f2(2.4022242e-1f, 2.4022242e-1f));
-  q = ffma2(q, f, f2(6.9314706e-1f, 6.9314706e-1f));
-  q = ffma2(q, f, f2(1.0f, 1.0f));
-  float q0, q1, t0, t1;
-  f2_split(q, q0, q1);
-  f2_split(t, t0, t1);
-  return f2(__uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)),
-            __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)));
-}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    su32(dst)),
@@ -1579,7 +1551,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
         for (int i = 0; i < kSVec * 4; ++i) {
           float a, b;
           f2_split(ffma2(f2(__uint_as_float(v[i] << 16), __uint_as_float(v[i] & 0xffff0000u)), sc2, nm2), a, b);
-          const uint64_t e = i >= kSVec * 4 - kSPolyPairs ? ex2_poly2(a, b) : f2(ex2_approx(a), ex2_approx(b));
+          const uint64_t e = f2(ex2_approx(a), ex2_approx(b));
           if (i & 1) acc_b = fadd2(acc_b, e);
           else acc_a = fadd2(acc_a, e);
         }
@@ -1831,10 +1803,12 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
     plan.G = min(sms - plan.walkers, p.num_rows * nchunks);
     plan.nchunks = nchunks;
     // the rows past the last full round of G are split by chunk over all CTAs
-    // only when every CTA streams few rows: a split chunk costs its merger a
-    // global atomic and, for the last chunk, the row's merge
+    // when that adds at most two chunks per CTA or every CTA streams few rows
+    // (a split chunk costs its merger a global atomic and, for the last
+    // chunk, the row's merge); otherwise they go whole, one more row for some
     const int rounds = p.num_rows / plan.G;
-    plan.split_first_row = rounds >= 4 ? p.num_rows : rounds * plan.G;
+    const int rem = p.num_rows - rounds * plan.G;
+    plan.split_first_row = (rounds < 4 || rem * nchunks <= 2 * plan.G) ? rounds * plan.G : p.num_rows;
     plan.whole_rows_per_cta = (plan.split_first_row + plan.G - 1) / plan.G;
     plan.split_items = (p.num_rows - plan.split_first_row) * nchunks;
     plan.num_rows = p.num_rows;

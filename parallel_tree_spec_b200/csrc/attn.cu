@@ -69,7 +69,7 @@ struct __align__(8) Bars {
   uint64_t s_full[2];    // S_t(j) computed                  (tcgen05.commit)
   uint64_t s_free[2];    // S_t(j) copied out of TMEM          (4 softmax warps)
   uint64_t p_full[2];    // P_t(j) in shared memory, O_t ready (4 softmax warps)
-  uint64_t p_empty[2][2];  // PV_t(j) done: P buffer j % 2 free   (tcgen05.commit)
+  uint64_t p_empty[2][2];  // PV_t(j) done (O_t may be rescaled)      (tcgen05.commit)
   uint64_t o_full[2];
   uint64_t drain[2];
   uint32_t tmem;
@@ -351,25 +351,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = mblk;
       }
       const float msub = m_used == -INFINITY ? 0.0f : m_used;
-      float ls0 = 0.0f, ls1 = 0.0f;
+      // column pairs: scale and shift, and the row sums, on the FMA pipe's
+      // two-lane form
+      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-msub, -msub);
+      uint64_t ls = f2(0.0f, 0.0f);
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < kBlockN; c += 2) {
-        const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -msub));
-        const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -msub));
-        ls0 += e0;
-        ls1 += e1;
+        float a, b;
+        f2_split(ffma2(f2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nm2), a, b);
+        const uint64_t e = f2(fast_exp2(a), fast_exp2(b));
+        ls = fadd2(ls, e);
+        float e0, e1;
+        f2_split(e, e0, e1);
         pk[c / 2] = pack_bf16x2(e0, e1);
       }
+      float ls0, ls1;
+      f2_split(ls, ls0, ls1);
       l_sum += ls0 + ls1;
-      // P buffer j % 2 is free once PV_t(j-2) has completed
-      if (j > 1) {
-        if (!mbar_wait(&bars.p_empty[t][j & 1], ((j >> 1) - 1) & 1)) {
-          record_abort(bars, p, 33);
-          ok = false;
-          break;
-        }
-      }
+      // P buffer j % 2 is free: PV_t(j-2) has completed, because the issuer
+      // (one elected thread) issues S_t(j) after PV_t(j-2) and the s_full
+      // commit waited on above tracks every earlier MMA of that thread
       const uint32_t pbuf = prow + (uint32_t)(j & 1) * kPBytes;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
