@@ -109,6 +109,14 @@ __device__ __forceinline__ void record_abort(Bars& bars, const AttnParams& p, in
 
 __device__ __forceinline__ bool aborted(const Bars& bars) { return *(volatile const int*)&bars.abort != 0; }
 
+// Named barrier `id` over `count` threads: wait for it / arrive without waiting.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ uint64_t low_bits(int n) {          // n in [0, 64]
   return n >= 64 ? ~0ull : ((1ull << n) - 1ull);
 }
@@ -312,11 +320,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float m_used = -INFINITY, l_sum = 0.0f;
     bool ok = active_tile;
-    for (int j = 0; ok && j < n_blocks; ++j) {
-      if (!mbar_wait(&bars.s_full[t], j & 1)) {
-        record_abort(bars, p, 31);
-        ok = false;
-        break;
+    // With two tiles, their warpgroups take turns at the exponentials (named
+    // barriers 2 and 3 pass the turn), so one tile's exp2 phase has the MUFU
+    // pipe to itself while the other loads S, takes the row max, stores P and
+    // hands off.  Both warpgroups then run every block -- a named barrier
+    // cannot time out, so an abort skips the work but never the turn.
+    const bool turns = n_tiles == 2;
+    const int turn_wait = t == 0 ? 2 : 3, turn_pass = t == 0 ? 3 : 2;
+    for (int j = 0; j < n_blocks && (ok || turns); ++j) {
+      const bool wait_turn = turns && (t == 1 || j > 0);
+      const bool pass_turn = turns && !(t == 1 && j == n_blocks - 1);
+      if (ok && aborted(bars)) ok = false;
+      if (ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars.s_full[t], j & 1));
+        if (!ok) record_abort(bars, p, 31);
+      }
+      if (!ok) {                                        // the turns only
+        if (wait_turn) named_bar_sync(turn_wait, 256);
+        if (pass_turn) named_bar_arrive(turn_pass, 256);
+        continue;
       }
       tc_fence_after();
       uint32_t sr[64];
@@ -351,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = mblk;
       }
       const float msub = m_used == -INFINITY ? 0.0f : m_used;
+      if (wait_turn) named_bar_sync(turn_wait, 256);   // this tile's turn at the exponentials
       // column pairs: scale and shift, and the row sums, on the FMA pipe's
       // two-lane form
       const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-msub, -msub);
@@ -366,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         f2_split(e, e0, e1);
         pk[c / 2] = pack_bf16x2(e0, e1);
       }
+      if (pass_turn) named_bar_arrive(turn_pass, 256);   // the other tile's turn
       float ls0, ls1;
       f2_split(ls, ls0, ls1);
       l_sum += ls0 + ls1;
@@ -379,10 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O_t may be rescaled once its last update, PV_t(j-1), has completed
-        if (!mbar_wait(&bars.p_empty[t][(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars.p_empty[t][(j - 1) & 1], ((j - 1) >> 1) & 1));
+        if (!ok) {
           record_abort(bars, p, 35);
-          ok = false;
-          break;
+          continue;
         }
         tc_fence_after();
         for (int cb = 0; cb < 4; ++cb) {
@@ -399,7 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.p_full[t]);
-      if (aborted(bars)) ok = false;
     }
     // ------------------------------------------------------------ epilogue
     if (ok && mbar_wait(&bars.o_full[t], 0)) {
