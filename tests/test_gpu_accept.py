@@ -18,15 +18,15 @@ def bf16(bits: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
 
 
-def run_batch(trees, logits_bits, method, eos=None, T=1.0, seed=0, offset=0):
+def run_batch(trees, logits_bits, method, eos=None, T=1.0, seed=0, offset=0, max_nodes=None):
     indptr, par, tok, dp = wl.stack_trees(trees)
     x = bf16(np.concatenate(logits_bits, 0)).to(DEV)
     args = (x, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV), torch.from_numpy(tok).to(DEV))
     if method == "exact":
-        ot, oh, oc = K.accept_greedy(*args, eos_token_id=eos)
+        ot, oh, oc = K.accept_greedy(*args, eos_token_id=eos, max_nodes=max_nodes)
     else:
         ot, oh, oc = K.accept_traversal(*args, torch.from_numpy(dp).to(DEV), eos_token_id=eos, temperature=T,
-                                        seed=seed, offset=offset)
+                                        seed=seed, offset=offset, max_nodes=max_nodes)
     ot, oh, oc = ot.cpu().numpy(), oh.cpu().numpy(), oc.cpu().numpy()
     res = []
     for b in range(len(trees)):
@@ -63,16 +63,21 @@ def test_golden_acceptance_cases(accept_golden):
         assert (out["total_len"], out["accept_len"]) == (rec["total_len"], rec["accept_len"]), c
 
 
-@pytest.mark.parametrize("method,T,plant", [("exact", 1.0, 0.7), ("exact", 1.0, 0.0), ("traversal", 1.0, 1.0),
-                                            ("traversal", 0.8, 1.0), ("traversal", 1.0, 0.0)])
-def test_batched_full_vocab_vs_oracle(method, T, plant):
-    """Benchmark shape: 16 trees of 65 rows over a 128256 vocabulary."""
+@pytest.mark.parametrize("method,T,plant,max_nodes", [("exact", 1.0, 0.7, None), ("exact", 1.0, 0.0, None),
+                                                      ("traversal", 1.0, 1.0, None), ("traversal", 0.8, 1.0, None),
+                                                      ("traversal", 1.0, 0.0, None), ("exact", 1.0, 0.7, 65),
+                                                      ("traversal", 1.0, 1.0, 65), ("traversal", 0.8, 1.0, 65)])
+def test_batched_full_vocab_vs_oracle(method, T, plant, max_nodes):
+    """Benchmark shape: 16 trees of 65 rows over a 128256 vocabulary; with
+    max_nodes = 65 (the tree size, as the benchmark and the drop-in module
+    pass it) traversal streams the internal rows in depth-first order and
+    walks on CTAs of their own."""
     rng = np.random.default_rng(11 + int(plant * 10) + int(T * 100))
     V = 128256
     trees = [wl.make_tree(rng, 8, 8, V) for _ in range(16)]
     logits = [wl.make_logits(rng, t, V, plant=plant, soft=(method == "traversal")) for t in trees]
     seed, offset = 1234, 77
-    out = run_batch(trees, logits, method, T=T, seed=seed, offset=offset)
+    out = run_batch(trees, logits, method, T=T, seed=seed, offset=offset, max_nodes=max_nodes)
     accepted = 0
     for b, (t, x) in enumerate(zip(trees, logits)):
         am, p = acc.row_stats(x, T if method == "traversal" else 1.0)
@@ -87,6 +92,30 @@ def test_batched_full_vocab_vs_oracle(method, T, plant):
         accepted += al
     if plant > 0:
         assert accepted > 0
+
+
+@pytest.mark.parametrize("shapes,V", [
+    ([(8, 8)] * 40, 8192),            # 40 requests: every CTA streams and walks (depth-first order)
+    ([(8, 8)] * 70, 4096),            # 4550 rows: internal rows in row order
+    ([(1, 64)] * 12, 4096),           # 65-deep chains: keys longer than 64 bits
+    ([(16, 8), (1, 64), (4, 3), (0, 0), (8, 8), (2, 30)] * 4, 4096),   # ragged sizes, 129-node trees
+])
+def test_traversal_stream_orders_vs_oracle(shapes, V):
+    """Traversal beyond the benchmark shape, with max_nodes = the largest
+    tree: the stream orders and walker placements of the persistent kernel."""
+    rng = np.random.default_rng(len(shapes) * 31 + V)
+    trees = [wl.make_tree(rng, w, d, V) for w, d in shapes]
+    logits = [wl.make_logits(rng, t, V, plant=1.0, soft=True) for t in trees]
+    seed, offset = 99, 3
+    mn = max(len(t.parents) for t in trees)
+    out = run_batch(trees, logits, "traversal", seed=seed, offset=offset, max_nodes=mn)
+    for b, (t, x) in enumerate(zip(trees, logits)):
+        am, p = acc.row_stats(x, 1.0)
+        mb = acc.mb_from_probs(t.parents, t.tokens, p)
+        s, h, tl, al, _ = acc.traversal_walk(t.parents, t.tokens, t.draft_probs, mb, am,
+                                             UniformStream(seed, offset, b))
+        assert out[b]["tokens"] == s and out[b]["hidden"] == h, (b, out[b], s, h)
+        assert (out[b]["total_len"], out[b]["accept_len"]) == (tl, al)
 
 
 def test_near_tie_rows_vs_oracle():
