@@ -4,11 +4,11 @@
 One step = the verification of one batch of draft trees against the target's
 paged KV cache, for one attention layer, on one GPU:
 
-  1. tree masks and append positions (one launch)     (pts_tree_prepare)
-  2. append of the tree tokens' K/V into the pages      (pts_kv_append)
-  3. tree-masked paged attention                        (pts_tree_attn_run)
-  4. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
-  5. compaction of each accepted path's KV              (pts_kv_compact)
+  1. tree masks, append positions and the append of the tree tokens' K/V
+     into the pages, in one launch                      (pts_tree_prepare_append)
+  2. tree-masked paged attention                        (pts_tree_attn_run)
+  3. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
+  4. compaction of each accepted path's KV              (pts_kv_compact)
 
 Workload (default): 16 requests, 4096-token prefix, 65-row trees (root + 8
 levels of 8), 32 query / 8 KV heads, head_dim 128, 16-token pages, logits
@@ -252,20 +252,20 @@ class Step:
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
-        self.launches_per_step = 5
+        self.launches_per_step = 4
 
     def run(self, ev=None):
         from parallel_tree_spec_b200._lib import check
         a, W, L, s = self.a, self.W, self.L, self.stream
         B, n = a.batch, W["n"]
         P = W["page_indptr"]
-        check(L.pts_tree_prepare(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(), B,
-                                 W["mask_words"], W["bits"].data_ptr(), W["bi"].data_ptr(), W["pos"].data_ptr(), s),
-              "prepare")
         lay = W["layer"]
-        check(L.pts_kv_append(W["k_new"].data_ptr(), W["v_new"].data_ptr(), a.hkv * 128, a.hkv * 128, lay.data_ptr(),
-                              W["bi"].data_ptr(), W["pos"].data_ptr(), P.data_ptr(), W["page_indices"].data_ptr(),
-                              B * n, a.hkv, 128, 16, lay.shape[0], 2, s), "append")
+        check(L.pts_tree_prepare_append(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(),
+                                        B, W["mask_words"], W["bits"].data_ptr(), W["bi"].data_ptr(),
+                                        W["pos"].data_ptr(), W["k_new"].data_ptr(), W["v_new"].data_ptr(),
+                                        a.hkv * 128, a.hkv * 128, lay.data_ptr(), P.data_ptr(),
+                                        W["page_indices"].data_ptr(), B * n, a.hkv, 128, 16, lay.shape[0], 2, s),
+              "prepare+append")
         if ev is not None:
             ev[0].record()
         check(L.pts_tree_attn_run(W["q"].data_ptr(), lay.data_ptr(), W["qo_indptr"].data_ptr(), P.data_ptr(),
@@ -578,10 +578,10 @@ def run_tp(a):
     res = {}
 
     def one(ev=None):
-        check(L.pts_tree_prepare(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw, bits.data_ptr(),
-                                 bi.data_ptr(), pos.data_ptr(), s), "prepare")
-        check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), hkv * D, hkv * D, layer.data_ptr(), bi.data_ptr(),
-                              pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, hkv, D, pl, max_pages, 2, s), "app")
+        check(L.pts_tree_prepare_append(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw,
+                                        bits.data_ptr(), bi.data_ptr(), pos.data_ptr(), kn.data_ptr(), vn.data_ptr(),
+                                        hkv * D, hkv * D, layer.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, hkv,
+                                        D, pl, max_pages, 2, s), "prepare+append")
         if ev is not None:
             ev[0].record()
         check(L.pts_tree_attn_run(q.data_ptr(), layer.data_ptr(), qo.data_ptr(), pind.data_ptr(), perm.data_ptr(),
@@ -714,10 +714,10 @@ def run_sparse(a):
     s = torch.cuda.current_stream(dev).cuda_stream
 
     def one(ev=None):
-        check(L.pts_tree_prepare(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw, bits.data_ptr(),
-                                 bi.data_ptr(), pos.data_ptr(), s), "prepare")
-        check(L.pts_kv_append(kn.data_ptr(), vn.data_ptr(), Hkv * D, Hkv * D, layer.data_ptr(), bi.data_ptr(),
-                              pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, Hkv, D, pl, max_pages, 2, s), "app")
+        check(L.pts_tree_prepare_append(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw,
+                                        bits.data_ptr(), bi.data_ptr(), pos.data_ptr(), kn.data_ptr(), vn.data_ptr(),
+                                        Hkv * D, Hkv * D, layer.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, Hkv,
+                                        D, pl, max_pages, 2, s), "prepare+append")
         if ev is not None:
             ev[0].record()
         check(L.pts_tree_attn_run_head_pages(q.data_ptr(), layer.data_ptr(), qo.data_ptr(), hi.data_ptr(),

@@ -252,6 +252,21 @@ int pts_tree_prepare(const int32_t* parents, const int32_t* qo_indptr, const int
                      int mask_words, uint64_t* mask_bits, int32_t* batch_indices, int32_t* positions,
                      pts_stream_t stream);
 
+/* pts_tree_prepare (with batch indices and positions) and pts_kv_append of
+ * the tree tokens' K/V, [num_tokens = qo_indptr[batch]] rows at the
+ * token strides given, in one launch.  The append derives each token's page
+ * slot itself (the same position seq_lens[b] - N_b + i), so it does not wait
+ * for the masks.  Replaces Tree.create_attention_mask + the mask packing,
+ * get_batch_indices_positions and append_paged_kv_cache of one layer
+ * (tree.py:167-194, flashinfer/cache_manager.py:263-271,
+ * flashinfer/attention_wrapper.py:201-212). */
+int pts_tree_prepare_append(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens, int batch,
+                            int mask_words, uint64_t* mask_bits, int32_t* batch_indices, int32_t* positions,
+                            const void* k, const void* v, int64_t k_token_stride, int64_t v_token_stride,
+                            void* kv_layer, const int32_t* page_indptr, const int32_t* page_indices,
+                            int num_tokens, int num_kv_heads, int head_dim, int page_len, int max_pages,
+                            int elem_bytes, pts_stream_t stream);
+
 /* Pack a boolean custom mask [sum_b N_b * kv_len_b] (FlashInfer's flattened
  * custom_mask, flashinfer/attention_wrapper.py:141) into tree bitmasks.
  * Columns before kv_len_b - N_b must all be true; *bad_rows (device int,

@@ -171,6 +171,86 @@ __global__ void tree_prepare_kernel(const int32_t* __restrict__ parents, const i
   }
 }
 
+// Tree preparation and KV append in one launch: CTAs 0 .. batch-1 are
+// tree_prepare_kernel (masks, batch indices, positions); CTA batch + t appends
+// token t, whose request and position it derives itself (the same
+// seq_lens[b] - n_b + i as the positions), so the two halves do not wait on
+// each other.
+constexpr int kPrepSmemIndptr = 1024;    // requests whose qo_indptr the append CTAs stage in shared memory
+__global__ void tree_prepare_append_kernel(const int32_t* __restrict__ parents, const int32_t* __restrict__ qo_indptr,
+                                           const int32_t* __restrict__ seq_lens, int batch, int words,
+                                           uint64_t* __restrict__ bits, int32_t* __restrict__ batch_indices,
+                                           int32_t* __restrict__ positions, const char* __restrict__ k,
+                                           const char* __restrict__ v, int64_t k_stride_b, int64_t v_stride_b,
+                                           char* __restrict__ layer, const int32_t* __restrict__ page_indptr,
+                                           const int32_t* __restrict__ page_indices, int row_bytes, int page_len,
+                                           int max_pages) {
+  __shared__ int16_t sp[PTS_MAX_TREE_NODES];
+  __shared__ int32_t sq[kPrepSmemIndptr + 1];
+  if ((int)blockIdx.x < batch) {
+    const int b = blockIdx.x;
+    const int base = qo_indptr[b], n = qo_indptr[b + 1] - base;
+    const bool staged = n <= PTS_MAX_TREE_NODES;
+    if (staged)
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int p = parents[base + i];
+        sp[i] = (int16_t)((p >= 0 && p < i) ? p : -1);
+      }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      uint64_t* out = bits + (int64_t)(base + i) * words;
+      for (int w = 0; w < words; ++w) {
+        uint64_t acc = 0ull;
+        int node = i;
+        for (int guard = 0; node >= 0 && guard <= PTS_MAX_TREE_NODES; ++guard) {
+          if ((node >> 6) == w) acc |= 1ull << (node & 63);
+          int p;
+          if (staged) {
+            p = sp[node];
+          } else {
+            p = parents[base + node];
+            p = (p >= 0 && p < node) ? p : -1;
+          }
+          node = p;
+        }
+        out[w] = acc;
+      }
+      batch_indices[base + i] = b;
+      positions[base + i] = seq_lens[b] - n + i;
+    }
+    return;
+  }
+  const int t = blockIdx.x - batch;
+  const bool in_smem = batch <= kPrepSmemIndptr;
+  if (in_smem)
+    for (int i = threadIdx.x; i <= batch; i += blockDim.x) sq[i] = qo_indptr[i];
+  __syncthreads();
+  const int32_t* qi = in_smem ? sq : qo_indptr;
+  int lo = 0, hi = batch - 1;                          // the last request whose first row is <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (qi[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  const int b = lo;
+  if (t < qi[b] || t >= qi[b + 1]) return;
+  const int pos = seq_lens[b] - (qi[b + 1] - qi[b]) + (t - qi[b]);
+  const int p0 = page_indptr[b], p1 = page_indptr[b + 1];
+  const int pi = pos / page_len;
+  if (pos < 0 || p0 + pi >= p1) return;
+  const int page = page_indices[p0 + pi];
+  if (page < 0 || page >= max_pages) return;
+  const int slot = pos % page_len;
+  char* kd = layer + ((int64_t)(page * 2 + 0) * page_len + slot) * row_bytes;
+  char* vd = layer + ((int64_t)(page * 2 + 1) * page_len + slot) * row_bytes;
+  const char* ks = k + (int64_t)t * k_stride_b;
+  const char* vs = v + (int64_t)t * v_stride_b;
+  for (int o = threadIdx.x * 16; o < row_bytes; o += blockDim.x * 16) {
+    *(uint4*)(kd + o) = *(const uint4*)(ks + o);
+    *(uint4*)(vd + o) = *(const uint4*)(vs + o);
+  }
+}
+
 // One warp per row of the flattened boolean custom mask.
 __global__ void mask_from_bool_kernel(const uint8_t* __restrict__ mask, const int32_t* __restrict__ qo_indptr,
                                       const int32_t* __restrict__ mask_indptr, const int32_t* __restrict__ kv_lens,
@@ -314,4 +394,28 @@ extern "C" int pts_tree_prepare(const int32_t* parents, const int32_t* qo_indptr
   tree_prepare_kernel<<<batch, 128, 0, (cudaStream_t)stream>>>(parents, qo_indptr, seq_lens, mask_words, mask_bits,
                                                               batch_indices, positions);
   return launch_status("tree_prepare_kernel");
+}
+
+extern "C" int pts_tree_prepare_append(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens,
+                                       int batch, int mask_words, uint64_t* mask_bits, int32_t* batch_indices,
+                                       int32_t* positions, const void* k, const void* v, int64_t k_token_stride,
+                                       int64_t v_token_stride, void* kv_layer, const int32_t* page_indptr,
+                                       const int32_t* page_indices, int num_tokens, int num_kv_heads, int head_dim,
+                                       int page_len, int max_pages, int elem_bytes, pts_stream_t stream) {
+  PTS_CHECK_ARG(parents && qo_indptr && seq_lens && mask_bits && batch_indices && positions, "null pointer");
+  PTS_CHECK_ARG(k && v && kv_layer && page_indptr && page_indices, "null pointer");
+  PTS_CHECK_ARG(batch > 0 && mask_words > 0 && num_tokens >= 0, "bad sizes");
+  PTS_CHECK_ARG(elem_bytes == 2 || elem_bytes == 4, "elem_bytes must be 2 or 4");
+  PTS_CHECK_ARG(num_kv_heads > 0 && head_dim > 0 && page_len > 0 && max_pages > 0, "bad shape");
+  const int row_bytes = num_kv_heads * head_dim * elem_bytes;
+  PTS_CHECK_ARG(row_bytes % 16 == 0, "Hkv * D * elem_bytes must be a multiple of 16");
+  PTS_CHECK_ARG((k_token_stride * elem_bytes) % 16 == 0 && (v_token_stride * elem_bytes) % 16 == 0,
+                "token strides must be multiples of 16 bytes");
+  PTS_CHECK_ARG((((uintptr_t)k | (uintptr_t)v | (uintptr_t)kv_layer) & 15) == 0, "pointers must be 16-byte aligned");
+  PTS_CHECK_ARG((int64_t)batch + num_tokens <= 0x7fffffff, "too many blocks");
+  tree_prepare_append_kernel<<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
+      parents, qo_indptr, seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
+      (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer, page_indptr,
+      page_indices, row_bytes, page_len, max_pages);
+  return launch_status("tree_prepare_append_kernel");
 }

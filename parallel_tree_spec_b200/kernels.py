@@ -308,6 +308,34 @@ def tree_prepare(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_words: int
     return bits, bi, pos
 
 
+def tree_prepare_append(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_words: int, seq_lens: torch.Tensor,
+                        k: torch.Tensor, v: torch.Tensor, kv_layer: torch.Tensor, page_indptr: torch.Tensor,
+                        page_indices: torch.Tensor):
+    """``tree_prepare`` with positions and ``kv_append`` of the tree tokens'
+    k/v [T, Hkv, D] into one layer [max_pages, 2, page_len, Hkv, D], in one
+    launch.  Returns (bits, batch_indices, positions)."""
+    dev = _need_cuda(parents, qo_indptr, seq_lens, k, v, kv_layer, page_indptr, page_indices)
+    if kv_layer.dim() != 5 or kv_layer.shape[1] != 2 or not kv_layer.is_contiguous():
+        raise ValueError("kv_layer must be a contiguous [max_pages, 2, page_len, Hkv, D] tensor")
+    P, _, pl, H, D = kv_layer.shape
+    if k.dtype != kv_layer.dtype or v.dtype != kv_layer.dtype:
+        raise ValueError("k/v dtype must match the cache dtype")
+    parents, qo_indptr = _i32(parents, "parents"), _i32(qo_indptr, "qo_indptr")
+    T = parents.numel()
+    if k.shape[0] != T or v.shape[0] != T:
+        raise ValueError("k and v need one row per tree token")
+    k = k.reshape(T, H * D) if k.stride(-1) == 1 and k[0].is_contiguous() else k.contiguous().reshape(-1, H * D)
+    v = v.reshape(T, H * D) if v.stride(-1) == 1 and v[0].is_contiguous() else v.contiguous().reshape(-1, H * D)
+    bits = torch.empty(T, mask_words, dtype=torch.int64, device=dev)
+    bi = torch.empty(T, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, dtype=torch.int32, device=dev)
+    _lib.call("pts_tree_prepare_append", parents.data_ptr(), qo_indptr.data_ptr(), _i32(seq_lens, "seq_lens").data_ptr(),
+              qo_indptr.numel() - 1, mask_words, bits.data_ptr(), bi.data_ptr(), pos.data_ptr(), k.data_ptr(),
+              v.data_ptr(), k.stride(0), v.stride(0), kv_layer.data_ptr(), _i32(page_indptr, "indptr").data_ptr(),
+              _i32(page_indices, "indices").data_ptr(), T, H, D, pl, P, kv_layer.element_size(), _stream(dev))
+    return bits, bi, pos
+
+
 def tree_mask_from_bool(mask: torch.Tensor, qo_indptr: torch.Tensor, mask_indptr: torch.Tensor,
                         kv_lens: torch.Tensor, mask_words: int, total_q: Optional[int] = None,
                         check: bool = True) -> torch.Tensor:

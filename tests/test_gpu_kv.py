@@ -165,3 +165,38 @@ def test_tree_prepare_matches_masks_and_positions():
     assert torch.equal(bi, rbi) and torch.equal(pos, rpos)
     bits2, none_bi, none_pos = K.tree_prepare(dpar, dind, words)
     assert torch.equal(bits2, ref_bits) and none_bi is None and none_pos is None
+
+
+@pytest.mark.parametrize("shapes", [[(8, 8), (0, 0), (16, 8), (1, 40), (3, 5)], [(0, 0), (2, 1), (1, 3)] * 367])
+def test_tree_prepare_append_matches_separate_launches(shapes):
+    """pts_tree_prepare_append (one launch) = pts_tree_prepare + pts_kv_append:
+    the same masks and positions and every byte of the layer, for a ragged
+    batch and for 1101 requests (the append CTAs then search qo_indptr in
+    global memory)."""
+    rng = np.random.default_rng(len(shapes))
+    trees = [wl.make_tree(rng, w, d, 500) for (w, d) in shapes]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    T, B = int(indptr[-1]), len(trees)
+    Hkv, D, pl = 2, 64, 16
+    prefix = rng.integers(0, 70, size=B)
+    seq = prefix + np.array([t.size for t in trees])
+    npages = (seq + pl - 1) // pl
+    P = int(npages.sum()) + 3
+    perm = rng.permutation(P)[:int(npages.sum())].astype(np.int32)
+    pind = np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)
+    layer = torch.randn(P, 2, pl, Hkv, D, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(DEV)
+    k = torch.randn(T, Hkv, D, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(DEV)
+    v = torch.randn(T, Hkv, D, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
+    words = K.mask_words_for(max(t.size for t in trees))
+    dpar, dind = torch.from_numpy(par).to(DEV), torch.from_numpy(indptr).to(DEV)
+    dseq = torch.from_numpy(seq.astype(np.int32)).to(DEV)
+    dpind, dperm = torch.from_numpy(pind).to(DEV), torch.from_numpy(perm).to(DEV)
+    fused = layer.clone()
+    bits, bi, pos = K.tree_prepare_append(dpar, dind, words, dseq, k, v, fused, dpind, dperm)
+    sep = layer.clone()
+    rbits, rbi, rpos = K.tree_prepare(dpar, dind, words, dseq)
+    K.kv_append(k, v, sep, rbi, rpos, dpind, dperm)
+    torch.cuda.synchronize()
+    assert torch.equal(bits, rbits) and torch.equal(bi, rbi) and torch.equal(pos, rpos)
+    assert torch.equal(fused.view(torch.int16), sep.view(torch.int16))
+    assert not torch.equal(fused.view(torch.int16), layer.view(torch.int16))
