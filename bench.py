@@ -7,8 +7,9 @@ paged KV cache, for one attention layer, on one GPU:
   1. tree masks, append positions and the append of the tree tokens' K/V
      into the pages, in one launch                      (pts_tree_prepare_append)
   2. tree-masked paged attention                        (pts_tree_attn_run)
-  3. acceptance over the [B*N, V] bf16 logits + walk    (pts_accept_traversal / _greedy)
-  4. compaction of each accepted path's KV              (pts_kv_compact)
+  3. acceptance over the [B*N, V] bf16 logits + walk, with the compaction of
+     each accepted path's KV in the same launch         (pts_accept_traversal_compact;
+                                                          greedy: pts_accept_greedy + pts_kv_compact)
 
 Workload (default): 16 requests, 4096-token prefix, 65-row trees (root + 8
 levels of 8), 32 query / 8 KV heads, head_dim 128, 16-token pages, logits
@@ -27,6 +28,7 @@ ranks of the device-timed region.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -252,7 +254,11 @@ class Step:
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
-        self.launches_per_step = 4
+        self.launches_per_step = 3 if a.mode == "traversal" else 4
+        pool = W["pool"]
+        self.compact = _lib.KvCompactArgs(pool.data_ptr(), 1, W["layer"].shape[0], 16, a.hkv, 128, 2,
+                                          W["page_indptr"].data_ptr(), W["page_indices"].data_ptr(),
+                                          W["offsets"].data_ptr(), None, None)
 
     def run(self, ev=None):
         from parallel_tree_spec_b200._lib import check
@@ -276,25 +282,26 @@ class Step:
         if ev is not None:
             ev[1].record()
         x = W["logits"]
+        # acceptance; each walk then compacts its request's accepted KV in the same launch
         if a.mode == "traversal":
-            check(L.pts_accept_traversal(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
-                                         W["tokens"].data_ptr(), W["draft_probs"].data_ptr(), B, B * n, a.vocab, n,
-                                         -1, a.temperature, a.top_p, 0, self.philox_seed, self.step_index,
-                                         W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
-                                         self.acc_ws.data_ptr(), self.acc_ws.numel(), s), "accept")
+            check(L.pts_accept_traversal_compact(
+                x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(), W["tokens"].data_ptr(),
+                W["draft_probs"].data_ptr(), B, B * n, a.vocab, n, -1, a.temperature, a.top_p, 0, self.philox_seed,
+                self.step_index, W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
+                self.acc_ws.data_ptr(), self.acc_ws.numel(), ctypes.byref(self.compact), s), "accept+compact")
         else:
+            # greedy walks end with the stream, so the compaction's dependent copies would lengthen the
+            # launch: it runs as its own launch here
             check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
                                       W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(),
                                       W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
                                       self.acc_ws.numel(), s), "accept")
+            pool = W["pool"]
+            check(L.pts_kv_compact(pool.data_ptr(), 1, W["layer"].shape[0], 16, a.hkv, 128, 2,
+                                   W["page_indptr"].data_ptr(), W["page_indices"].data_ptr(), W["oh"].data_ptr(), n,
+                                   W["oc"].data_ptr(), 4, W["offsets"].data_ptr(), B, n, None, None, s), "compact")
         if ev is not None:
             ev[2].record()
-        pool = W["pool"]
-        check(L.pts_kv_compact(pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
-                               W["page_indices"].data_ptr(), W["oh"].data_ptr(), n, W["oc"].data_ptr(), 4,
-                               W["offsets"].data_ptr(), B, n, None, None, s), "compact")
-        if ev is not None:
-            ev[3].record()
         self.step_index += 1
 
 
@@ -402,7 +409,7 @@ def run_b200(a):
         step.run()
     torch.cuda.synchronize()
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local).start()
     if world > 1:
@@ -421,7 +428,6 @@ def run_b200(a):
     elapsed_ms = start.elapsed_time(end)
     attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
     acc_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    cmp_ms = [e[2].elapsed_time(e[3]) for e in evs]
     if world > 1:
         t = torch.tensor([elapsed_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -465,7 +471,7 @@ def run_b200(a):
                      "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes},
         "step_roofline": {"algorithmic_bytes": ab["step"], "achieved_gbs": ab["step"] / (ms_per_step * 1e-3) / 1e9,
                           "frac": ab["step"] / (ms_per_step * 1e-3) / 1e9 / peak},
-        "kernels_us": {"tree_attn": k_attn * 1e6, "accept": k_acc * 1e6, "compact": statistics.mean(cmp_ms) * 1e3},
+        "kernels_us": {"tree_attn": k_attn * 1e6, "accept_with_compaction": k_acc * 1e6},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": step.launches_per_step * a.steps,
@@ -711,6 +717,8 @@ def run_sparse(a):
     oh = torch.empty(B, n, dtype=torch.int32, device=dev)
     oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
     pool = layer.view(1, *layer.shape)
+    cargs = _lib.KvCompactArgs(pool.data_ptr(), 1, max_pages, pl, Hkv, D, 2, pind.data_ptr(), perm.data_ptr(),
+                               offs.data_ptr(), None, None)
     s = torch.cuda.current_stream(dev).cuda_stream
 
     def one(ev=None):
@@ -726,13 +734,12 @@ def run_sparse(a):
                                              attn_ws.data_ptr(), attn_ws.numel(), s), "attention")
         if ev is not None:
             ev[1].record()
-        check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), qo.data_ptr(), parents.data_ptr(), tokens.data_ptr(),
-                                  B, T, V, n, -1, ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), n,
-                                  acc_ws.data_ptr(), acc_ws.numel(), s), "accept")
+        check(L.pts_accept_greedy_compact(x.data_ptr(), x.stride(0), qo.data_ptr(), parents.data_ptr(),
+                                          tokens.data_ptr(), B, T, V, n, -1, ot.data_ptr(), oh.data_ptr(),
+                                          oc.data_ptr(), n, acc_ws.data_ptr(), acc_ws.numel(), ctypes.byref(cargs),
+                                          s), "accept+compact")
         if ev is not None:
             ev[2].record()
-        check(L.pts_kv_compact(pool.data_ptr(), 1, max_pages, pl, Hkv, D, 2, pind.data_ptr(), perm.data_ptr(),
-                               oh.data_ptr(), n, oc.data_ptr(), 4, offs.data_ptr(), B, n, None, None, s), "compact")
 
     for _ in range(max(3, a.warmup)):
         one()

@@ -87,6 +87,43 @@ int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32
                          int32_t* out_counts, int out_stride, void* workspace,
                          size_t workspace_bytes, pts_stream_t stream);
 
+/* The KV compaction of the accepted paths (pts_kv_compact with accepted =
+ * out_hidden, accepted_stride = max_accepted = out_stride, counts =
+ * out_counts column 0), done by the acceptance launch itself: each walk
+ * compacts its request as soon as its path is known.  kv_pool is
+ * [num_layers, max_pages, 2, page_len, Hkv, D]; offsets[b] is the cache slot of
+ * request b's tree row 0; new_kv_len / new_last_page_len (nullable) receive
+ * offsets[b] + count and its last-page fill.  The pool's tree rows must be
+ * written before the acceptance launch (stream order) and read by nothing else
+ * during it.  Replaces reorder_cache_with_offset after verification
+ * (flashinfer/cache_manager.py:103-140, 196-213). */
+typedef struct pts_kv_compact_args {
+  void* kv_pool;
+  int num_layers, max_pages, page_len, num_kv_heads, head_dim, elem_bytes;
+  const int32_t* page_indptr;
+  const int32_t* page_indices;
+  const int32_t* offsets;
+  int32_t* new_kv_len;
+  int32_t* new_last_page_len;
+} pts_kv_compact_args;
+
+/* pts_accept_greedy / pts_accept_traversal followed, in the same launch, by
+ * the KV compaction described by *compact (NULL: none). */
+int pts_accept_greedy_compact(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                              const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                              int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
+                              int32_t* out_hidden, int32_t* out_counts, int out_stride,
+                              void* workspace, size_t workspace_bytes,
+                              const pts_kv_compact_args* compact, pts_stream_t stream);
+int pts_accept_traversal_compact(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                                 const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                                 int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                                 float temperature, float top_p, int do_sample, uint64_t philox_seed,
+                                 uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                                 int32_t* out_counts, int out_stride, void* workspace,
+                                 size_t workspace_bytes, const pts_kv_compact_args* compact,
+                                 pts_stream_t stream);
+
 /* verify_tree_exact / verify_tree_traversal over fp32 logits (small fp32
  * models, for example the reference's 2-layer configuration): the
  * probabilities stay fp32 as torch's softmax of fp32 logits does

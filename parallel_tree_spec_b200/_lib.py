@@ -26,6 +26,14 @@ _lib = None
 
 i32, i64, u64, f32, sz, vp = C.c_int32, C.c_int64, C.c_uint64, C.c_float, C.c_size_t, C.c_void_p
 
+class KvCompactArgs(C.Structure):
+    """pts_kv_compact_args: the KV compaction an acceptance launch performs."""
+    _fields_ = [("kv_pool", C.c_void_p), ("num_layers", C.c_int), ("max_pages", C.c_int), ("page_len", C.c_int),
+                ("num_kv_heads", C.c_int), ("head_dim", C.c_int), ("elem_bytes", C.c_int),
+                ("page_indptr", C.c_void_p), ("page_indices", C.c_void_p), ("offsets", C.c_void_p),
+                ("new_kv_len", C.c_void_p), ("new_last_page_len", C.c_void_p)]
+
+
 SIGNATURES = {
     "pts_last_error": (C.c_char_p, []),
     "pts_version": (C.c_int, []),
@@ -34,6 +42,10 @@ SIGNATURES = {
                                     C.c_int, vp, sz, vp]),
     "pts_accept_traversal": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, f32, f32,
                                        C.c_int, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
+    "pts_accept_greedy_compact": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, vp, vp,
+                                            vp, C.c_int, vp, sz, vp, vp]),
+    "pts_accept_traversal_compact": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, f32,
+                                               f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp, vp]),
     "pts_accept_traversal_noalloc": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64,
                                                f32, f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp]),
     "pts_accept_shard_partials": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,

@@ -97,6 +97,9 @@ struct AcceptParams {
   const float* topp_thresh;  // per row: smallest (scaled) logit value inside the nucleus
   const float* topp_mass;    // per row: sum of exp(x - m) over the nucleus
   const float* logits_f32;   // fp32 logits (instead of bf16): probabilities stay fp32
+  // KV compaction of the accepted paths by the walks (pts_accept_*_compact)
+  int compact;
+  pts_kv_compact_args cp;
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -311,6 +314,70 @@ __device__ void write_counts(const AcceptParams& p, int b, int n_out, int total,
   c[1] = total;
   c[2] = acc;
   c[3] = node;
+}
+
+// KV compaction of request b's accepted path by one warp, right after its
+// walk stored the hidden indices and counts (pts_kv_compact's semantics:
+// slot offsets[b] + hidden[i] -> offsets[b] + i for every layer, K and V, and
+// head, i < count).  Entries go in order of i, each one's rows spread over the
+// lanes.  A path's hidden indices rise (hidden[i] >= i; the bonus entry
+// repeats the last node), so a slot is written only after every entry that
+// reads it, which gives pts_kv_compact's staged result without staging.
+__device__ void compact_request_warp(const AcceptParams& p, int b) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  const pts_kv_compact_args& a = p.cp;
+  const int na = min(max(p.out_counts[(int64_t)b * 4], 0), p.out_stride);
+  const int32_t* acc = p.out_hidden + (int64_t)b * p.out_stride;
+  const int off = a.offsets[b];
+  const int p0 = a.page_indptr[b], np = a.page_indptr[b + 1] - p0;
+  const int head_bytes = a.head_dim * a.elem_bytes, vec = head_bytes / 16;
+  const int64_t row_bytes = (int64_t)a.num_kv_heads * head_bytes;
+  const int64_t layer_bytes = (int64_t)a.max_pages * 2 * a.page_len * row_bytes;
+  const int per_kv = a.num_kv_heads * vec;                // 16-byte pieces of one slot's K (or V) row
+  const int items = a.num_layers * 2 * per_kv;
+  // the path's slots lie in pages off / page_len onward: lane l holds the l-th
+  // of them and the l-th hidden index, so an entry needs no dependent lookups
+  // (paths longer than 32 entries or windows wider than 32 pages look up)
+  const int pg0 = off >= 0 ? off / a.page_len : 0;
+  int my_page = -1;
+  if (pg0 + lane < np) {
+    const int pg = a.page_indices[p0 + pg0 + lane];
+    my_page = (pg >= 0 && pg < a.max_pages) ? pg : -1;
+  }
+  const int my_src = lane < na ? acc[lane] : 0;
+  auto page_of = [&](int slot) -> int {
+    const int pi = slot / a.page_len;
+    int page = __shfl_sync(0xffffffffu, my_page, (pi - pg0) & 31);
+    if (slot < 0 || pi >= np) return -1;
+    if (pi < pg0 || pi - pg0 >= 32) {
+      page = a.page_indices[p0 + pi];
+      page = (page >= 0 && page < a.max_pages) ? page : -1;
+    }
+    return page;
+  };
+  for (int i = 0; i < na; ++i) {
+    const int src = i < 32 ? __shfl_sync(0xffffffffu, my_src, i) : acc[i];
+    if (src != i) {
+      const int sp = page_of(off + src), dp = page_of(off + i);
+      if (sp >= 0 && dp >= 0) {
+        const int ss = (off + src) % a.page_len, ds = (off + i) % a.page_len;
+        for (int e = lane; e < items; e += 32) {
+          const int layer = e / (2 * per_kv), kv = (e / per_kv) & 1, q = e % per_kv;
+          char* base = (char*)a.kv_pool + layer * layer_bytes + (int64_t)q * 16;
+          const uint4 x = *(const uint4*)(base + ((int64_t)(sp * 2 + kv) * a.page_len + ss) * row_bytes);
+          *(uint4*)(base + ((int64_t)(dp * 2 + kv) * a.page_len + ds) * row_bytes) = x;
+        }
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    const int len = off + na;
+    if (a.new_kv_len) a.new_kv_len[b] = len;
+    if (a.new_last_page_len) a.new_last_page_len[b] = len == 0 ? 0 : (len - 1) % a.page_len + 1;
+  }
+  __syncwarp();
 }
 
 // Correctly rounded a / b for a >= 0 and b > 0 normal, without sending a zero
@@ -749,6 +816,7 @@ template <bool kLazy = false, class G>
 __device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
   if (n <= 0 || n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
+    if (!kLazy && p.compact && g.rank() < 32) compact_request_warp(p, b);   // (the lengths)
     return false;
   }
   int* cnt = reinterpret_cast<int*>(w.val);               // child counts, then slot bases
@@ -782,6 +850,7 @@ __device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const 
   g.sync();
   if (bad) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
+    if (!kLazy && p.compact && g.rank() < 32) compact_request_warp(p, b);
     return false;
   }
   if (g.rank() < 32) {
@@ -894,12 +963,14 @@ __device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const 
     g.sync();
     if (late) {
       if (g.rank() == 0) write_counts(p, b, -3, 0, 0, 0);
+      if (p.compact && g.rank() < 32) compact_request_warp(p, b);
       return false;
     }
     if (g.rank() < 32) walk_traversal_warp(p, b, lo, n, w);
   } else if (g.rank() < 32) {
     walk_greedy_warp(p, b, lo, w);
   }
+  if (p.compact && g.rank() < 32) compact_request_warp(p, b);
   g.sync();
   return false;
 }
@@ -1708,6 +1779,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       named_barrier(1, 64);
       if (b < 0) break;
       if (go) walk_traversal_warp<true>(p, b, lo, n, w);
+      if (p.compact) compact_request_warp(p, b);
       if (lane == 0) *(volatile int*)&ctl.walk_done = 1;
       named_barrier(2, 64);
     }
@@ -2228,12 +2300,38 @@ extern "C" size_t pts_accept_workspace_size(int num_rows, int vocab) {
   return ws_layout(num_rows, vocab, &a, &b, &c, &d) + topp_ws_bytes(num_rows);
 }
 
+// The compaction arguments into p (nullptr: none), checked like pts_kv_compact's.
+static int set_compact(AcceptParams& p, const pts_kv_compact_args* c) {
+  if (!c) return PTS_OK;
+  PTS_CHECK_ARG(c->kv_pool && c->page_indptr && c->page_indices && c->offsets, "null compaction pointer");
+  PTS_CHECK_ARG(c->elem_bytes == 2 || c->elem_bytes == 4, "elem_bytes must be 2 or 4");
+  PTS_CHECK_ARG(c->num_layers > 0 && c->max_pages > 0 && c->page_len > 0 && c->num_kv_heads > 0 && c->head_dim > 0,
+                "bad compaction shape");
+  PTS_CHECK_ARG((c->head_dim * c->elem_bytes) % 16 == 0, "head_dim * elem_bytes must be a multiple of 16");
+  PTS_CHECK_ARG(((uintptr_t)c->kv_pool & 15) == 0, "pool must be 16-byte aligned");
+  p.compact = 1;
+  p.cp = *c;
+  return PTS_OK;
+}
+
 extern "C" int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
                                  const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
                                  int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
                                  int32_t* out_hidden, int32_t* out_counts, int out_stride,
                                  void* workspace, size_t workspace_bytes, pts_stream_t stream) {
+  return pts_accept_greedy_compact(logits, row_stride, row_indptr, parents, tokens, batch, num_rows, vocab,
+                                   max_nodes, eos_token_id, out_tokens, out_hidden, out_counts, out_stride, workspace,
+                                   workspace_bytes, nullptr, stream);
+}
+
+extern "C" int pts_accept_greedy_compact(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                                         const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
+                                         int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
+                                         int32_t* out_hidden, int32_t* out_counts, int out_stride,
+                                         void* workspace, size_t workspace_bytes,
+                                         const pts_kv_compact_args* compact, pts_stream_t stream) {
   AcceptParams p{};
+  if (int rc = set_compact(p, compact)) return rc;
   p.logits = logits;
   p.row_stride = row_stride;
   p.row_indptr = row_indptr;
@@ -2259,9 +2357,24 @@ extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, 
                                     uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
                                     int32_t* out_counts, int out_stride, void* workspace,
                                     size_t workspace_bytes, pts_stream_t stream) {
+  return pts_accept_traversal_compact(logits, row_stride, row_indptr, parents, tokens, draft_probs, batch, num_rows,
+                                      vocab, max_nodes, eos_token_id, temperature, top_p, do_sample, philox_seed,
+                                      philox_offset, out_tokens, out_hidden, out_counts, out_stride, workspace,
+                                      workspace_bytes, nullptr, stream);
+}
+
+extern "C" int pts_accept_traversal_compact(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
+                                            const int32_t* parents, const int32_t* tokens, const float* draft_probs,
+                                            int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
+                                            float temperature, float top_p, int do_sample, uint64_t philox_seed,
+                                            uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
+                                            int32_t* out_counts, int out_stride, void* workspace,
+                                            size_t workspace_bytes, const pts_kv_compact_args* compact,
+                                            pts_stream_t stream) {
   if (!draft_probs) return set_error(PTS_ERR_INVALID, "null draft_probs");
   if (!(top_p > 0.0f && top_p <= 1.0f)) return set_error(PTS_ERR_INVALID, "top_p must be in (0, 1]");
   AcceptParams p{};
+  if (int rc = set_compact(p, compact)) return rc;
   p.logits = logits;
   p.row_stride = row_stride;
   p.row_indptr = row_indptr;

@@ -7,6 +7,7 @@ raises.
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 from typing import Dict, Optional, Tuple
 
@@ -59,13 +60,38 @@ def _accept_common(logits, row_indptr, parents, tokens):
     return dev, _i32(row_indptr, "row_indptr"), _i32(parents, "parents"), _i32(tokens, "tokens")
 
 
+def kv_compact_args(pool: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor,
+                    offsets: torch.Tensor, new_kv_len: Optional[torch.Tensor] = None,
+                    new_last_page_len: Optional[torch.Tensor] = None):
+    """The ``compact=`` argument of the acceptance functions: compact the
+    accepted paths of ``pool`` [L, max_pages, 2, page_len, Hkv, D] in the same
+    launch (``kv_compact`` with the acceptance's hidden indices and counts).
+    The index tensors must stay alive until the launch has run."""
+    _need_cuda(pool, page_indptr, page_indices, offsets)
+    if pool.dim() != 6 or pool.shape[2] != 2 or not pool.is_contiguous():
+        raise ValueError("pool must be a contiguous [L, max_pages, 2, page_len, Hkv, D] tensor")
+    L, P, _, pl, H, D = pool.shape
+    keep = [_i32(page_indptr, "indptr"), _i32(page_indices, "indices"), _i32(offsets, "offsets")]
+    for t in (new_kv_len, new_last_page_len):
+        if t is not None and (t.dtype != torch.int32 or not t.is_contiguous()):
+            raise ValueError("new_kv_len / new_last_page_len must be contiguous int32")
+    args = _lib.KvCompactArgs(pool.data_ptr(), L, P, pl, H, D, pool.element_size(), keep[0].data_ptr(),
+                              keep[1].data_ptr(), keep[2].data_ptr(),
+                              new_kv_len.data_ptr() if new_kv_len is not None else None,
+                              new_last_page_len.data_ptr() if new_last_page_len is not None else None)
+    args._keep = keep
+    return args
+
+
 def accept_greedy(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch.Tensor, tokens: torch.Tensor,
                   eos_token_id: Optional[int] = None, max_nodes: Optional[int] = None,
-                  out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+                  out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None, compact=None):
     """Greedy acceptance (``verify_tree_exact``) for a batch of trees.
 
     Returns (tokens [B, S] int32, hidden [B, S] int32, counts [B, 4] int32)
-    with counts = (n_out, total_len, accept_len, accepted_node).
+    with counts = (n_out, total_len, accept_len, accepted_node).  With
+    ``compact`` (from ``kv_compact_args``, bf16 logits) the same launch also
+    compacts the accepted paths' KV.
     """
     dev, row_indptr, parents, tokens = _accept_common(logits, row_indptr, parents, tokens)
     B = row_indptr.numel() - 1
@@ -80,10 +106,18 @@ def accept_greedy(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch
         ot, oh, oc = out
     wsz = _lib.lib().pts_accept_workspace_size(R, V)
     ws = workspace(dev, "accept", wsz)
+    eos = -1 if eos_token_id is None else int(eos_token_id)
+    if compact is not None:
+        if logits.dtype != torch.bfloat16:
+            raise ValueError("compact takes bf16 logits in this build")
+        _lib.call("pts_accept_greedy_compact", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
+                  parents.data_ptr(), tokens.data_ptr(), B, R, V, mn, eos, ot.data_ptr(), oh.data_ptr(),
+                  oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), C.byref(compact), _stream(dev))
+        return ot, oh, oc
     fn = "pts_accept_greedy_f32" if logits.dtype == torch.float32 else "pts_accept_greedy"
     _lib.call(fn, logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(), parents.data_ptr(),
-              tokens.data_ptr(), B, R, V, mn, -1 if eos_token_id is None else int(eos_token_id), ot.data_ptr(),
-              oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
+              tokens.data_ptr(), B, R, V, mn, eos, ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), ot.shape[1],
+              ws.data_ptr(), ws.numel(), _stream(dev))
     return ot, oh, oc
 
 
@@ -91,9 +125,11 @@ def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
                      draft_probs: torch.Tensor, eos_token_id: Optional[int] = None, temperature: float = 1.0,
                      top_p: float = 1.0, do_sample: bool = False, seed: int = 0, offset: int = 0,
                      max_nodes: Optional[int] = None,
-                     out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+                     out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None, compact=None):
     """Traversal verification (``verify_tree_traversal``) for a batch of trees;
-    the per-iteration uniform of request b is Philox stream (seed, offset, b)."""
+    the per-iteration uniform of request b is Philox stream (seed, offset, b).
+    With ``compact`` (from ``kv_compact_args``, bf16 logits) the same launch
+    also compacts the accepted paths' KV."""
     dev, row_indptr, parents, tokens = _accept_common(logits, row_indptr, parents, tokens)
     if draft_probs.dtype != torch.float32:
         draft_probs = draft_probs.to(torch.float32)
@@ -112,19 +148,23 @@ def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
     wsz = _lib.lib().pts_accept_workspace_size(R, V)
     ws = workspace(dev, "accept", wsz)
     if logits.dtype == torch.float32:
-        if top_p < 1.0 or do_sample:
-            raise ValueError("top_p < 1 and do_sample take bf16 logits in this build")
+        if top_p < 1.0 or do_sample or compact is not None:
+            raise ValueError("top_p < 1, do_sample and compact take bf16 logits in this build")
         _lib.call("pts_accept_traversal_f32", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
                   parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr(), B, R, V, mn,
                   -1 if eos_token_id is None else int(eos_token_id), float(temperature), int(seed) & (2 ** 64 - 1),
                   int(offset) & (2 ** 64 - 1), ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), ot.shape[1],
                   ws.data_ptr(), ws.numel(), _stream(dev))
         return ot, oh, oc
-    _lib.call("pts_accept_traversal", logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(),
-              parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr(), B, R, V, mn,
-              -1 if eos_token_id is None else int(eos_token_id), float(temperature), float(top_p),
-              1 if do_sample else 0, int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), ot.data_ptr(),
-              oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
+    args = (logits.data_ptr(), logits.stride(0), row_indptr.data_ptr(), parents.data_ptr(), tokens.data_ptr(),
+            draft_probs.data_ptr(), B, R, V, mn, -1 if eos_token_id is None else int(eos_token_id),
+            float(temperature), float(top_p), 1 if do_sample else 0, int(seed) & (2 ** 64 - 1),
+            int(offset) & (2 ** 64 - 1), ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), ot.shape[1], ws.data_ptr(),
+            ws.numel())
+    if compact is not None:
+        _lib.call("pts_accept_traversal_compact", *args, C.byref(compact), _stream(dev))
+    else:
+        _lib.call("pts_accept_traversal", *args, _stream(dev))
     return ot, oh, oc
 
 

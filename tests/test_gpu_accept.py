@@ -177,3 +177,54 @@ def test_bad_arguments_raise():
         K.accept_traversal(x, ind, par, tok, torch.ones(4, device=DEV), temperature=0.0)
     with pytest.raises(ValueError):
         K.accept_greedy(x.cpu(), ind, par, tok)
+
+
+@pytest.mark.parametrize("method,B,max_nodes", [("traversal", 16, 65), ("traversal", 30, 65), ("exact", 16, 65),
+                                                ("traversal", 6, None)])
+def test_accept_with_compaction_matches_separate_launch(method, B, max_nodes):
+    """Acceptance with compact= (each walk compacts its request's KV in the
+    same launch) = acceptance, then pts_kv_compact: the same outputs, pool
+    bytes and new lengths, over a 2-layer pool with scattered pages."""
+    rng = np.random.default_rng(B * 3 + (max_nodes or 0))
+    V = 16384
+    trees = [wl.make_tree(rng, 8, 8, V) for _ in range(B)]
+    logits = [wl.make_logits(rng, t, V, plant=1.0, soft=(method == "traversal")) for t in trees]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    x = bf16(np.concatenate(logits, 0)).to(DEV)
+    L, Hkv, D, pl = 2, 2, 64, 16
+    prefix = rng.integers(0, 100, size=B)
+    kv_len = prefix + np.array([t.size for t in trees])
+    npages = (kv_len + pl - 1) // pl
+    P = int(npages.sum()) + 5
+    perm = rng.permutation(P)[:int(npages.sum())].astype(np.int32)
+    pind = torch.from_numpy(np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)).to(DEV)
+    pidx = torch.from_numpy(perm).to(DEV)
+    offs = torch.from_numpy(prefix.astype(np.int32)).to(DEV)
+    pool0 = torch.randint(-2 ** 15, 2 ** 15, (L, P, 2, pl, Hkv, D), dtype=torch.int16,
+                          generator=torch.Generator().manual_seed(B)).view(torch.bfloat16).to(DEV)
+    args = (x, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV), torch.from_numpy(tok).to(DEV))
+    kw = dict(max_nodes=max_nodes)
+    if method == "traversal":
+        args = args + (torch.from_numpy(dp).to(DEV),)
+        kw.update(seed=21, offset=4)
+    fn = K.accept_traversal if method == "traversal" else K.accept_greedy
+    # separate launches
+    pool_a = pool0.clone()
+    ot_a, oh_a, oc_a = fn(*args, **kw)
+    nl_a = torch.zeros(B, dtype=torch.int32, device=DEV)
+    lp_a = torch.zeros(B, dtype=torch.int32, device=DEV)
+    K.kv_compact(pool_a, pind, pidx, oh_a, oc_a, offs, nl_a, lp_a)
+    # fused
+    pool_b = pool0.clone()
+    nl_b = torch.zeros(B, dtype=torch.int32, device=DEV)
+    lp_b = torch.zeros(B, dtype=torch.int32, device=DEV)
+    ca = K.kv_compact_args(pool_b, pind, pidx, offs, nl_b, lp_b)
+    ot_b, oh_b, oc_b = fn(*args, **kw, compact=ca)
+    torch.cuda.synchronize()
+    assert torch.equal(oc_a, oc_b)
+    for b in range(B):
+        n = int(oc_a[b, 0])
+        assert torch.equal(ot_a[b, :n], ot_b[b, :n]) and torch.equal(oh_a[b, :n], oh_b[b, :n])
+    assert torch.equal(nl_a, nl_b) and torch.equal(lp_a, lp_b)
+    assert torch.equal(pool_a.view(torch.int16), pool_b.view(torch.int16))
+    assert int((oc_a[:, 0] > 1).sum()) > 0          # some paths really move rows
