@@ -304,6 +304,38 @@ int pts_tree_prepare_append(const int32_t* parents, const int32_t* qo_indptr, co
                             int num_tokens, int num_kv_heads, int head_dim, int page_len, int max_pages,
                             int elem_bytes, pts_stream_t stream);
 
+/* pts_kv_append with the rotary position embedding applied on the way (the
+ * per-layer form of pts_tree_prepare_append_rope, for callers that have the
+ * batch indices and positions): k rotated into the cache, v copied, q
+ * rotated into q_out [num_tokens, Hq, D] (contiguous); the same rounding
+ * as pts_tree_prepare_append_rope.  Replaces apply_rotary_pos_emb +
+ * append_paged_kv_cache (flashinfer/attention.py:83-88,
+ * flashinfer/attention_wrapper.py:201-212). */
+int pts_kv_append_rope(const void* q, int64_t q_token_stride, void* q_out, int num_qo_heads, const void* k,
+                       const void* v, int64_t k_token_stride, int64_t v_token_stride, const void* cos,
+                       const void* sin, int64_t cos_sin_token_stride, void* kv_layer,
+                       const int32_t* batch_indices, const int32_t* positions, const int32_t* page_indptr,
+                       const int32_t* page_indices, int num_tokens, int num_kv_heads, int head_dim,
+                       int page_len, int max_pages, int elem_bytes, pts_stream_t stream);
+
+/* pts_tree_prepare_append with the rotary position embedding applied on the
+ * way: the tree tokens' k [num_tokens, Hkv, D] are rotated into the cache, v
+ * copied, and q [num_tokens, Hq, D] rotated into q_out (contiguous), as
+ * x * cos + rotate_half(x) * sin with each product and the sum rounded to the
+ * element type (bf16 or fp32), as the reference's model applies
+ * apply_rotary_pos_emb before the append (flashinfer/attention.py:83-88).
+ * cos / sin [num_tokens, D] are the model's position embeddings of the tree
+ * tokens (token stride cos_sin_token_stride elements); head_dim * elem_bytes
+ * must be a multiple of 32. */
+int pts_tree_prepare_append_rope(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens,
+                                 int batch, int mask_words, uint64_t* mask_bits, int32_t* batch_indices,
+                                 int32_t* positions, const void* q, int64_t q_token_stride, void* q_out,
+                                 int num_qo_heads, const void* k, const void* v, int64_t k_token_stride,
+                                 int64_t v_token_stride, const void* cos, const void* sin,
+                                 int64_t cos_sin_token_stride, void* kv_layer, const int32_t* page_indptr,
+                                 const int32_t* page_indices, int num_tokens, int num_kv_heads, int head_dim,
+                                 int page_len, int max_pages, int elem_bytes, pts_stream_t stream);
+
 /* Pack a boolean custom mask [sum_b N_b * kv_len_b] (FlashInfer's flattened
  * custom_mask, flashinfer/attention_wrapper.py:141) into tree bitmasks.
  * Columns before kv_len_b - N_b must all be true; *bad_rows (device int,

@@ -17,6 +17,11 @@ Restates (parallel_tree_spec, ``src/parallel_tree_spec/flashinfer``):
   follows the request's page table (logical slots); identical to the flat
   rule when the request owns physical pages 0..n-1 in order.
 
+* ``rope_bf16``          -- ``apply_rotary_pos_emb`` as the reference's model
+  applies it to q and k before the append (``flashinfer/attention.py:83``):
+  ``x * cos + rotate_half(x) * sin`` in the activation dtype, each torch
+  elementwise op rounding its fp32 result to bf16.
+
 Pools are NumPy arrays ``[L, max_pages, 2, page_len, Hkv, D]`` of any dtype
 (bf16 kept as uint16 bits): every operation here is a bit copy.
 """
@@ -86,3 +91,28 @@ def request_reorder(cache: np.ndarray, page_indices: List[int], kv_len: int, bea
     kept = list(page_indices[:need])
     freed = list(page_indices[need:]) if len(page_indices) > need else []
     return new_len, last, kept, freed
+
+
+def _bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bits (finite inputs)."""
+    u = x.astype(np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def rope_bf16(x_bits: np.ndarray, cos_bits: np.ndarray, sin_bits: np.ndarray) -> np.ndarray:
+    """x [..., T, H, D], cos / sin [T, D], all bf16 bits: x * cos +
+    rotate_half(x) * sin with rotate_half(x) = cat(-x[D/2:], x[:D/2]); every
+    product and the sum rounded to bf16 (products of two bf16 values and the
+    fp32 sum are what torch computes before rounding)."""
+    x = _bf16_to_f32(x_bits)
+    c = _bf16_to_f32(cos_bits)[:, None, :]
+    s = _bf16_to_f32(sin_bits)[:, None, :]
+    h = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+    p1 = _bf16_to_f32(_f32_to_bf16((x * c).astype(np.float32)))
+    p2 = _bf16_to_f32(_f32_to_bf16((rot * s).astype(np.float32)))
+    return _f32_to_bf16((p1 + p2).astype(np.float32))

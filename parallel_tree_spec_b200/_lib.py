@@ -65,6 +65,11 @@ SIGNATURES = {
                                  vp, C.c_int, vp, C.c_int, C.c_int, vp, vp, vp]),
     "pts_tree_mask_from_parents": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "pts_tree_prepare": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, vp, vp, vp, vp]),
+    "pts_kv_append_rope": (C.c_int, [vp, i64, vp, C.c_int, vp, vp, i64, i64, vp, vp, i64, vp, vp, vp, vp, vp,
+                                     C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+    "pts_tree_prepare_append_rope": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, vp, vp, vp, vp, i64, vp, C.c_int, vp, vp,
+                                               i64, i64, vp, vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, vp]),
     "pts_tree_prepare_append": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, vp, vp, vp, vp, vp, i64, i64, vp, vp, vp,
                                           C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
     "pts_tree_mask_from_bool": (C.c_int, [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]),

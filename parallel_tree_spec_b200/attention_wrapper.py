@@ -21,7 +21,7 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 from enum import Enum
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -123,16 +123,29 @@ class BeFlashinferWrapper:
     # --------------------------------------------------------------- compute
     def computeAttention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cacheData: torch.Tensor, mode: str,
                          batchPosition: KvCacheBatchPosition, rotaryParams: AttentionRotaryParams, layer_idx: int,
-                         appendBatchPosition: Optional[KvCacheBatchPosition] = None):
+                         appendBatchPosition: Optional[KvCacheBatchPosition] = None,
+                         position_embeddings: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
         """Append K/V, then attention with the planned mask; returns
-        [tokens, hidden] (``attention_wrapper.py:218-252``)."""
+        [tokens, hidden] (``attention_wrapper.py:218-252``).  With
+        ``position_embeddings`` = (cos, sin) [tokens, D] (the model's, for
+        these tokens), q and k are taken before the rotary embedding and the
+        append applies it (to k on its way into the cache, to q for the
+        attention), replacing the model's ``apply_rotary_pos_emb`` call."""
         if mode not in ("prefill", "tree", "decode"):
             raise ValueError(f"Invalid attention mode: {mode}")
         plan = self._plan
         if plan is None:
             raise RuntimeError("prepareAttention must be called before computeAttention")
         append_pos = appendBatchPosition if appendBatchPosition is not None else batchPosition
-        self.append_kv_cache(q, k, v, append_pos, cacheData, self.page_len)
+        if position_embeddings is not None:
+            cos, sin = position_embeddings
+            D = cacheData.shape[-1]
+            q = K.kv_append_rope(q.reshape(q.shape[0], -1, D), k.reshape(k.shape[0], -1, D),
+                                 v.reshape(v.shape[0], -1, D), cos.reshape(-1, D), sin.reshape(-1, D), cacheData,
+                                 append_pos.batch_indices, append_pos.positions, append_pos.kv_page_indptr,
+                                 append_pos.kv_page_indices)
+        else:
+            self.append_kv_cache(q, k, v, append_pos, cacheData, self.page_len)
         bp = plan["bp"]
         out = K.tree_attention(q.contiguous(), cacheData, bp.seq_indptr, bp.kv_page_indptr, bp.kv_page_indices,
                                bp.kv_last_page_len, plan["bits"], plan["max_qo"], plan["max_kv"],

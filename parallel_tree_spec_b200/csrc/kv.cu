@@ -3,6 +3,8 @@
 // All of these are byte movers bounded by HBM bandwidth: 16-byte vector
 // accesses, one CTA per (token) or (request, layer, K|V, head) slice, page
 // slots resolved through the request's page table.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace pts {
@@ -177,6 +179,63 @@ __global__ void tree_prepare_kernel(const int32_t* __restrict__ parents, const i
 // seq_lens[b] - n_b + i as the positions), so the two halves do not wait on
 // each other.
 constexpr int kPrepSmemIndptr = 1024;    // requests whose qo_indptr the append CTAs stage in shared memory
+
+// Rotary position embedding applied by the append (pts_tree_prepare_append_rope).
+struct RopeArgs {
+  const char* q;             // [T, Hq, D] at q_stride bytes per token
+  int64_t q_stride;
+  char* q_out;               // [T, Hq, D] contiguous
+  int hq;
+  const char* cos;           // [T, D] at cs_stride bytes per token (the model's position embeddings)
+  const char* sin;
+  int64_t cs_stride;
+  int head_dim;
+};
+
+__device__ __forceinline__ float bf16_at(const uint4& v, int e) {
+  const uint32_t w = (&v.x)[e >> 1];
+  return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+__device__ __forceinline__ float round_bf16f(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One 16-byte piece (elements i0 .. i0 + 16/elem - 1) of a rotated head row,
+// x * cos + rotate_half(x) * sin with rotate_half(x) = cat(-x[D/2:], x[:D/2])
+// (apply_rotary_pos_emb of the reference's model, attention.py:83).  Each
+// product and the sum are rounded to the element type, as torch's eager
+// elementwise operations round them.
+template <int kElem>
+__device__ __forceinline__ uint4 rope_piece(const char* x_row, const char* c_row, const char* s_row, int D, int i0) {
+  const int half = D / 2;
+  const int j0 = i0 < half ? i0 + half : i0 - half;
+  const float sign = i0 < half ? -1.0f : 1.0f;
+  const uint4 xv = *(const uint4*)(x_row + i0 * kElem), pv = *(const uint4*)(x_row + j0 * kElem);
+  const uint4 cv = *(const uint4*)(c_row + i0 * kElem), sv = *(const uint4*)(s_row + i0 * kElem);
+  uint4 o;
+  if (kElem == 2) {
+    uint32_t* ow = &o.x;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float r[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float p1 = round_bf16f(__fmul_rn(bf16_at(xv, e + h), bf16_at(cv, e + h)));
+        const float p2 = round_bf16f(__fmul_rn(sign * bf16_at(pv, e + h), bf16_at(sv, e + h)));
+        r[h] = __fadd_rn(p1, p2);
+      }
+      const __nv_bfloat162 b = __floats2bfloat162_rn(r[0], r[1]);
+      ow[e >> 1] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+  } else {
+    const float* x = (const float*)&xv; const float* pp = (const float*)&pv;
+    const float* c = (const float*)&cv; const float* sn = (const float*)&sv;
+    float* of = (float*)&o;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) of[e] = __fadd_rn(__fmul_rn(x[e], c[e]), __fmul_rn(sign * pp[e], sn[e]));
+  }
+  return o;
+}
+
+template <bool kRope, int kElem>
 __global__ void tree_prepare_append_kernel(const int32_t* __restrict__ parents, const int32_t* __restrict__ qo_indptr,
                                            const int32_t* __restrict__ seq_lens, int batch, int words,
                                            uint64_t* __restrict__ bits, int32_t* __restrict__ batch_indices,
@@ -184,7 +243,7 @@ __global__ void tree_prepare_append_kernel(const int32_t* __restrict__ parents, 
                                            const char* __restrict__ v, int64_t k_stride_b, int64_t v_stride_b,
                                            char* __restrict__ layer, const int32_t* __restrict__ page_indptr,
                                            const int32_t* __restrict__ page_indices, int row_bytes, int page_len,
-                                           int max_pages) {
+                                           int max_pages, RopeArgs rope) {
   __shared__ int16_t sp[PTS_MAX_TREE_NODES];
   __shared__ int32_t sq[kPrepSmemIndptr + 1];
   if ((int)blockIdx.x < batch) {
@@ -245,8 +304,68 @@ __global__ void tree_prepare_append_kernel(const int32_t* __restrict__ parents, 
   char* vd = layer + ((int64_t)(page * 2 + 1) * page_len + slot) * row_bytes;
   const char* ks = k + (int64_t)t * k_stride_b;
   const char* vs = v + (int64_t)t * v_stride_b;
-  for (int o = threadIdx.x * 16; o < row_bytes; o += blockDim.x * 16) {
-    *(uint4*)(kd + o) = *(const uint4*)(ks + o);
+  if (!kRope) {
+    for (int o = threadIdx.x * 16; o < row_bytes; o += blockDim.x * 16) {
+      *(uint4*)(kd + o) = *(const uint4*)(ks + o);
+      *(uint4*)(vd + o) = *(const uint4*)(vs + o);
+    }
+    return;
+  }
+  // K rotated into the cache, V copied, Q rotated into q_out
+  const int D = rope.head_dim, per_head = D * kElem / 16;
+  const char* cr = rope.cos + (int64_t)t * rope.cs_stride;
+  const char* sr = rope.sin + (int64_t)t * rope.cs_stride;
+  const int hkv = row_bytes / (D * kElem);
+  for (int pc = threadIdx.x; pc < hkv * per_head; pc += blockDim.x) {
+    const int h = pc / per_head, i0 = (pc % per_head) * (16 / kElem);
+    const int64_t o = (int64_t)h * D * kElem + i0 * kElem;
+    *(uint4*)(kd + o) = rope_piece<kElem>(ks + (int64_t)h * D * kElem, cr, sr, D, i0);
+    *(uint4*)(vd + o) = *(const uint4*)(vs + o);
+  }
+  const char* qs = rope.q + (int64_t)t * rope.q_stride;
+  char* qd = rope.q_out + (int64_t)t * rope.hq * D * kElem;
+  for (int pc = threadIdx.x; pc < rope.hq * per_head; pc += blockDim.x) {
+    const int h = pc / per_head, i0 = (pc % per_head) * (16 / kElem);
+    *(uint4*)(qd + (int64_t)h * D * kElem + i0 * kElem) = rope_piece<kElem>(qs + (int64_t)h * D * kElem, cr, sr, D, i0);
+  }
+}
+
+// pts_kv_append with the rotary embedding: token t's k rotated into its
+// slot, v copied, q rotated into q_out.
+template <int kElem>
+__global__ void kv_append_rope_kernel(const char* __restrict__ k, const char* __restrict__ v, int64_t k_stride_b,
+                                      int64_t v_stride_b, char* __restrict__ layer,
+                                      const int32_t* __restrict__ batch_indices,
+                                      const int32_t* __restrict__ positions, const int32_t* __restrict__ page_indptr,
+                                      const int32_t* __restrict__ page_indices, int row_bytes, int page_len,
+                                      int max_pages, RopeArgs rope) {
+  const int t = blockIdx.x;
+  const int D = rope.head_dim, per_head = D * kElem / 16;
+  const char* cr = rope.cos + (int64_t)t * rope.cs_stride;
+  const char* sr = rope.sin + (int64_t)t * rope.cs_stride;
+  const char* qs = rope.q + (int64_t)t * rope.q_stride;
+  char* qd = rope.q_out + (int64_t)t * rope.hq * D * kElem;
+  for (int pc = threadIdx.x; pc < rope.hq * per_head; pc += blockDim.x) {
+    const int h = pc / per_head, i0 = (pc % per_head) * (16 / kElem);
+    *(uint4*)(qd + (int64_t)h * D * kElem + i0 * kElem) = rope_piece<kElem>(qs + (int64_t)h * D * kElem, cr, sr, D, i0);
+  }
+  const int b = batch_indices[t];
+  const int pos = positions[t];
+  const int lo = page_indptr[b], hi = page_indptr[b + 1];
+  const int pi = pos / page_len;
+  if (pos < 0 || lo + pi >= hi) return;
+  const int page = page_indices[lo + pi];
+  if (page < 0 || page >= max_pages) return;
+  const int slot = pos % page_len;
+  char* kd = layer + ((int64_t)(page * 2 + 0) * page_len + slot) * row_bytes;
+  char* vd = layer + ((int64_t)(page * 2 + 1) * page_len + slot) * row_bytes;
+  const char* ks = k + (int64_t)t * k_stride_b;
+  const char* vs = v + (int64_t)t * v_stride_b;
+  const int hkv = row_bytes / (D * kElem);
+  for (int pc = threadIdx.x; pc < hkv * per_head; pc += blockDim.x) {
+    const int h = pc / per_head, i0 = (pc % per_head) * (16 / kElem);
+    const int64_t o = (int64_t)h * D * kElem + i0 * kElem;
+    *(uint4*)(kd + o) = rope_piece<kElem>(ks + (int64_t)h * D * kElem, cr, sr, D, i0);
     *(uint4*)(vd + o) = *(const uint4*)(vs + o);
   }
 }
@@ -413,9 +532,87 @@ extern "C" int pts_tree_prepare_append(const int32_t* parents, const int32_t* qo
                 "token strides must be multiples of 16 bytes");
   PTS_CHECK_ARG((((uintptr_t)k | (uintptr_t)v | (uintptr_t)kv_layer) & 15) == 0, "pointers must be 16-byte aligned");
   PTS_CHECK_ARG((int64_t)batch + num_tokens <= 0x7fffffff, "too many blocks");
-  tree_prepare_append_kernel<<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
+  tree_prepare_append_kernel<false, 2><<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
       parents, qo_indptr, seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
       (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer, page_indptr,
-      page_indices, row_bytes, page_len, max_pages);
+      page_indices, row_bytes, page_len, max_pages, RopeArgs{});
   return launch_status("tree_prepare_append_kernel");
+}
+
+extern "C" int pts_tree_prepare_append_rope(const int32_t* parents, const int32_t* qo_indptr, const int32_t* seq_lens,
+                                            int batch, int mask_words, uint64_t* mask_bits, int32_t* batch_indices,
+                                            int32_t* positions, const void* q, int64_t q_token_stride, void* q_out,
+                                            int num_qo_heads, const void* k, const void* v, int64_t k_token_stride,
+                                            int64_t v_token_stride, const void* cos, const void* sin,
+                                            int64_t cos_sin_token_stride, void* kv_layer, const int32_t* page_indptr,
+                                            const int32_t* page_indices, int num_tokens, int num_kv_heads,
+                                            int head_dim, int page_len, int max_pages, int elem_bytes,
+                                            pts_stream_t stream) {
+  PTS_CHECK_ARG(parents && qo_indptr && seq_lens && mask_bits && batch_indices && positions, "null pointer");
+  PTS_CHECK_ARG(q && q_out && k && v && cos && sin && kv_layer && page_indptr && page_indices, "null pointer");
+  PTS_CHECK_ARG(batch > 0 && mask_words > 0 && num_tokens >= 0, "bad sizes");
+  PTS_CHECK_ARG(elem_bytes == 2 || elem_bytes == 4, "elem_bytes must be 2 or 4");
+  PTS_CHECK_ARG(num_kv_heads > 0 && num_qo_heads > 0 && page_len > 0 && max_pages > 0, "bad shape");
+  PTS_CHECK_ARG(head_dim > 0 && (head_dim * elem_bytes) % 32 == 0,
+                "head_dim * elem_bytes must be a multiple of 32 (each half of a head in 16-byte pieces)");
+  const int row_bytes = num_kv_heads * head_dim * elem_bytes;
+  PTS_CHECK_ARG((q_token_stride * elem_bytes) % 16 == 0 && (k_token_stride * elem_bytes) % 16 == 0 &&
+                    (v_token_stride * elem_bytes) % 16 == 0 && (cos_sin_token_stride * elem_bytes) % 16 == 0,
+                "token strides must be multiples of 16 bytes");
+  PTS_CHECK_ARG((((uintptr_t)q | (uintptr_t)q_out | (uintptr_t)k | (uintptr_t)v | (uintptr_t)cos | (uintptr_t)sin |
+                  (uintptr_t)kv_layer) & 15) == 0,
+                "pointers must be 16-byte aligned");
+  PTS_CHECK_ARG((int64_t)batch + num_tokens <= 0x7fffffff, "too many blocks");
+  RopeArgs r;
+  r.q = (const char*)q;
+  r.q_stride = q_token_stride * elem_bytes;
+  r.q_out = (char*)q_out;
+  r.hq = num_qo_heads;
+  r.cos = (const char*)cos;
+  r.sin = (const char*)sin;
+  r.cs_stride = cos_sin_token_stride * elem_bytes;
+  r.head_dim = head_dim;
+  auto kernel = elem_bytes == 2 ? tree_prepare_append_kernel<true, 2> : tree_prepare_append_kernel<true, 4>;
+  kernel<<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
+      parents, qo_indptr, seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
+      (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer, page_indptr,
+      page_indices, row_bytes, page_len, max_pages, r);
+  return launch_status("tree_prepare_append_kernel");
+}
+
+extern "C" int pts_kv_append_rope(const void* q, int64_t q_token_stride, void* q_out, int num_qo_heads, const void* k,
+                                  const void* v, int64_t k_token_stride, int64_t v_token_stride, const void* cos,
+                                  const void* sin, int64_t cos_sin_token_stride, void* kv_layer,
+                                  const int32_t* batch_indices, const int32_t* positions, const int32_t* page_indptr,
+                                  const int32_t* page_indices, int num_tokens, int num_kv_heads, int head_dim,
+                                  int page_len, int max_pages, int elem_bytes, pts_stream_t stream) {
+  PTS_CHECK_ARG(q && q_out && k && v && cos && sin && kv_layer && batch_indices && positions && page_indptr &&
+                    page_indices,
+                "null pointer");
+  PTS_CHECK_ARG(elem_bytes == 2 || elem_bytes == 4, "elem_bytes must be 2 or 4");
+  PTS_CHECK_ARG(num_kv_heads > 0 && num_qo_heads > 0 && page_len > 0 && max_pages > 0, "bad shape");
+  PTS_CHECK_ARG(head_dim > 0 && (head_dim * elem_bytes) % 32 == 0,
+                "head_dim * elem_bytes must be a multiple of 32 (each half of a head in 16-byte pieces)");
+  PTS_CHECK_ARG((q_token_stride * elem_bytes) % 16 == 0 && (k_token_stride * elem_bytes) % 16 == 0 &&
+                    (v_token_stride * elem_bytes) % 16 == 0 && (cos_sin_token_stride * elem_bytes) % 16 == 0,
+                "token strides must be multiples of 16 bytes");
+  PTS_CHECK_ARG((((uintptr_t)q | (uintptr_t)q_out | (uintptr_t)k | (uintptr_t)v | (uintptr_t)cos | (uintptr_t)sin |
+                  (uintptr_t)kv_layer) & 15) == 0,
+                "pointers must be 16-byte aligned");
+  if (num_tokens <= 0) return PTS_OK;
+  const int row_bytes = num_kv_heads * head_dim * elem_bytes;
+  RopeArgs r;
+  r.q = (const char*)q;
+  r.q_stride = q_token_stride * elem_bytes;
+  r.q_out = (char*)q_out;
+  r.hq = num_qo_heads;
+  r.cos = (const char*)cos;
+  r.sin = (const char*)sin;
+  r.cs_stride = cos_sin_token_stride * elem_bytes;
+  r.head_dim = head_dim;
+  auto kernel = elem_bytes == 2 ? kv_append_rope_kernel<2> : kv_append_rope_kernel<4>;
+  kernel<<<num_tokens, 128, 0, (cudaStream_t)stream>>>(
+      (const char*)k, (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer,
+      batch_indices, positions, page_indptr, page_indices, row_bytes, page_len, max_pages, r);
+  return launch_status("kv_append_rope_kernel");
 }

@@ -289,6 +289,36 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, kv_layer: torch.Tensor, batch_in
               P, kv_layer.element_size(), _stream(dev))
 
 
+def kv_append_rope(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                   kv_layer: torch.Tensor, batch_indices: torch.Tensor, positions: torch.Tensor,
+                   page_indptr: torch.Tensor, page_indices: torch.Tensor,
+                   q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``kv_append`` with the rotary embedding: q [T, Hq, D] and k/v
+    [T, Hkv, D] before RoPE, cos/sin [T, D] their position embeddings; k is
+    rotated into the cache and the rotated q is returned."""
+    dev = _need_cuda(q, k, v, cos, sin, kv_layer, batch_indices, positions, page_indptr, page_indices)
+    if kv_layer.dim() != 5 or kv_layer.shape[1] != 2 or not kv_layer.is_contiguous():
+        raise ValueError("kv_layer must be a contiguous [max_pages, 2, page_len, Hkv, D] tensor")
+    P, _, pl, H, D = kv_layer.shape
+    dt = kv_layer.dtype
+    if any(t.dtype != dt for t in (q, k, v, cos, sin)):
+        raise ValueError("q, k, v, cos and sin must have the cache dtype")
+    T = q.shape[0]
+    rows = lambda t, w: t.reshape(T, w) if t.stride(-1) == 1 and t[0].is_contiguous() else t.contiguous().reshape(T, w)
+    q2, k2, v2 = rows(q, q.shape[1] * D), rows(k, H * D), rows(v, H * D)
+    cos2, sin2 = rows(cos, D), rows(sin, D)
+    if cos2.stride(0) != sin2.stride(0):
+        cos2, sin2 = cos2.contiguous(), sin2.contiguous()
+    if q_out is None:
+        q_out = torch.empty(T, q.shape[1], D, dtype=dt, device=dev)
+    _lib.call("pts_kv_append_rope", q2.data_ptr(), q2.stride(0), q_out.data_ptr(), q.shape[1], k2.data_ptr(),
+              v2.data_ptr(), k2.stride(0), v2.stride(0), cos2.data_ptr(), sin2.data_ptr(), cos2.stride(0),
+              kv_layer.data_ptr(), _i32(batch_indices, "bi").data_ptr(), _i32(positions, "pos").data_ptr(),
+              _i32(page_indptr, "indptr").data_ptr(), _i32(page_indices, "indices").data_ptr(), T, H, D, pl, P,
+              kv_layer.element_size(), _stream(dev))
+    return q_out
+
+
 def kv_compact(pool: torch.Tensor, page_indptr: torch.Tensor, page_indices: torch.Tensor,
                accepted: torch.Tensor, accepted_counts: torch.Tensor, offsets: torch.Tensor,
                new_kv_len: Optional[torch.Tensor] = None, new_last_page_len: Optional[torch.Tensor] = None) -> None:
@@ -374,6 +404,45 @@ def tree_prepare_append(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_wor
               v.data_ptr(), k.stride(0), v.stride(0), kv_layer.data_ptr(), _i32(page_indptr, "indptr").data_ptr(),
               _i32(page_indices, "indices").data_ptr(), T, H, D, pl, P, kv_layer.element_size(), _stream(dev))
     return bits, bi, pos
+
+
+def tree_prepare_append_rope(parents: torch.Tensor, qo_indptr: torch.Tensor, mask_words: int,
+                             seq_lens: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                             cos: torch.Tensor, sin: torch.Tensor, kv_layer: torch.Tensor, page_indptr: torch.Tensor,
+                             page_indices: torch.Tensor, q_out: Optional[torch.Tensor] = None):
+    """``tree_prepare_append`` with the rotary embedding applied on the way:
+    q [T, Hq, D], k/v [T, Hkv, D] are the tree tokens' projections before
+    RoPE and cos/sin [T, D] their position embeddings (the model's
+    ``position_embeddings``).  k is rotated into the cache and q into
+    ``q_out``.  Returns (bits, batch_indices, positions, q_out)."""
+    dev = _need_cuda(parents, qo_indptr, seq_lens, q, k, v, cos, sin, kv_layer, page_indptr, page_indices)
+    if kv_layer.dim() != 5 or kv_layer.shape[1] != 2 or not kv_layer.is_contiguous():
+        raise ValueError("kv_layer must be a contiguous [max_pages, 2, page_len, Hkv, D] tensor")
+    P, _, pl, H, D = kv_layer.shape
+    dt = kv_layer.dtype
+    if any(t.dtype != dt for t in (q, k, v, cos, sin)):
+        raise ValueError("q, k, v, cos and sin must have the cache dtype")
+    parents, qo_indptr = _i32(parents, "parents"), _i32(qo_indptr, "qo_indptr")
+    T = parents.numel()
+    if q.dim() != 3 or q.shape[0] != T or q.shape[2] != D or k.shape[0] != T or v.shape[0] != T:
+        raise ValueError("q [T, Hq, D] and k, v [T, Hkv, D] need one row per tree token")
+    rows = lambda t, w: t.reshape(T, w) if t.stride(-1) == 1 and t[0].is_contiguous() else t.contiguous().reshape(T, w)
+    q2, k2, v2 = rows(q, q.shape[1] * D), rows(k, H * D), rows(v, H * D)
+    cos2, sin2 = rows(cos, D), rows(sin, D)
+    if cos2.stride(0) != sin2.stride(0):
+        cos2, sin2 = cos2.contiguous(), sin2.contiguous()
+    if q_out is None:
+        q_out = torch.empty(T, q.shape[1], D, dtype=dt, device=dev)
+    bits = torch.empty(T, mask_words, dtype=torch.int64, device=dev)
+    bi = torch.empty(T, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, dtype=torch.int32, device=dev)
+    _lib.call("pts_tree_prepare_append_rope", parents.data_ptr(), qo_indptr.data_ptr(),
+              _i32(seq_lens, "seq_lens").data_ptr(), qo_indptr.numel() - 1, mask_words, bits.data_ptr(),
+              bi.data_ptr(), pos.data_ptr(), q2.data_ptr(), q2.stride(0), q_out.data_ptr(), q.shape[1],
+              k2.data_ptr(), v2.data_ptr(), k2.stride(0), v2.stride(0), cos2.data_ptr(), sin2.data_ptr(),
+              cos2.stride(0), kv_layer.data_ptr(), _i32(page_indptr, "indptr").data_ptr(),
+              _i32(page_indices, "indices").data_ptr(), T, H, D, pl, P, kv_layer.element_size(), _stream(dev))
+    return bits, bi, pos, q_out
 
 
 def tree_mask_from_bool(mask: torch.Tensor, qo_indptr: torch.Tensor, mask_indptr: torch.Tensor,

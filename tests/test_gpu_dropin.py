@@ -151,3 +151,54 @@ def test_wrapper_tree_attention_vs_fp32(use_bool_mask):
     ref = torch.cat(refs)
     d = (out.float() - ref).abs()
     assert d.max().item() <= 2e-2 and d.mean().item() <= 1e-3, (d.max().item(), d.mean().item())
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def test_wrapper_applies_rope_in_the_append():
+    """computeAttention(..., position_embeddings=(cos, sin)) with q, k before
+    the rotary embedding = the reference's order (apply_rotary_pos_emb in the
+    model, then computeAttention): the same output and cache bytes."""
+    g = torch.Generator(device="cpu").manual_seed(4)
+    rng = np.random.default_rng(4)
+    Hq, Hkv, D, pl, L = 8, 2, 128, 16, 1
+    prefixes, n = [50, 17], 13
+    runs = []
+    for fused in (False, True):
+        pool = cm.KvCachePool(32, L, Hkv, D, pl, torch.bfloat16, DEV)
+        pool.cache_data.copy_((torch.randn(pool.cache_data.shape, generator=torch.Generator().manual_seed(1))
+                               / math.sqrt(D)).to(torch.bfloat16))
+        reqs = []
+        for p in prefixes:
+            r = cm.RequestKvCache(pool, pl, p)
+            r.increment(n)
+            reqs.append(r)
+        bp = cm.getKvCacheBatchPosition(reqs, "tree", DEV, treeTokens=n)
+        wrapper = BeFlashinferWrapper(Hq, Hkv, Hq * D, pl, device=DEV)
+        ws = [wl.make_tree(np.random.default_rng(7), 4, 3, 500) for _ in prefixes]
+        assert all(w.size == n for w in ws)
+        parents = torch.tensor(np.concatenate([w.parents for w in ws]), dtype=torch.int32, device=DEV)
+        wrapper.set_tree_masks(parents, bp, n)
+        T = n * len(prefixes)
+        gg = torch.Generator().manual_seed(11)
+        q = torch.randn(T, Hq, D, generator=gg).to(torch.bfloat16).to(DEV)
+        k = (torch.randn(T, Hkv, D, generator=gg) / math.sqrt(D)).to(torch.bfloat16).to(DEV)
+        v = torch.randn(T, Hkv, D, generator=gg).to(torch.bfloat16).to(DEV)
+        pos = torch.cat([torch.arange(p, p + n) for p in prefixes]).float()
+        inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2).float() / D))
+        emb = torch.cat([pos[:, None] * inv[None]] * 2, dim=-1)
+        cos, sin = emb.cos().to(torch.bfloat16).to(DEV), emb.sin().to(torch.bfloat16).to(DEV)
+        if fused:
+            out = wrapper.computeAttention(q, k, v, pool.cache_data[0], "tree", bp, None, 0,
+                                           position_embeddings=(cos, sin))
+        else:
+            qr = q * cos[:, None] + _rotate_half(q) * sin[:, None]
+            kr = k * cos[:, None] + _rotate_half(k) * sin[:, None]
+            out = wrapper.computeAttention(qr, kr, v, pool.cache_data[0], "tree", bp, None, 0)
+        torch.cuda.synchronize()
+        runs.append((out.clone(), pool.cache_data.clone()))
+    assert torch.equal(runs[0][0].view(torch.int16), runs[1][0].view(torch.int16))
+    assert torch.equal(runs[0][1].view(torch.int16), runs[1][1].view(torch.int16))

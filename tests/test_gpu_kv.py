@@ -200,3 +200,78 @@ def test_tree_prepare_append_matches_separate_launches(shapes):
     assert torch.equal(bits, rbits) and torch.equal(bi, rbi) and torch.equal(pos, rpos)
     assert torch.equal(fused.view(torch.int16), sep.view(torch.int16))
     assert not torch.equal(fused.view(torch.int16), layer.view(torch.int16))
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_tree_prepare_append_rope_matches_torch(dtype):
+    """pts_tree_prepare_append_rope = apply_rotary_pos_emb in torch (q * cos +
+    rotate_half(q) * sin, eager ops in the same dtype) followed by
+    pts_tree_prepare_append: bit-exact q, masks, positions and cache bytes."""
+    rng = np.random.default_rng(21)
+    trees = [wl.make_tree(rng, w, d, 500) for (w, d) in [(8, 8), (0, 0), (4, 3), (2, 5)]]
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    T, B = int(indptr[-1]), len(trees)
+    Hq, Hkv, D, pl = 8, 2, 128, 16
+    prefix = rng.integers(0, 70, size=B)
+    seq = prefix + np.array([t.size for t in trees])
+    npages = (seq + pl - 1) // pl
+    P = int(npages.sum()) + 2
+    perm = rng.permutation(P)[:int(npages.sum())].astype(np.int32)
+    pind = torch.from_numpy(np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)).to(DEV)
+    pidx = torch.from_numpy(perm).to(DEV)
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(T, Hq, D, generator=g).to(dtype).to(DEV)
+    k = torch.randn(T, Hkv, D, generator=g).to(dtype).to(DEV)
+    v = torch.randn(T, Hkv, D, generator=g).to(dtype).to(DEV)
+    # Llama-style embeddings: positions of the tree tokens, theta 500000, fp32 then the model dtype
+    posn = torch.from_numpy(np.concatenate([np.arange(s - t.size, s) for s, t in zip(seq, trees)])).float()
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2).float() / D))
+    emb = torch.cat([posn[:, None] * inv[None], posn[:, None] * inv[None]], dim=-1)
+    cos, sin = emb.cos().to(dtype).to(DEV), emb.sin().to(dtype).to(DEV)
+    layer = torch.randn(P, 2, pl, Hkv, D, generator=g).to(dtype).to(DEV)
+    words = K.mask_words_for(max(t.size for t in trees))
+    dpar, dind = torch.from_numpy(par).to(DEV), torch.from_numpy(indptr).to(DEV)
+    dseq = torch.from_numpy(seq.astype(np.int32)).to(DEV)
+    fused = layer.clone()
+    bits, bi, pos, q_rot = K.tree_prepare_append_rope(dpar, dind, words, dseq, q, k, v, cos, sin, fused, pind, pidx)
+    q_ref = q * cos[:, None] + _rotate_half(q) * sin[:, None]
+    k_ref = k * cos[:, None] + _rotate_half(k) * sin[:, None]
+    sep = layer.clone()
+    rbits, rbi, rpos = K.tree_prepare_append(dpar, dind, words, dseq, k_ref, v, sep, pind, pidx)
+    torch.cuda.synchronize()
+    iv = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    assert torch.equal(q_rot.view(iv), q_ref.view(iv))
+    assert torch.equal(bits, rbits) and torch.equal(bi, rbi) and torch.equal(pos, rpos)
+    assert torch.equal(fused.view(iv), sep.view(iv))
+
+
+def test_kv_append_rope_matches_torch():
+    """pts_kv_append_rope = torch's apply_rotary_pos_emb arithmetic, then
+    pts_kv_append: bit-exact rotated q and cache bytes (bf16)."""
+    g = torch.Generator().manual_seed(8)
+    T, Hq, Hkv, D, pl, P = 40, 4, 2, 128, 16, 8
+    bi = torch.tensor([t // 20 for t in range(T)], dtype=torch.int32, device=DEV)
+    pos = torch.tensor([5 + t % 20 for t in range(T)], dtype=torch.int32, device=DEV)
+    pind = torch.tensor([0, 3, 6], dtype=torch.int32, device=DEV)
+    pidx = torch.tensor([4, 0, 7, 2, 5, 1], dtype=torch.int32, device=DEV)
+    q = torch.randn(T, Hq, D, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(T, Hkv, D, generator=g).to(torch.bfloat16).to(DEV)
+    v = torch.randn(T, Hkv, D, generator=g).to(torch.bfloat16).to(DEV)
+    emb = torch.randn(T, D // 2, generator=g) * 30
+    emb = torch.cat([emb, emb], dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16).to(DEV), emb.sin().to(torch.bfloat16).to(DEV)
+    layer = torch.randn(P, 2, pl, Hkv, D, generator=g).to(torch.bfloat16).to(DEV)
+    fused = layer.clone()
+    qr = K.kv_append_rope(q, k, v, cos, sin, fused, bi, pos, pind, pidx)
+    q_ref = q * cos[:, None] + _rotate_half(q) * sin[:, None]
+    k_ref = k * cos[:, None] + _rotate_half(k) * sin[:, None]
+    sep = layer.clone()
+    K.kv_append(k_ref, v, sep, bi, pos, pind, pidx)
+    torch.cuda.synchronize()
+    assert torch.equal(qr.view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(fused.view(torch.int16), sep.view(torch.int16))

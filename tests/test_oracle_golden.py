@@ -144,3 +144,25 @@ def test_oracle_matches_reference_acceptance_f32():
                                                  UniformStream(c["philox_seed"], c.get("philox_offset", 0),
                                                                c.get("request", 0)))
         assert (list(s), list(h), tl, al) == (rec["tokens"], rec["hidden"], rec["total_len"], rec["accept_len"]), c
+
+
+def test_rope_oracle_matches_transformers():
+    """oracle.kv.rope_bf16 = transformers' apply_rotary_pos_emb (the function
+    the reference's attention calls before the append) on bf16 CPU tensors,
+    bit for bit, for q and k of a Llama-shaped layer."""
+    torch = pytest.importorskip("torch")
+    mod = pytest.importorskip("transformers.models.llama.modeling_llama")
+    from oracle import kv as okv
+    g = torch.Generator().manual_seed(3)
+    T, Hq, Hkv, D = 37, 8, 2, 128
+    q = torch.randn(1, Hq, T, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, Hkv, T, D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(4090, 4090 + T).float()
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2).float() / D))
+    emb = torch.cat([pos[:, None] * inv[None]] * 2, dim=-1)[None]
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    q_ref, k_ref = mod.apply_rotary_pos_emb(q, k, cos, sin)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    for x, ref in ((q, q_ref), (k, k_ref)):
+        got = okv.rope_bf16(bits(x[0].transpose(0, 1)), bits(cos[0]), bits(sin[0]))
+        assert np.array_equal(got, bits(ref[0].transpose(0, 1)))
