@@ -319,11 +319,14 @@ __device__ void write_counts(const AcceptParams& p, int b, int n_out, int total,
 // KV compaction of request b's accepted path by one warp, right after its
 // walk stored the hidden indices and counts (pts_kv_compact's semantics:
 // slot offsets[b] + hidden[i] -> offsets[b] + i for every layer, K and V, and
-// head, i < count).  Entries go in order of i, each one's rows spread over the
-// lanes.  A path's hidden indices rise (hidden[i] >= i; the bonus entry
-// repeats the last node), so a slot is written only after every entry that
-// reads it, which gives pts_kv_compact's staged result without staging.
-__device__ void compact_request_warp(const AcceptParams& p, int b) {
+// head, i < count).  With a shared-memory `stage` that holds the whole path,
+// every source piece is copied in with cp.async before any destination is
+// written (two HBM round trips for the path).  Otherwise entries go in order
+// of i, each one's rows spread over the lanes: a path's hidden indices rise
+// (hidden[i] >= i; the bonus entry repeats the last node), so a slot is
+// written only after every entry that reads it -- the staged result again.
+__device__ void compact_request_warp(const AcceptParams& p, int b, uint8_t* stage = nullptr,
+                                     size_t stage_bytes = 0) {
   const int lane = threadIdx.x & 31;
   __syncwarp();
   const pts_kv_compact_args& a = p.cp;
@@ -356,6 +359,39 @@ __device__ void compact_request_warp(const AcceptParams& p, int b) {
     }
     return page;
   };
+  if (stage && (size_t)na * items * 16 <= stage_bytes) {
+    for (int i = 0; i < na; ++i) {                    // every source piece in flight at once
+      const int src = i < 32 ? __shfl_sync(0xffffffffu, my_src, i) : acc[i];
+      const int sp = src != i ? page_of(off + src) : -1;
+      if (sp >= 0) {
+        const int ss = (off + src) % a.page_len;
+        for (int e = lane; e < items; e += 32) {
+          const int layer = e / (2 * per_kv), kv = (e / per_kv) & 1, q = e % per_kv;
+          const char* from = (const char*)a.kv_pool + layer * layer_bytes + (int64_t)q * 16 +
+                             ((int64_t)(sp * 2 + kv) * a.page_len + ss) * row_bytes;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                       ::"r"((uint32_t)__cvta_generic_to_shared(stage + ((size_t)i * items + e) * 16)), "l"(from)
+                       : "memory");
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    for (int i = 0; i < na; ++i) {
+      const int src = i < 32 ? __shfl_sync(0xffffffffu, my_src, i) : acc[i];
+      const int sp = src != i ? page_of(off + src) : -1, dp = src != i ? page_of(off + i) : -1;
+      if (sp >= 0 && dp >= 0) {
+        const int ds = (off + i) % a.page_len;
+        for (int e = lane; e < items; e += 32) {
+          const int layer = e / (2 * per_kv), kv = (e / per_kv) & 1, q = e % per_kv;
+          char* to = (char*)a.kv_pool + layer * layer_bytes + (int64_t)q * 16 +
+                     ((int64_t)(dp * 2 + kv) * a.page_len + ds) * row_bytes;
+          *(uint4*)to = *(const uint4*)(stage + ((size_t)i * items + e) * 16);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
   for (int i = 0; i < na; ++i) {
     const int src = i < 32 ? __shfl_sync(0xffffffffu, my_src, i) : acc[i];
     if (src != i) {
@@ -371,6 +407,7 @@ __device__ void compact_request_warp(const AcceptParams& p, int b) {
       }
     }
     __syncwarp();
+  }
   }
   if (lane == 0) {
     const int len = off + na;
@@ -813,7 +850,8 @@ struct WarpGroup {
 // node's token logit read and every expansion flag cleared; returns whether
 // the walk is to run (the caller runs it against its expander warp).
 template <bool kLazy = false, class G>
-__device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm) {
+__device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const WalkSmem& w, G g, int* red_sm,
+                             uint8_t* stage = nullptr, size_t stage_bytes = 0) {
   if (n <= 0 || n > p.max_nodes || n > PTS_MAX_TREE_NODES) {
     if (g.rank() == 0) write_counts(p, b, -1, 0, 0, 0);
     if (!kLazy && p.compact && g.rank() < 32) compact_request_warp(p, b);   // (the lengths)
@@ -970,7 +1008,7 @@ __device__ bool walk_request(const AcceptParams& p, int b, int lo, int n, const 
   } else if (g.rank() < 32) {
     walk_greedy_warp(p, b, lo, w);
   }
-  if (p.compact && g.rank() < 32) compact_request_warp(p, b);
+  if (p.compact && g.rank() < 32) compact_request_warp(p, b, stage, stage_bytes);
   g.sync();
   return false;
 }
@@ -1761,7 +1799,8 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       if (!p.traversal) {
         if (b < 0) break;
         const int lo = p.row_indptr[b];
-        walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr);
+        walk_request(p, b, lo, p.row_indptr[b + 1] - lo, w, WarpGroup{}, nullptr, streams ? nullptr : ring,
+                     streams ? 0 : kSRingBytes);
         continue;
       }
       // traversal: set-up, hand the request to the expander, walk lazily
@@ -1779,7 +1818,8 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       named_barrier(1, 64);
       if (b < 0) break;
       if (go) walk_traversal_warp<true>(p, b, lo, n, w);
-      if (p.compact) compact_request_warp(p, b);
+      // a walker CTA streams nothing: its copy ring stages the compaction
+      if (p.compact) compact_request_warp(p, b, streams ? nullptr : ring, streams ? 0 : kSRingBytes);
       if (lane == 0) *(volatile int*)&ctl.walk_done = 1;
       named_barrier(2, 64);
     }
