@@ -290,8 +290,8 @@ class Step:
                 self.step_index, W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
                 self.acc_ws.data_ptr(), self.acc_ws.numel(), ctypes.byref(self.compact), s), "accept+compact")
         else:
-            # greedy walks end with the stream, so the compaction's dependent copies would lengthen the
-            # launch: it runs as its own launch here
+            # greedy walks run on streaming CTAs and end with the stream, so the compaction's copies
+            # would lengthen the launch: it runs as its own launch here
             check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
                                       W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(),
                                       W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
