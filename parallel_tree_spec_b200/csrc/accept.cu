@@ -1989,8 +1989,9 @@ __device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uin
 }
 
 // One CTA per row: counts of every distinct value in a window of kToppWindow
-// coarse bins below the row max, then the cumulative mass from the top; the
-// window moves down until the mass reaches top_p * s.
+// coarse bins below the row max (16-byte loads where rows are aligned), then
+// the cumulative mass from the top; the window moves down until the mass
+// reaches top_p * s.
 __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p, float top_p, float* thresh,
                                                              float* mass) {
   __shared__ uint32_t cnt[kToppWindow * 256];
@@ -2001,6 +2002,7 @@ __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p
   const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
   const double target = (double)top_p * (double)rs.s;
   const int top_coarse = (int)(bf16_key(__float_as_uint(rs.m) >> 16) >> 8);
+  const bool vec = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
   double cum = 0.0;                       // thread 0's running mass over the windows
   if (tid == 0) s_done = 0;
   for (int hi_c = top_coarse; hi_c >= 0; hi_c -= kToppWindow) {
@@ -2008,10 +2010,36 @@ __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p
     const uint32_t lo_key = (uint32_t)lo_c << 8, hi_key = ((uint32_t)hi_c << 8) | 0xffu;
     for (int i = tid; i < kToppWindow * 256; i += kToppThreads) cnt[i] = 0u;
     __syncthreads();
-    for (int e = tid; e < p.vocab; e += kToppThreads) {
-      const uint32_t k = bf16_key(scaled_bits(p, rp, e));
+    auto count = [&](uint32_t bits) {
+      const uint32_t k = bf16_key(bits);
       if (k >= lo_key && k <= hi_key) atomicAdd(&cnt[k - lo_key], 1u);
+    };
+    int e_tail = 0;
+    if (vec) {
+      // 16-byte loads, four in flight per thread before any is counted
+      const int nv = p.vocab / 8;
+      for (int v0 = tid; v0 < nv; v0 += 4 * kToppThreads) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int vi = v0 + u * kToppThreads;
+          x[u] = vi < nv ? ld_stream(rp + (int64_t)vi * 8) : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (v0 + u * kToppThreads >= nv) continue;
+          uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (p.use_temp) w[j] = scale_pair(w[j], p.inv_temp);
+            count(w[j] & 0xffffu);
+            count(w[j] >> 16);
+          }
+        }
+      }
+      e_tail = nv * 8;
     }
+    for (int e = e_tail + tid; e < p.vocab; e += kToppThreads) count(scaled_bits(p, rp, e));
     __syncthreads();
     if (tid == 0) {
       for (int k = (int)hi_key; k >= (int)lo_key; --k) {
