@@ -174,6 +174,19 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- workload
+def over_ranks(values, op, device):
+    """``values`` (floats) reduced element-wise over all ranks with op "max"
+    or "min", in one all-reduce; the values themselves without a process
+    group."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return [float(v) for v in values]
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}[op])
+    return [float(v) for v in t.tolist()]
+
+
 def build_workload(a, device, seed):
     import torch
     from parallel_tree_spec_b200 import kernels as K
@@ -428,19 +441,13 @@ def run_b200(a):
     elapsed_ms = start.elapsed_time(end)
     attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
     acc_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms, = over_ranks([elapsed_ms], "max", device)          # the slowest rank's time
     ms_per_step = elapsed_ms / a.steps
     value = world * a.steps / (elapsed_ms / 1e3)
 
     # e2e: tree inputs from pinned host memory, results back to the host every step
     e2e = run_e2e(a, W, step, device)
-    if world > 1:
-        t = torch.tensor([e2e["value"]], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MIN)
-        e2e["value"] = float(t.item()) * world
+    e2e["value"] = over_ranks([e2e["value"]], "min", device)[0] * world   # the slowest rank's rate, N times
 
     ab = algorithmic_bytes(a)
     peak, peak_kind = measured_peaks()
@@ -574,12 +581,7 @@ def run_tp(a):
     s = torch.cuda.current_stream(dev).cuda_stream
     pool = layer.view(1, *layer.shape)
 
-    def gather(t):
-        if world == 1:
-            return t.unsqueeze(0)
-        o = torch.empty(world, *t.shape, dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(o, t)
-        return o
+    gather = K.gather_shards
 
     res = {}
 
@@ -626,10 +628,8 @@ def run_tp(a):
     el = start.elapsed_time(end)
     attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
     acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    el, attn, acc = over_ranks([el, attn, acc], "max", dev)
     if world > 1:
-        t = torch.tensor([el, attn, acc], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        el, attn, acc = (float(x) for x in t.tolist())
         counts = gather(res["oc"])
         same = bool(all(torch.equal(counts[0], counts[k]) for k in range(world)))
     else:

@@ -413,3 +413,101 @@ def row_stats_f32(x: np.ndarray, temperature: float = 1.0):
     s = e.astype(np.float64).sum(axis=-1, keepdims=True).astype(np.float32)
     p = (e / s).astype(np.float32)
     return np.argmax(p, axis=-1).astype(np.int64), p
+
+
+# ------------------------------------------------------- vocabulary shards
+# The library's tensor-parallel acceptance splits the vocabulary over ranks
+# (include/pts_b200.h, pts_accept_shard_partials .. pts_accept_walk_merged).
+# The reference has no sharded form, so these restate the exchange itself:
+# per-shard partials, the merge in shard order, the exchange of tie indices.
+# The merged statistics must reproduce row_stats and mb_from_probs of whole
+# rows (verification.py:46-55, :349); tests check exactly that.
+INT_MAX = 2 ** 31 - 1
+
+
+def _exp_rounded(d: np.ndarray) -> np.ndarray:
+    """fp32 exp of an fp32 difference, as row_probs evaluates it."""
+    return np.exp(np.asarray(d, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def shard_partials(shard_bits: np.ndarray, vocab_offset: int, row_indptr, parents, tokens,
+                   temperature: float = 1.0):
+    """One shard's partials.  ``shard_bits``: uint16 [rows, Vs], vocabulary
+    columns vocab_offset .. vocab_offset + Vs - 1 of every row.
+
+    Returns (parts [rows, 3] float64: the shard's max m_k, the float64 sum of
+    fp32 exp(x - m_k), the first global index of m_k; tok [rows] float32:
+    node i's token logit in its parent's row if this shard holds the token,
+    else -inf, and -inf for tree roots)."""
+    x = scale_logits(shard_bits, temperature)
+    R, Vs = x.shape
+    m = x.max(axis=-1)
+    s = _exp_rounded(x - m[:, None]).astype(np.float64).sum(axis=-1)
+    first = np.argmax(x, axis=-1) + int(vocab_offset)
+    parts = np.stack([m.astype(np.float64), s, first.astype(np.float64)], axis=-1)
+    tok = np.full(R, -np.inf, dtype=np.float32)
+    for b in range(len(row_indptr) - 1):
+        lo, hi = int(row_indptr[b]), int(row_indptr[b + 1])
+        for i in range(lo, hi):
+            p, t = int(parents[i]), int(tokens[i]) - int(vocab_offset)
+            if p >= 0 and 0 <= t < Vs:
+                tok[i] = x[lo + p, t]
+    return parts, tok
+
+
+def _prev_bf16(v: np.ndarray) -> np.ndarray:
+    """The largest bf16 value below each (bf16-exact, finite) value."""
+    bits = f32_to_bf16_bits(v).astype(np.int64)
+    out = np.where(v > 0, bits - 1, np.where(v < 0, bits + 1, 0x8001))
+    return bf16_bits_to_f32(out.astype(np.uint16))
+
+
+def merge_shards(parts_all: np.ndarray, tok_all: np.ndarray):
+    """Merge partials gathered in shard order: parts_all [shards, rows, 3],
+    tok_all [shards, rows].  Returns (m [rows] f32, s [rows] f32, first index
+    of the max [rows] int64, tie flag [rows] bool, token logit [rows] f32).
+
+    s = sum_k s_k exp(m_k - m) in float64, rounded to fp32.  A row is flagged
+    when the largest bf16 value below its max still rounds to the max's
+    probability bf16(1 / s): only then can an index before the first max hold
+    the largest rounded probability, and the shards settle it."""
+    mk = parts_all[..., 0]
+    m = mk.max(axis=0)
+    s = (parts_all[..., 1] * np.exp(mk - m)).sum(axis=0).astype(np.float32)
+    k = np.argmax(mk == m, axis=0)                       # first shard holding the max
+    first = parts_all[k, np.arange(m.shape[0]), 2].astype(np.int64)
+    m32 = m.astype(np.float32)
+    qmax = round_bf16(np.float32(1.0) / s)
+    flag = round_bf16(_exp_rounded(_prev_bf16(m32) - m32) / s) == qmax
+    return m32, s, first, flag, tok_all.max(axis=0).astype(np.float32)
+
+
+def shard_ties(shard_bits: np.ndarray, vocab_offset: int, m: np.ndarray, s: np.ndarray, flag: np.ndarray,
+               temperature: float = 1.0) -> np.ndarray:
+    """Per flagged row the first global index of this shard whose rounded
+    probability equals the row's largest, bf16(1 / s); INT_MAX elsewhere."""
+    x = scale_logits(shard_bits, temperature)
+    p = round_bf16(_exp_rounded(x - m[:, None]) / s[:, None])
+    hit = p == round_bf16(np.float32(1.0) / s)[:, None]
+    got = np.where(hit.any(axis=-1), np.argmax(hit, axis=-1) + int(vocab_offset), INT_MAX)
+    return np.where(flag, got, INT_MAX).astype(np.int64)
+
+
+def merged_row_argmax(first: np.ndarray, flag: np.ndarray, ties_all: np.ndarray) -> np.ndarray:
+    """The rows' argmax: the smallest tie index over all shards where flagged."""
+    return np.where(flag, ties_all.min(axis=0), first).astype(np.int64)
+
+
+def merged_mb(row_indptr, parents, m: np.ndarray, s: np.ndarray, tok: np.ndarray) -> np.ndarray:
+    """Mb per node (mb_from_probs) from the merged statistics: the rounded
+    probability bf16(exp(x - m) / s) of the node's token logit x in its
+    parent's row; 1 for tree roots."""
+    mb = np.ones(len(tok), dtype=np.float32)
+    for b in range(len(row_indptr) - 1):
+        lo, hi = int(row_indptr[b]), int(row_indptr[b + 1])
+        for i in range(lo, hi):
+            p = int(parents[i])
+            if p >= 0:
+                r = lo + p
+                mb[i] = round_bf16(_exp_rounded(np.float32(tok[i]) - m[r]) / s[r])
+    return mb

@@ -237,6 +237,21 @@ def accept_walk_merged(stats: torch.Tensor, tok: torch.Tensor, ties_all: torch.T
     return ot, oh, oc
 
 
+def gather_shards(t: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather ``t`` from every rank of ``group`` into [ranks, *t.shape],
+    rank r's tensor at index r (rank order is shard order).  One collective
+    into one buffer; NCCL for CUDA tensors, gloo for CPU tensors.  Without an
+    initialised process group the result is ``t`` itself as the one shard."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return t.unsqueeze(0)
+    K = dist.get_world_size(group)
+    t = t.contiguous()
+    out = torch.empty(K * t.shape[0], *t.shape[1:], dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t, group=group)
+    return out.view(K, *t.shape)
+
+
 def accept_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab: int, row_indptr: torch.Tensor,
                    parents: torch.Tensor, tokens: torch.Tensor, draft_probs: Optional[torch.Tensor] = None,
                    group=None, eos_token_id: Optional[int] = None, temperature: float = 1.0, seed: int = 0,
@@ -244,17 +259,9 @@ def accept_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab: int, ro
     """Tensor-parallel acceptance on one rank of ``group`` (torch.distributed,
     NCCL): the shard partials and the tie indices are all-gathered, every
     rank merges in shard order and walks; all ranks return the same paths."""
-    import torch.distributed as dist
-    K = dist.get_world_size(group)
     parts, tok = accept_shard_partials(logits_shard, vocab_offset, row_indptr, parents, tokens, temperature)
-    parts_all = torch.empty(K, *parts.shape, dtype=parts.dtype, device=parts.device)
-    tok_all = torch.empty(K, *tok.shape, dtype=tok.dtype, device=tok.device)
-    dist.all_gather_into_tensor(parts_all, parts, group=group)
-    dist.all_gather_into_tensor(tok_all, tok, group=group)
-    stats, tokm = accept_merge_shards(parts_all, tok_all)
-    first = accept_shard_ties(logits_shard, vocab_offset, stats, temperature)
-    ties_all = torch.empty(K, *first.shape, dtype=first.dtype, device=first.device)
-    dist.all_gather_into_tensor(ties_all, first, group=group)
+    stats, tokm = accept_merge_shards(gather_shards(parts, group), gather_shards(tok, group))
+    ties_all = gather_shards(accept_shard_ties(logits_shard, vocab_offset, stats, temperature), group)
     return accept_walk_merged(stats, tokm, ties_all, vocab, row_indptr, parents, tokens, draft_probs,
                               eos_token_id, seed, offset, max_nodes)
 
