@@ -2673,6 +2673,10 @@ extern "C" int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_
                                             uint64_t philox_offset, int32_t* out_tokens, int32_t* out_hidden,
                                             int32_t* out_counts, int out_stride, pts_stream_t stream) {
   if (num_rows <= 0 || vocab <= 0) return set_error(PTS_ERR_INVALID, "need num_rows > 0 and vocab > 0");
+  // the pointer checks of pts_accept_traversal, here before the scratch lookup touches the device
+  PTS_CHECK_ARG(logits && row_indptr && parents && tokens, "null input pointer");
+  PTS_CHECK_ARG(draft_probs, "null draft_probs");
+  PTS_CHECK_ARG(out_tokens && out_hidden && out_counts, "null output pointer");
   size_t a, b, c, d;
   const size_t need = ws_layout(num_rows, vocab, &a, &b, &c, &d) + topp_ws_bytes(num_rows);
   if (need > kNoAllocScratchBytes)

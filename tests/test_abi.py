@@ -1,5 +1,6 @@
 """The C-ABI library loads and exports every function include/pts_b200.h declares
 (no GPU needed: nothing is called except the error-string and version getters)."""
+import ctypes as C
 import os
 import re
 
@@ -37,3 +38,19 @@ def test_host_side_argument_checks_need_no_gpu():
     rc = lib.pts_kv_append(None, None, 0, 0, None, None, None, None, None, 1, 8, 128, 16, 10, 2, None)
     assert rc == _lib.PTS_ERR_INVALID
     assert lib.pts_accept_workspace_size(1040, 128256) > 0
+
+
+def test_every_entry_rejects_null_pointers_on_the_host():
+    """Every status-returning entry, given null pointers and sizes of 1,
+    returns PTS_ERR_INVALID from its host-side checks, before any CUDA call
+    (which here, without a GPU, would give PTS_ERR_CUDA instead)."""
+    lib = _lib.lib()
+    checked = 0
+    for name, (res, args) in sorted(_lib.SIGNATURES.items()):
+        if res is not C.c_int or not args:
+            continue
+        vals = [None if a is C.c_void_p else 1.0 if a in (C.c_float, C.c_double) else 1 for a in args]
+        rc = getattr(lib, name)(*vals)
+        assert rc == _lib.PTS_ERR_INVALID, (name, rc, lib.pts_last_error())
+        checked += 1
+    assert checked >= 20
