@@ -464,8 +464,9 @@ def _prev_bf16(v: np.ndarray) -> np.ndarray:
 
 def merge_shards(parts_all: np.ndarray, tok_all: np.ndarray):
     """Merge partials gathered in shard order: parts_all [shards, rows, 3],
-    tok_all [shards, rows].  Returns (m [rows] f32, s [rows] f32, first index
-    of the max [rows] int64, tie flag [rows] bool, token logit [rows] f32).
+    tok_all [shards, rows].  Returns (m [rows] f32, s [rows] f32, smallest
+    index of the max over the shards holding it [rows] int64, tie flag [rows]
+    bool, token logit [rows] f32).
 
     s = sum_k s_k exp(m_k - m) in float64, rounded to fp32.  A row is flagged
     when the largest bf16 value below its max still rounds to the max's
@@ -474,8 +475,7 @@ def merge_shards(parts_all: np.ndarray, tok_all: np.ndarray):
     mk = parts_all[..., 0]
     m = mk.max(axis=0)
     s = (parts_all[..., 1] * np.exp(mk - m)).sum(axis=0).astype(np.float32)
-    k = np.argmax(mk == m, axis=0)                       # first shard holding the max
-    first = parts_all[k, np.arange(m.shape[0]), 2].astype(np.int64)
+    first = np.where(mk == m, parts_all[..., 2], np.inf).min(axis=0).astype(np.int64)
     m32 = m.astype(np.float32)
     qmax = round_bf16(np.float32(1.0) / s)
     flag = round_bf16(_exp_rounded(_prev_bf16(m32) - m32) / s) == qmax

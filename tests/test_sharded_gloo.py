@@ -33,7 +33,7 @@ def _inputs():
     rng = np.random.default_rng(17)
     trees = [wl.make_tree(rng, 4, 4, V) for _ in range(4)]
     x = np.concatenate([wl.make_logits(rng, t, V, plant=0.8, soft=True) for t in trees], 0)
-    # every value equal: the max is in both shards, the first shard's wins
+    # every value equal: the max is in both shards, the smaller index wins
     x[1, :] = x[1, 0]
     # the max only in the second shard, the bf16 value just below it everywhere else: both round to
     # the same probability, so the argmax is the first column of the first shard
@@ -51,9 +51,9 @@ def _inputs():
     return x, indptr, par, tok, dp
 
 
-def _sharded_stats(x, rank, indptr, par, tok, T):
+def _sharded_stats(x, shard, indptr, par, tok, T):
     from parallel_tree_spec_b200.kernels import gather_shards
-    lo, hi = BOUNDS[rank], BOUNDS[rank + 1]
+    lo, hi = BOUNDS[shard], BOUNDS[shard + 1]
     parts, tk = acc.shard_partials(x[:, lo:hi], lo, indptr, par, tok, T)
     m, s, first, flag, tm = acc.merge_shards(gather_shards(torch.from_numpy(parts)).numpy(),
                                              gather_shards(torch.from_numpy(tk)).numpy())
@@ -72,8 +72,9 @@ def _rank_main(rank, port):
 
         from parallel_tree_spec_b200.kernels import gather_shards
         x, indptr, par, tok, dp = _inputs()
-        for T in (1.0, 0.8):
-            am, mb, flag = _sharded_stats(x, rank, indptr, par, tok, T)
+        # shards in vocabulary order over the ranks, then reversed
+        for T, shard in ((1.0, rank), (0.8, rank), (1.0, WORLD - 1 - rank)):
+            am, mb, flag = _sharded_stats(x, shard, indptr, par, tok, T)
             ref_am, probs = acc.row_stats(x, T)
             assert np.array_equal(am, ref_am), np.nonzero(am != ref_am)
             assert flag[5] and flag[9] and not flag[1]
