@@ -15,7 +15,7 @@ import torch
 
 from . import _lib
 
-_WS: Dict[Tuple[int, str], torch.Tensor] = {}
+_WS: Dict[Tuple[int, int, str], torch.Tensor] = {}
 
 
 def _stream(device: torch.device) -> int:
@@ -41,8 +41,11 @@ def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
 
 
 def workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
-    """A per-device, per-kind scratch buffer (256-byte aligned), grown on demand."""
-    key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
+    """A scratch buffer per device, current stream and kind (256-byte aligned),
+    grown on demand.  Calls on one stream run in order and share it; calls on
+    different streams get different buffers, so they may overlap."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, _stream(torch.device("cuda", index)), kind)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)

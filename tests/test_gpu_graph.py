@@ -63,7 +63,7 @@ def test_verification_step_replays_from_a_cuda_graph():
     new_len = torch.zeros(x["B"], dtype=torch.int32, device=DEV)
     cargs = K.kv_compact_args(x["pool"], x["pind"], x["pidx"], x["offs"], new_len)
     pool0 = x["pool"].clone()
-    eager = [t.clone() for t in _step(x, cargs)]          # also allocates the cached workspaces
+    eager = [t.clone() for t in _step(x, cargs)]
     eager_pool, eager_len = x["pool"].clone(), new_len.clone()
     # warm up on a side stream, as torch's capture expects, then capture
     side = torch.cuda.Stream()
@@ -72,8 +72,8 @@ def test_verification_step_replays_from_a_cuda_graph():
         _step(x, cargs)
     torch.cuda.current_stream().wait_stream(side)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        outs = _step(x, cargs)
+    with torch.cuda.graph(graph):                         # workspaces are per stream: the capture stream's
+        outs = _step(x, cargs)                            # come from the graph's memory pool
     for _ in range(2):
         x["pool"].copy_(pool0)
         new_len.zero_()
