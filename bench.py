@@ -63,10 +63,12 @@ def parse_args(argv=None):
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--top-p", type=float, default=1.0, help="nucleus target distribution for traversal (extension)")
     ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--cpu-sample-requests", type=int, default=1)
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
                     help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the sub-records (other acceptance modes, the config-3 path, tensor-parallel and "
+                         "strong-scaling steps)")
     ap.add_argument("--sparse", action="store_true",
                     help="long-context sparse step (batch 8, 32768-token prefixes, 129-row trees, attention over "
                          "per-KV-head sets of 4 first + 64 top-scored + 8 last prefix pages, greedy)")
@@ -105,6 +107,18 @@ def measured_peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Sustained dense bf16 TFLOP/s (the attention kernel runs inside a long step)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured (sustained)"
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return 1400.0, "fallback (sustained)"
 
 
 def traffic_table():
@@ -253,145 +267,209 @@ def build_workload(a, device, seed):
 
 
 class Step:
-    """The verification step as raw C-ABI launches on the current stream."""
+    """The verification step as raw C-ABI launches on the current stream.  The
+    argument tuples are built once (every buffer stays in place), so a step
+    costs the host only the three or four foreign calls."""
 
     def __init__(self, a, W, device, philox_seed=5):
         import torch
         from parallel_tree_spec_b200 import _lib, kernels as K
         self.a, self.W, self.K, self.L = a, W, K, _lib.lib()
         self.dev = device
-        self.stream = torch.cuda.current_stream(device).cuda_stream
+        s = self.stream = torch.cuda.current_stream(device).cuda_stream
         B, n = a.batch, W["n"]
-        self.acc_ws = K.workspace(device, "accept", self.L.pts_accept_workspace_size(B * n, a.vocab))
-        self.attn_ws = K.workspace(device, "attn", max(256, self.L.pts_tree_attn_workspace_size(
+        L = self.L
+        self.acc_ws = K.workspace(device, "accept", L.pts_accept_workspace_size(B * n, a.vocab))
+        self.attn_ws = K.workspace(device, "attn", max(256, L.pts_tree_attn_workspace_size(
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
         self.launches_per_step = 3 if a.mode == "traversal" else 4
-        pool = W["pool"]
-        self.compact = _lib.KvCompactArgs(pool.data_ptr(), 1, W["layer"].shape[0], 16, a.hkv, 128, 2,
-                                          W["page_indptr"].data_ptr(), W["page_indices"].data_ptr(),
-                                          W["offsets"].data_ptr(), None, None)
-
-    def run(self, ev=None):
-        from parallel_tree_spec_b200._lib import check
-        a, W, L, s = self.a, self.W, self.L, self.stream
-        B, n = a.batch, W["n"]
-        P = W["page_indptr"]
-        lay = W["layer"]
-        check(L.pts_tree_prepare_append(W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(),
-                                        B, W["mask_words"], W["bits"].data_ptr(), W["bi"].data_ptr(),
-                                        W["pos"].data_ptr(), W["k_new"].data_ptr(), W["v_new"].data_ptr(),
-                                        a.hkv * 128, a.hkv * 128, lay.data_ptr(), P.data_ptr(),
-                                        W["page_indices"].data_ptr(), B * n, a.hkv, 128, 16, lay.shape[0], 2, s),
-              "prepare+append")
-        if ev is not None:
-            ev[0].record()
-        check(L.pts_tree_attn_run(W["q"].data_ptr(), lay.data_ptr(), W["qo_indptr"].data_ptr(), P.data_ptr(),
-                                  W["page_indices"].data_ptr(), W["last_page_len"].data_ptr(), W["bits"].data_ptr(),
-                                  W["mask_words"], W["out"].data_ptr(), B, B * n, n, W["kv_len"], a.hq, a.hkv, 128,
-                                  16, lay.shape[0], 1.0 / math.sqrt(128), self.attn_ws.data_ptr(),
-                                  self.attn_ws.numel(), s), "attention")
-        if ev is not None:
-            ev[1].record()
-        x = W["logits"]
-        # acceptance; each walk then compacts its request's accepted KV in the same launch
+        pool, lay, P, x = W["pool"], W["layer"], W["page_indptr"], W["logits"]
+        self.compact = _lib.KvCompactArgs(pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
+                                          W["page_indices"].data_ptr(), W["offsets"].data_ptr(), None, None)
+        self.prep = (L.pts_tree_prepare_append,
+                     (W["parents"].data_ptr(), W["qo_indptr"].data_ptr(), W["seq_lens"].data_ptr(), B,
+                      W["mask_words"], W["bits"].data_ptr(), W["bi"].data_ptr(), W["pos"].data_ptr(),
+                      W["k_new"].data_ptr(), W["v_new"].data_ptr(), a.hkv * 128, a.hkv * 128, lay.data_ptr(),
+                      P.data_ptr(), W["page_indices"].data_ptr(), B * n, a.hkv, 128, 16, lay.shape[0], 2, s))
+        self.attn = (L.pts_tree_attn_run,
+                     (W["q"].data_ptr(), lay.data_ptr(), W["qo_indptr"].data_ptr(), P.data_ptr(),
+                      W["page_indices"].data_ptr(), W["last_page_len"].data_ptr(), W["bits"].data_ptr(),
+                      W["mask_words"], W["out"].data_ptr(), B, B * n, n, W["kv_len"], a.hq, a.hkv, 128, 16,
+                      lay.shape[0], 1.0 / math.sqrt(128), self.attn_ws.data_ptr(), self.attn_ws.numel(), s))
         if a.mode == "traversal":
-            check(L.pts_accept_traversal_compact(
-                x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(), W["tokens"].data_ptr(),
-                W["draft_probs"].data_ptr(), B, B * n, a.vocab, n, -1, a.temperature, a.top_p, 0, self.philox_seed,
-                self.step_index, W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n,
-                self.acc_ws.data_ptr(), self.acc_ws.numel(), ctypes.byref(self.compact), s), "accept+compact")
+            # acceptance; each walk then compacts its request's accepted KV in the same launch
+            self.acc_head = (x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
+                             W["tokens"].data_ptr(), W["draft_probs"].data_ptr(), B, B * n, a.vocab, n, -1,
+                             a.temperature, a.top_p, 0, self.philox_seed)
+            self.acc_tail = (W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
+                             self.acc_ws.numel(), ctypes.byref(self.compact), s)
         else:
             # greedy walks run on streaming CTAs and end with the stream, so the compaction's copies
             # would lengthen the launch: it runs as its own launch here
-            check(L.pts_accept_greedy(x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
-                                      W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(),
-                                      W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
-                                      self.acc_ws.numel(), s), "accept")
-            pool = W["pool"]
-            check(L.pts_kv_compact(pool.data_ptr(), 1, W["layer"].shape[0], 16, a.hkv, 128, 2,
-                                   W["page_indptr"].data_ptr(), W["page_indices"].data_ptr(), W["oh"].data_ptr(), n,
-                                   W["oc"].data_ptr(), 4, W["offsets"].data_ptr(), B, n, None, None, s), "compact")
+            self.acc = (L.pts_accept_greedy,
+                        (x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
+                         W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(), W["oh"].data_ptr(),
+                         W["oc"].data_ptr(), n, self.acc_ws.data_ptr(), self.acc_ws.numel(), s))
+            self.comp = (L.pts_kv_compact,
+                         (pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
+                          W["page_indices"].data_ptr(), W["oh"].data_ptr(), n, W["oc"].data_ptr(), 4,
+                          W["offsets"].data_ptr(), B, n, None, None, s))
+
+    def run(self, ev=None):
+        from parallel_tree_spec_b200._lib import check
+        check(self.prep[0](*self.prep[1]), "prepare+append")
+        if ev is not None:
+            ev[0].record()
+        check(self.attn[0](*self.attn[1]), "attention")
+        if ev is not None:
+            ev[1].record()
+        if self.a.mode == "traversal":
+            check(self.L.pts_accept_traversal_compact(*self.acc_head, self.step_index, *self.acc_tail),
+                  "accept+compact")
+        else:
+            check(self.acc[0](*self.acc[1]), "accept")
+            check(self.comp[0](*self.comp[1]), "compact")
         if ev is not None:
             ev[2].record()
         self.step_index += 1
 
 
 # ---------------------------------------------------------------- CPU (oracle port)
-def cpu_sample_time(a, seed, n_req):
-    """Seconds the NumPy restatement of the path takes per request, measured on
-    ``n_req`` requests of the same workload (attention over the request's
-    4k-prefix KV for all query heads, acceptance over its [N, V] logits and
-    the walk, compaction of the accepted path)."""
+def _cpu_request_inputs(a, seed, r):
+    """Request r's inputs of the CPU sample (seeded per request, so every
+    worker builds the same inputs for the same request)."""
+    from oracle import attention as oatt
+    from parallel_tree_spec_b200 import workload as wl
+    rng = np.random.default_rng([seed + 100, r])
+    n = 1 + a.width * a.depth
+    kv_len = a.prefix + n
+    npg = (kv_len + 15) // 16
+    t = wl.make_tree(rng, a.width, a.depth, a.vocab)
+    x = wl.make_logits(rng, t, a.vocab, plant=1.0, soft=True)
+    layer = (rng.standard_normal((npg, 2, 16, a.hkv, 128), dtype=np.float32) / np.sqrt(128)).astype(np.float32)
+    q = rng.standard_normal((n, a.hq, 128), dtype=np.float32)
+    return dict(r=r, t=t, x=x, layer=layer, q=q, mask=oatt.tree_mask(t.parents, a.prefix), npg=npg, kv_len=kv_len)
+
+
+def _cpu_request_path(a, inp):
+    """The path on the host for one request: attention over its prefix KV for
+    every query head, acceptance over its [N, V] logits and the walk, the
+    compaction of the accepted path (the NumPy restatement)."""
     from oracle import accept as oacc
     from oracle import attention as oatt
     from oracle import kv as okv
     from oracle.philox import UniformStream
-    from parallel_tree_spec_b200 import workload as wl
+    t, n = inp["t"], inp["t"].size
+    oatt.tree_attention(inp["q"], inp["layer"], [list(range(inp["npg"]))], [inp["kv_len"]], [0, n], [inp["mask"]],
+                        1 / math.sqrt(128))
+    am, p = oacc.row_stats(inp["x"], a.temperature if a.mode == "traversal" else 1.0)
+    if a.mode == "traversal":
+        mb = oacc.mb_from_probs(t.parents, t.tokens, p)
+        s, h, tl, al, _ = oacc.traversal_walk(t.parents, t.tokens, t.draft_probs, mb, am,
+                                              UniformStream(5, 0, inp["r"]))
+    else:
+        s, h, tl, al = oacc.greedy_walk(t.parents, t.tokens, am)
+        h = list(h)
+    layer = inp["layer"].copy()
+    okv.request_reorder(layer[None], list(range(inp["npg"])), inp["kv_len"], h, a.prefix + 1)
 
-    rng = np.random.default_rng(seed + 100)
-    n = 1 + a.width * a.depth
-    kv_len = a.prefix + n
-    pl = 16
-    npg = (kv_len + pl - 1) // pl
-    t_total = 0.0
-    for r in range(n_req):
-        t = wl.make_tree(rng, a.width, a.depth, a.vocab)
-        x = wl.make_logits(rng, t, a.vocab, plant=1.0, soft=True)
-        layer = (rng.standard_normal((npg, 2, pl, a.hkv, 128), dtype=np.float32) / np.sqrt(128)).astype(np.float32)
-        q = rng.standard_normal((n, a.hq, 128), dtype=np.float32)
-        mask = oatt.tree_mask(t.parents, a.prefix)
+
+def _cpu_worker(conn, a_dict, seed, reqs):
+    """One host process: builds its requests' inputs once, then runs the path
+    over all of them on every "go" (single-threaded NumPy)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(1)
+    except Exception:
+        pass
+    a = argparse.Namespace(**a_dict)
+    inputs = [_cpu_request_inputs(a, seed, r) for r in reqs]
+    conn.send("ready")
+    while conn.recv() == "go":
+        for inp in inputs:
+            _cpu_request_path(a, inp)
+        conn.send("done")
+
+
+class CpuPath:
+    """The path over ``requests`` requests on the host cores: one process per
+    core (started with spawn), each owning a fixed share of the requests, so a
+    step's wall time is the batch over all cores."""
+
+    def __init__(self, a, requests, seed):
+        import multiprocessing as mp
+        ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        self.workers = max(1, min(ncpu, requests))
+        self.requests, self.cpus = requests, ncpu
+        ctx = mp.get_context("spawn")
+        self.conns, self.procs = [], []
+        for w in range(self.workers):
+            here, there = ctx.Pipe()
+            reqs = list(range(w, requests, self.workers))
+            pr = ctx.Process(target=_cpu_worker, args=(there, vars(a), seed, reqs), daemon=True)
+            pr.start()
+            self.conns.append(here)
+            self.procs.append(pr)
+        for c in self.conns:
+            assert c.recv() == "ready"
+
+    def step(self) -> float:
         t0 = time.perf_counter()
-        oatt.tree_attention(q, layer, [list(range(npg))], [kv_len], [0, n], [mask], 1 / math.sqrt(128))
-        am, p = oacc.row_stats(x, a.temperature if a.mode == "traversal" else 1.0)
-        if a.mode == "traversal":
-            mb = oacc.mb_from_probs(t.parents, t.tokens, p)
-            s, h, tl, al, _ = oacc.traversal_walk(t.parents, t.tokens, t.draft_probs, mb, am, UniformStream(5, 0, r))
-        else:
-            s, h, tl, al = oacc.greedy_walk(t.parents, t.tokens, am)
-            h = list(h)
-        pool = layer[None]
-        okv.request_reorder(pool, list(range(npg)), kv_len, h, a.prefix + 1)
-        t_total += time.perf_counter() - t0
-    return t_total / n_req
+        for c in self.conns:
+            c.send("go")
+        for c in self.conns:
+            assert c.recv() == "done"
+        return time.perf_counter() - t0
+
+    def close(self):
+        for c in self.conns:
+            try:
+                c.send("stop")
+            except Exception:
+                pass
+        for pr in self.procs:
+            pr.join(timeout=10)
 
 
 def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        info = threadpool_info()
-        return max([d.get("num_threads", 1) for d in info] or [1])
-    except Exception:
-        return os.cpu_count() or 1
+    """Host cores available to this process."""
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
 
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     n = 1 + a.width * a.depth
-    t_req = cpu_sample_time(a, a.seed, a.cpu_sample_requests)       # warm (first call pays imports)
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(max(1, min(a.warmup, 3))):
-        cpu_sample_time(a, a.seed, a.cpu_sample_requests)
-    for _ in range(max(1, a.steps)):
-        times.append(cpu_sample_time(a, a.seed, a.cpu_sample_requests) * a.batch)
-        if time.perf_counter() - t_start > a.cpu_time_budget:
-            break
+    requests = a.batch * max(world, a.gpus)                        # the same global batch as the GPU arm
+    cpu = CpuPath(a, requests, a.seed)
+    try:
+        for _ in range(max(1, min(a.warmup, 3))):
+            cpu.step()
+        times = []
+        t_start = time.perf_counter()
+        for _ in range(max(1, a.steps)):
+            times.append(cpu.step())
+            if time.perf_counter() - t_start > a.cpu_time_budget:
+                break
+    finally:
+        cpu.close()
     step_s = statistics.mean(times)
     value = 1.0 / step_s
     rec = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus, "steps": len(times),
         "warmup": a.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": workload_name(a), "global_batch": a.batch, "prefix": a.prefix, "tree_rows": n,
+        "config": {"workload": workload_name(a), "global_batch": requests, "prefix": a.prefix, "tree_rows": n,
                    "vocab": a.vocab, "mode": a.mode},
-        "tokens_per_s": value * a.batch * n,
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{a.cpu_sample_requests} request(s) of the {a.batch}-request step per timed "
-                                   f"step, scaled by {a.batch}; {len(times)} timed steps"},
+        "tokens_per_s": value * requests * n,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.workers, "host_cpus": cpu.cpus, "kind": "port",
+                         "sample": f"every step is the whole {requests}-request batch (attention for all heads, "
+                                   f"acceptance over [{n}, {a.vocab}] per request, compaction) on {cpu.workers} "
+                                   f"single-threaded host processes; {len(times)} timed steps"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(rec), flush=True)
@@ -399,6 +477,47 @@ def run_reference(a):
 
 
 # ---------------------------------------------------------------- GPU arm
+def time_steps(run, steps, n_events=3):
+    """Time ``steps`` calls of ``run(ev)`` on the current stream: total CUDA-event
+    milliseconds and the per-step event lists (ev[0..n_events-1] recorded by run)."""
+    import torch
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_events)] for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(steps):
+        run(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end), evs
+
+
+def mode_record(a, W, device, mode, top_p, steps, peak):
+    """One more acceptance mode of the same workload (greedy, or traversal with
+    a top-p target) timed on its own: steps/s, kernel times and the HBM
+    fraction of the slower hot kernel."""
+    import copy
+    b = copy.copy(a)
+    b.mode, b.top_p = mode, top_p
+    st = Step(b, W, device)
+    for _ in range(3):
+        st.run()
+    el, evs = time_steps(st.run, steps)
+    attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
+    acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    ab = algorithmic_bytes(b)
+    dom, dom_bytes, dom_us = (("tree_attn_kernel", ab["attention"], attn) if attn >= acc
+                              else ("acceptance", ab["accept"], acc))
+    return {"workload": workload_name(b), "value": steps / (el / 1e3), "unit": UNIT, "steps": steps,
+            "ms_per_step": el / steps,
+            "kernels_us": {"tree_attn": attn, "accept_with_compaction" if mode == "traversal" else
+                           "accept_then_compact": acc},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": dom_bytes / (dom_us * 1e-6) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": dom_bytes / (dom_us * 1e-6) / 1e9 / peak,
+                         "accept_frac": ab["accept"] / (acc * 1e-6) / 1e9 / peak},
+            "accept_len_mean": float(W["oc"][:, 2].float().mean().item())}
+
+
 def run_b200(a):
     import torch
     import torch.distributed as dist
@@ -422,28 +541,22 @@ def run_b200(a):
         step.run()
     torch.cuda.synchronize()
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local).start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_host0 = time.perf_counter()
-    start.record()
-    for i in range(a.steps):
-        step.run(evs[i])
-    end.record()
-    torch.cuda.synchronize()
+    elapsed_ms, evs = time_steps(step.run, a.steps)
     t_host1 = time.perf_counter()
     if world > 1:
         dist.barrier()
     sampler.stop()
-    elapsed_ms = start.elapsed_time(end)
     attn_ms = [e[0].elapsed_time(e[1]) for e in evs]
     acc_ms = [e[1].elapsed_time(e[2]) for e in evs]
     elapsed_ms, = over_ranks([elapsed_ms], "max", device)          # the slowest rank's time
     ms_per_step = elapsed_ms / a.steps
     value = world * a.steps / (elapsed_ms / 1e3)
+    accept_len = float(W["oc"][:, 2].float().mean().item())
 
     # e2e: tree inputs from pinned host memory, results back to the host every step
     e2e = run_e2e(a, W, step, device)
@@ -451,6 +564,7 @@ def run_b200(a):
 
     ab = algorithmic_bytes(a)
     peak, peak_kind = measured_peaks()
+    tpeak, tpeak_kind = measured_tensor_peak()
     k_attn = statistics.mean(attn_ms) * 1e-3
     k_acc = statistics.mean(acc_ms) * 1e-3
     dom = "tree_attn_kernel" if k_attn >= k_acc else "accept_stream_kernel"
@@ -459,12 +573,31 @@ def run_b200(a):
     achieved = dom_bytes / dom_s / 1e9
     traffic = traffic_table().get(dom)
     n = W["n"]
+    sub_steps = max(10, min(a.steps, 50))
+    sub = {}
+    if not a.no_sub:
+        # the other acceptance modes of the same workload (greedy; traversal with top-p 0.9)
+        sub["greedy"] = mode_record(a, W, device, "greedy", 1.0, sub_steps, peak)
+        sub["traversal_top_p_0.9"] = mode_record(a, W, device, "traversal", 0.9, sub_steps, peak)
+        if world == 1:
+            sub["config3_path"] = config3_record(a, device, sub_steps, peak)
+        else:
+            sub["tp"] = tp_record(a, world, rank, device, sub_steps)
+            sub["strong"] = strong_record(a, world, rank, device, sub_steps)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        t_req = cpu_sample_time(a, a.seed, a.cpu_sample_requests)
-        cpu = {"value": 1.0 / (t_req * a.batch), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"{a.cpu_sample_requests} request(s) of the {a.batch}-request step (attention for all "
-                         f"heads, acceptance over [{n}, {a.vocab}], compaction), scaled by {a.batch}"}
+        cp = CpuPath(a, a.batch, a.seed)
+        try:
+            cp.step()
+            ts = [cp.step() for _ in range(2)]
+        finally:
+            cp.close()
+        cpu = {"value": 1.0 / statistics.mean(ts), "unit": UNIT, "cores": cp.workers, "host_cpus": cp.cpus,
+               "kind": "port",
+               "sample": f"the whole {a.batch}-request step (attention for all heads, acceptance over [{n}, "
+                         f"{a.vocab}] per request, compaction) on {cp.workers} single-threaded host processes, "
+                         f"mean of 2 timed steps"}
+    flops = 4.0 * a.batch * a.hq * n * W["kv_len"] * 128
     rec = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -475,7 +608,12 @@ def run_b200(a):
         "tokens_per_s": value * a.batch * n,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes},
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
+                     "attention_tensor": {"flops_per_launch": flops, "achieved_tflops": flops / k_attn / 1e12,
+                                          "peak_tflops": tpeak, "peak_kind": tpeak_kind,
+                                          "frac": flops / k_attn / 1e12 / tpeak},
+                     "attention_hbm_frac": ab["attention"] / k_attn / 1e9 / peak,
+                     "accept_hbm_frac": ab["accept"] / k_acc / 1e9 / peak},
         "step_roofline": {"algorithmic_bytes": ab["step"], "achieved_gbs": ab["step"] / (ms_per_step * 1e-3) / 1e9,
                           "frac": ab["step"] / (ms_per_step * 1e-3) / 1e9 / peak},
         "kernels_us": {"tree_attn": k_attn * 1e6, "accept_with_compaction": k_acc * 1e6},
@@ -483,7 +621,8 @@ def run_b200(a):
         "e2e": e2e,
         "gpu_launches": step.launches_per_step * a.steps,
         "clocks": sampler.summary(t_host0, t_host1),
-        "accept_len_mean": float(W["oc"][:, 2].float().mean().item()),
+        "accept_len_mean": accept_len,
+        "sub": sub,
     }
     if rank == 0:
         print(json.dumps(rec), flush=True)
@@ -521,27 +660,19 @@ def run_e2e(a, W, step, device):
 
 
 # ---------------------------------------------------------------- tensor-parallel step
-def run_tp(a):
+def tp_record(a, world, rank, dev, steps):
     """Tensor-parallel verification step of a 70B-shaped target: every rank
     holds 8/N of the 8 KV heads (64/N query heads) and 1/N of the vocabulary;
     attention is local, acceptance exchanges per-row partials and tie indices
     over NCCL, and every rank walks the same trees.  Batch 64, prefixes drawn
     uniformly from [512, 8192], 65-row trees, random N(0, 3) logits (no
-    planting: nearly every node is rejected, the longest walks)."""
+    planting: nearly every node is rejected, the longest walks).  Every rank
+    calls this with the same arguments (it runs collectives)."""
     import torch
-    import torch.distributed as dist
     from parallel_tree_spec_b200 import _lib, kernels as K
     from parallel_tree_spec_b200 import workload as wl
     from parallel_tree_spec_b200._lib import check
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     if 8 % world:
         raise ValueError("--tp needs 1, 2, 4 or 8 ranks")
     L = _lib.lib()
@@ -608,24 +739,12 @@ def run_tp(a):
         K.kv_compact(pool, pind, perm, oh, oc, offs)
         res["oc"] = oc
 
-    for _ in range(max(3, a.warmup)):
+    for _ in range(3):
         one()
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local).start()
     if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    start.record()
-    for i in range(a.steps):
-        one(evs[i])
-    end.record()
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    sampler.stop()
-    el = start.elapsed_time(end)
+        torch.distributed.barrier()
+    el, evs = time_steps(one, steps)
     attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
     acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
     el, attn, acc = over_ranks([el, attn, acc], "max", dev)
@@ -634,25 +753,193 @@ def run_tp(a):
         same = bool(all(torch.equal(counts[0], counts[k]) for k in range(world)))
     else:
         same = True
-    rec = {
+    return {
         "metric": "tree-verify steps/s, tensor-parallel (vocabulary and KV heads split over the ranks)",
-        "value": a.steps / (el / 1e3), "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": el / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": "tensor-parallel tree-verify step: B=64 requests, prefixes U[512, 8192], tree rows "
-                               "65, Hq=64, Hkv=8, D=128, page 16, vocab 128256, traversal T=1.0, one layer",
-                   "parallelism": f"tp{world} (KV heads and vocabulary)"},
-        "tokens_per_s": a.steps / (el / 1e3) * B * n,
+        "value": steps / (el / 1e3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "ms_per_step": el / steps, "scaling": "strong",
+        "workload": "tensor-parallel tree-verify step: B=64 requests, prefixes U[512, 8192], tree rows 65, Hq=64, "
+                    "Hkv=8, D=128, page 16, vocab 128256, traversal T=1.0, one layer",
+        "parallelism": f"tp{world} (KV heads and vocabulary)",
+        "tokens_per_s": steps / (el / 1e3) * B * n,
         "kernels_us": {"tree_attn": attn, "accept_with_exchange": acc},
         "ranks_agree": same,
-        "clocks": sampler.summary(t0, t1),
     }
+
+
+def config3_record(a, dev, steps, peak):
+    """The path of a Llama-3-8B-shaped verify step: B=32 requests, prefixes
+    U[1024, 2048], 49-row trees (width 8, depth 6), 32 query / 8 KV heads,
+    32 attention layers (per layer: the tree K/V append and the tree
+    attention; layer 0's append shares a launch with the tree masks and
+    positions), then traversal acceptance at T=0.8 over [1568, 128256] bf16
+    logits with the accepted paths' KV compacted in all 32 layers.  The model's
+    projections, MLPs, norms and lm_head (library GEMMs, outside the path) do
+    not run: every layer's q and new k/v are seeded synthetic tensors."""
+    import torch
+    from parallel_tree_spec_b200 import _lib, kernels as K
+    from parallel_tree_spec_b200 import workload as wl
+    from parallel_tree_spec_b200._lib import check
+
+    L, B, Hq, Hkv, D, pl, V, temp = 32, 32, 32, 8, 128, 16, a.vocab, 0.8
+    lib = _lib.lib()
+    rng = np.random.default_rng(a.seed + 31)
+    trees = [wl.make_tree(rng, 8, 6, V) for _ in range(B)]
+    n = trees[0].size
+    prefix = rng.integers(1024, 2049, size=B)
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    kv_lens = prefix + n
+    npg = (kv_lens + pl - 1) // pl
+    page_indptr = np.concatenate([[0], np.cumsum(npg)]).astype(np.int32)
+    max_pages = int(page_indptr[-1]) + 16
+    T = B * n
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 33)
+    pool = torch.empty(L, max_pages, 2, pl, Hkv, D, dtype=torch.bfloat16, device=dev).normal_(0, 1 / math.sqrt(D),
+                                                                                            generator=g)
+    perm = torch.randperm(max_pages, generator=g, device=dev)[: page_indptr[-1]].to(torch.int32)
+    q = torch.randn(L, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    kn = (torch.randn(L, T, Hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    vn = (torch.randn(L, T, Hkv, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    x = (torch.randn(T, V, generator=g, device=dev) * 3.0).to(torch.bfloat16)
+    # children's tokens near their parent row's max, so walks go deep
+    prow = np.concatenate([indptr[b] + np.maximum(par[indptr[b]:indptr[b + 1]], 0) for b in range(B)])
+    child = np.nonzero(par >= 0)[0]
+    pr_t = torch.from_numpy(prow[child].astype(np.int64)).to(dev)
+    tk_t = torch.from_numpy(tok[child].astype(np.int64)).to(dev)
+    boost = torch.rand(child.size, generator=g, device=dev) * 3.0 - 0.5
+    x[pr_t, tk_t] = (x[pr_t].float().amax(dim=1) + boost).to(torch.bfloat16)
+    d = lambda v: torch.as_tensor(np.ascontiguousarray(v), dtype=torch.int32, device=dev)
+    qo, parents, tokens = d(indptr), d(par), d(tok)
+    draft = torch.as_tensor(dp, device=dev)
+    pind, lastp, seqlens, offs = d(page_indptr), d((kv_lens - 1) % pl + 1), d(kv_lens), d(prefix)
+    mw = K.mask_words_for(n)
+    bits = torch.empty(T, mw, dtype=torch.int64, device=dev)
+    bi = torch.empty(T, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, dtype=torch.int32, device=dev)
+    out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
+    attn_ws = K.workspace(dev, "attn", 256)
+    acc_ws = K.workspace(dev, "accept", lib.pts_accept_workspace_size(T, V))
+    ot = torch.empty(B, n, dtype=torch.int32, device=dev)
+    oh = torch.empty(B, n, dtype=torch.int32, device=dev)
+    oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    cargs = _lib.KvCompactArgs(pool.data_ptr(), L, max_pages, pl, Hkv, D, 2, pind.data_ptr(), perm.data_ptr(),
+                               offs.data_ptr(), None, None)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    layer_bytes = pool[0].numel() * 2
+    state = {"off": 0}
+
+    def one(ev=None):
+        if ev is not None:
+            ev[0].record()
+        for l in range(L):
+            lay = pool.data_ptr() + l * layer_bytes
+            if l == 0:
+                check(lib.pts_tree_prepare_append(parents.data_ptr(), qo.data_ptr(), seqlens.data_ptr(), B, mw,
+                                                  bits.data_ptr(), bi.data_ptr(), pos.data_ptr(), kn[0].data_ptr(),
+                                                  vn[0].data_ptr(), Hkv * D, Hkv * D, lay, pind.data_ptr(),
+                                                  perm.data_ptr(), T, Hkv, D, pl, max_pages, 2, s), "prepare+append")
+            else:
+                check(lib.pts_kv_append(kn[l].data_ptr(), vn[l].data_ptr(), Hkv * D, Hkv * D, lay, bi.data_ptr(),
+                                        pos.data_ptr(), pind.data_ptr(), perm.data_ptr(), T, Hkv, D, pl, max_pages, 2,
+                                        s), "append")
+            check(lib.pts_tree_attn_run(q[l].data_ptr(), lay, qo.data_ptr(), pind.data_ptr(), perm.data_ptr(),
+                                        lastp.data_ptr(), bits.data_ptr(), mw, out.data_ptr(), B, T, n,
+                                        int(kv_lens.max()), Hq, Hkv, D, pl, max_pages, 1 / math.sqrt(D),
+                                        attn_ws.data_ptr(), attn_ws.numel(), s), "attention")
+        if ev is not None:
+            ev[1].record()
+        check(lib.pts_accept_traversal_compact(x.data_ptr(), x.stride(0), qo.data_ptr(), parents.data_ptr(),
+                                               tokens.data_ptr(), draft.data_ptr(), B, T, V, n, -1, temp, 1.0, 0, 5,
+                                               state["off"], ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), n,
+                                               acc_ws.data_ptr(), acc_ws.numel(), ctypes.byref(cargs), s),
+              "accept+compact")
+        state["off"] += 1
+        if ev is not None:
+            ev[2].record()
+
+    for _ in range(3):
+        one()
+    el, evs = time_steps(one, steps)
+    layers_us = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
+    acc_us = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    kv_read = int(np.sum(kv_lens)) * Hkv * D * 2 * 2 * L
+    qo_bytes = 2 * T * Hq * D * 2 * L
+    append = T * Hkv * D * 2 * 2 * L
+    logit_bytes = T * V * 2
+    return {"workload": f"config-3 verify-step path: B={B} requests, prefixes U[1024, 2048], tree rows {n} (width 8, "
+                        f"depth 6), Hq={Hq}, Hkv={Hkv}, D=128, page 16, {L} attention layers, vocab {V}, traversal "
+                        f"T={temp}, compaction in all {L} layers; model GEMMs excluded",
+            "value": steps / (el / 1e3), "unit": UNIT, "steps": steps, "ms_per_step": el / steps,
+            "tokens_per_s": steps / (el / 1e3) * T,
+            "kernels_us": {"append_and_attention_32_layers": layers_us, "accept_with_compaction": acc_us},
+            "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
+                         "layers_frac": (kv_read + qo_bytes + append) / (layers_us * 1e-6) / 1e9 / peak,
+                         "accept_frac": logit_bytes / (acc_us * 1e-6) / 1e9 / peak,
+                         "step_frac": (kv_read + qo_bytes + append + logit_bytes) / (el / steps * 1e-3) / 1e9 / peak},
+            "accept_len_mean": float(oc[:, 2].float().mean().item())}
+
+
+def strong_record(a, world, rank, dev, steps):
+    """Strong scaling of the batch-sharded step: the 16 requests of the
+    benchmark workload split over the ranks (16/N each).  At N >= 4 a rank's KV
+    and logits fit in L2, so a 256 MB buffer is written between steps, outside
+    the timed events.  Every rank calls this (it reduces over ranks)."""
+    import copy
+    import torch
+    b = copy.copy(a)
+    b.batch = max(1, a.batch // world)
+    W = build_workload(b, dev, a.seed + 5000 + 1000 * rank)
+    st = Step(b, W, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        st.run()
+    per = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        st.run()
+        e1.record()
+        per.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in per)
+    ms, = over_ranks([ms], "max", dev)
+    return {"workload": workload_name(b).replace(f"B={b.batch} requests", f"B={a.batch} requests in total "
+                                                                        f"({b.batch} per rank)"),
+            "value": 1e3 / ms, "unit": UNIT, "n_gpus": world, "steps": steps, "ms_per_step": ms,
+            "scaling": "strong", "l2": "256 MB written between timed steps (outside the timed events)",
+            "tokens_per_s": 1e3 / ms * a.batch * W["n"]}
+
+
+def run_tp(a):
+    """``--tp``: the tensor-parallel step alone, one JSON line."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    sampler = ClockSampler(local).start()
+    t0 = time.perf_counter()
+    r = tp_record(a, world, rank, dev, a.steps)
+    t1 = time.perf_counter()
+    sampler.stop()
+    rec = {"metric": r["metric"], "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+           "config": {"workload": r["workload"], "parallelism": r["parallelism"]},
+           "tokens_per_s": r["tokens_per_s"], "kernels_us": r["kernels_us"], "ranks_agree": r["ranks_agree"],
+           "clocks": sampler.summary(t0, t1)}
     if rank == 0:
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0 if same else 1
+    return 0 if r["ranks_agree"] else 1
 
 
 # ---------------------------------------------------------------- long-context sparse step

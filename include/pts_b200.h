@@ -124,6 +124,20 @@ int pts_accept_traversal_compact(const uint16_t* logits, int64_t row_stride, con
                                  size_t workspace_bytes, const pts_kv_compact_args* compact,
                                  pts_stream_t stream);
 
+/* The per-row statistics the last bf16 acceptance call (pts_accept_greedy*,
+ * pts_accept_traversal* without top-p) on `workspace` used: out_argmax[r] =
+ * the argmax of row r's rounded softmax, out_mb[r] = the rounded probability
+ * of row r's token under its parent's row (1 for roots), with the same
+ * arithmetic the walks use.  The same logits, trees and temperature as that
+ * call.  These are _sample_probs(...).argmax() (verification.py:46-77) and
+ * probs[parent, token] (verification.py:310-349) as this library computes
+ * them, exported for diagnostics and parity measurements. */
+int pts_accept_export_row_stats(const void* workspace, size_t workspace_bytes, const uint16_t* logits,
+                                int64_t row_stride, const int32_t* row_indptr, const int32_t* parents,
+                                const int32_t* tokens, int batch, int num_rows, int vocab,
+                                float temperature, int32_t* out_argmax, float* out_mb,
+                                pts_stream_t stream);
+
 /* verify_tree_exact / verify_tree_traversal over fp32 logits (small fp32
  * models, for example the reference's 2-layer configuration): the
  * probabilities stay fp32 as torch's softmax of fp32 logits does
@@ -192,9 +206,10 @@ int pts_accept_walk_merged(void* row_stats, const float* token_logit, const int3
  * server whose device memory is planned up front and may not call cudaMalloc
  * later).  Scratch comes from a fixed 2 MiB device array inside the library
  * (present on every GPU that loads it, until exit); sizes needing more are
- * rejected with PTS_ERR_CAPACITY.  The first call on a device looks up that
- * array's device address -- make it before any stream capture.  Calls share
- * the array: calls whose kernels overlap on the GPU race. */
+ * rejected with PTS_ERR_CAPACITY.  The first call on a device (and the first
+ * after another CUDA context is made current there) looks up that array's
+ * device address -- make it before any stream capture.  Calls share the
+ * array: calls whose kernels overlap on the GPU race. */
 int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride,
                                  const int32_t* row_indptr, const int32_t* parents,
                                  const int32_t* tokens, const float* draft_probs, int batch,

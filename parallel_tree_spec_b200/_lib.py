@@ -48,6 +48,8 @@ SIGNATURES = {
                                                f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp, vp]),
     "pts_accept_traversal_noalloc": (C.c_int, [vp, i64, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64,
                                                f32, f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp]),
+    "pts_accept_export_row_stats": (C.c_int, [vp, sz, vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, f32, vp, vp,
+                                              vp]),
     "pts_accept_shard_partials": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,
                                             vp, sz, vp]),
     "pts_accept_merge_shards": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),

@@ -37,6 +37,7 @@
 //
 // Workspace (caller-owned): chunk partials, row stats, and per-row and
 // per-request counters that are cleared at the start of every call.
+#include <cuda.h>
 #include <float.h>
 #include <limits.h>
 
@@ -1930,24 +1931,13 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
     const size_t ssmem =
         ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan, p.batch);
     if (ssmem <= kMaxDynSmem) {
-      static size_t ssmem_attr[256] = {};
-      if (ssmem > ssmem_attr[dev]) {
-        PTS_CUDA_TRY(
-            cudaFuncSetAttribute(accept_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
-        ssmem_attr[dev] = ssmem;
-      }
+      if (int rc = ensure_smem_attr((const void*)accept_stream_kernel, ssmem)) return rc;
       accept_stream_kernel<<<plan.G + plan.walkers, kSThreads, ssmem, stream>>>(p, plan);
       return launch_status("accept_stream_kernel");
     }
   }
   const size_t smem = walk_smem_bytes(p.max_nodes);
-  static size_t smem_attr[256] = {};
-  if (smem > smem_attr[dev]) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    PTS_CUDA_TRY(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                      (int)cudaSharedmemCarveoutMaxShared));
-    smem_attr[dev] = smem;
-  }
+  if (int rc = ensure_smem_attr((const void*)accept_kernel, smem, true)) return rc;
   accept_kernel<<<dim3(nchunks, p.num_rows), kThreads, smem, stream>>>(p);
   return launch_status("accept_kernel");
 }
@@ -2221,13 +2211,7 @@ int accept_f32_launch(AcceptParams p, float temperature, void* workspace, size_t
   if (rc) return rc;
   const size_t smem = walk_smem_bytes(p.max_nodes);
   if (smem > kMaxDynSmem) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
-  int dev = 0;
-  PTS_CUDA_TRY(cudaGetDevice(&dev));
-  static size_t attr[256] = {};
-  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr[dev] = smem;
-  }
+  if (int rc = ensure_smem_attr((const void*)walk_merged_kernel, smem)) return rc;
   walk_merged_kernel<<<p.batch, 32, smem, stream>>>(p, nullptr, 0);
   return launch_status("walk_merged_kernel");
 }
@@ -2343,13 +2327,7 @@ int accept_traversal_extended(AcceptParams p, float temperature, float top_p, in
   }
   const size_t smem = walk_smem_bytes(p.max_nodes);
   if (smem > kMaxDynSmem) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
-  int dev = 0;
-  PTS_CUDA_TRY(cudaGetDevice(&dev));
-  static size_t attr[256] = {};
-  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr[dev] = smem;
-  }
+  if (int rc = ensure_smem_attr((const void*)walk_merged_kernel, smem)) return rc;
   walk_merged_kernel<<<p.batch, 32, smem, stream>>>(q, nullptr, 0);
   rc = launch_status("walk_merged_kernel");
   if (rc || !do_sample) return rc;
@@ -2366,6 +2344,66 @@ extern "C" size_t pts_accept_workspace_size(int num_rows, int vocab) {
   size_t a, b, c, d;
   if (num_rows <= 0 || vocab <= 0) return 0;
   return ws_layout(num_rows, vocab, &a, &b, &c, &d) + topp_ws_bytes(num_rows);
+}
+
+namespace pts {
+namespace {
+
+// One thread per row: the row's argmax as the last acceptance call on this
+// workspace determined it, and the row's node probability Mb = p[parent, token]
+// from the same row statistics and the same device arithmetic the walks use.
+__global__ void export_row_stats_kernel(AcceptParams p, const RowStat* rows, int32_t* out_argmax, float* out_mb) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= p.num_rows) return;
+  out_argmax[r] = rows[r].argmax;
+  // the request holding row r: binary search over row_indptr
+  int lo = 0, hi = p.batch;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (p.row_indptr[mid] <= r) lo = mid;
+    else hi = mid;
+  }
+  const int base = p.row_indptr[lo];
+  const int par = p.parents[r];
+  const int tk = p.tokens[r];
+  float mb = 1.0f;
+  if (par >= 0) {
+    const int pr = base + par;
+    const float x = (tk < 0 || tk >= p.vocab) ? -INFINITY : load_scaled(p, p.logits + (int64_t)pr * p.row_stride, tk);
+    mb = node_mb(p, x, pr, rows[pr].m, rows[pr].s);
+  }
+  out_mb[r] = mb;
+}
+
+}  // namespace
+}  // namespace pts
+
+extern "C" int pts_accept_export_row_stats(const void* workspace, size_t workspace_bytes, const uint16_t* logits,
+                                           int64_t row_stride, const int32_t* row_indptr, const int32_t* parents,
+                                           const int32_t* tokens, int batch, int num_rows, int vocab,
+                                           float temperature, int32_t* out_argmax, float* out_mb,
+                                           pts_stream_t stream) {
+  PTS_CHECK_ARG(workspace && logits && row_indptr && parents && tokens && out_argmax && out_mb, "null pointer");
+  PTS_CHECK_ARG(batch > 0 && num_rows >= batch && vocab > 0 && row_stride >= vocab, "bad sizes");
+  PTS_CHECK_ARG(temperature > 0.0f, "temperature must be positive");
+  size_t opt, orw, orc, oqc;
+  const size_t need = ws_layout(num_rows, vocab, &opt, &orw, &orc, &oqc);
+  if (workspace_bytes < need) return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", workspace_bytes,
+                                               need);
+  AcceptParams p{};
+  p.logits = logits;
+  p.row_stride = row_stride;
+  p.row_indptr = row_indptr;
+  p.parents = parents;
+  p.tokens = tokens;
+  p.batch = batch;
+  p.num_rows = num_rows;
+  p.vocab = vocab;
+  p.use_temp = (temperature != 1.0f);
+  p.inv_temp = 1.0f / temperature;
+  const RowStat* rows = (const RowStat*)((const uint8_t*)workspace + orw);
+  export_row_stats_kernel<<<(num_rows + 255) / 256, 256, 0, (cudaStream_t)stream>>>(p, rows, out_argmax, out_mb);
+  return launch_status("export_row_stats_kernel");
 }
 
 // The compaction arguments into p (nullptr: none), checked like pts_kv_compact's.
@@ -2552,13 +2590,7 @@ extern "C" int pts_accept_walk_merged(void* row_stats, const float* token_logit,
   p.stats_ready = 1;
   const size_t smem = walk_smem_bytes(max_nodes);
   if (smem > 232448) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
-  int dev = 0;
-  PTS_CUDA_TRY(cudaGetDevice(&dev));
-  static size_t attr[256] = {};
-  if (dev >= 0 && dev < 256 && smem > attr[dev]) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(walk_merged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr[dev] = smem;
-  }
+  if (int rc = ensure_smem_attr((const void*)walk_merged_kernel, smem)) return rc;
   walk_merged_kernel<<<batch, 32, smem, (cudaStream_t)stream>>>(p, ties_all, num_shards);
   return launch_status("walk_merged_kernel");
 }
@@ -2637,22 +2669,39 @@ constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;   // 2 MiB
 static __device__ __align__(256) uint8_t g_accept_scratch[kNoAllocScratchBytes];
 
 // The array's name in host code is only a host-side handle; the kernel needs
-// the device address, looked up once per device with that device current.
+// the device address, looked up with the device current.  That address
+// belongs to the CUDA context the module was loaded into, so the cache is
+// keyed on the current context's unique id (cuCtxGetId): a caller that makes
+// another context current, or a device reset that recreates the primary
+// context, gets a fresh lookup instead of a stale address.
 int noalloc_scratch(void** out) {
+  struct Entry {
+    unsigned long long ctx_id;
+    void* addr;
+  };
   static std::mutex mu;
-  static void* addr[256] = {};
+  static Entry cache[256] = {};
   int dev = 0;
   PTS_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 256) return set_error(PTS_ERR_UNSUPPORTED, "device ordinal %d", dev);
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_accept_scratch);
-    if (e != cudaSuccess || !p)
-      return set_error(PTS_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
-    addr[dev] = p;
+  unsigned long long id = 0;
+  const bool have_ctx = current_context_id(&id) == PTS_OK;
+  if (have_ctx && cache[dev].addr && cache[dev].ctx_id == id) {
+    *out = cache[dev].addr;
+    return PTS_OK;
   }
-  *out = addr[dev];
+  // first call in this context (the lookup also makes the device's primary
+  // context current when no context is yet)
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_accept_scratch);
+  if (e != cudaSuccess || !p)
+    return set_error(PTS_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+  int rc = current_context_id(&id);
+  if (rc != PTS_OK) return rc;
+  cache[dev].ctx_id = id;
+  cache[dev].addr = p;
+  *out = p;
   return PTS_OK;
 }
 
@@ -2660,12 +2709,14 @@ int noalloc_scratch(void** out) {
 }  // namespace pts
 
 // Same arguments and results as pts_accept_traversal, without the workspace.
-// The first call on a device looks up the scratch array's device address;
-// make that first call before capturing the stream into a CUDA graph.  All
-// calls share the one array (its counters are cleared at the start of every
-// call), so two calls whose kernels overlap on the same GPU (for example on
-// two streams at once) race and must be serialised by the caller.  Sizes whose scratch exceeds 2 MiB (for example more than 4096
-// tree rows at a 262144-entry vocabulary) are rejected with PTS_ERR_CAPACITY.
+// The first call in a CUDA context (per device, and again after the current
+// context changes) looks up the scratch array's device address; make that
+// first call before capturing the stream into a CUDA graph.  All calls share
+// the one array (its counters are cleared at the start of every call), so two
+// calls whose kernels overlap on the same GPU (for example on two streams at
+// once) race and must be serialised by the caller.  Sizes whose scratch
+// exceeds 2 MiB (about 292 bytes per tree row at a 262144-entry vocabulary,
+// so about 7000 rows there) are rejected with PTS_ERR_CAPACITY.
 extern "C" int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
                                             const int32_t* parents, const int32_t* tokens, const float* draft_probs,
                                             int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,

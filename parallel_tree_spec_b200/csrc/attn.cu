@@ -755,11 +755,7 @@ static int tree_attn_launch(const void* q, const void* kv_layer, const int32_t* 
   p.max_pages = max_pages;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.err = (int*)workspace;
-  static bool attr_set = false;
-  if (!attr_set) {
-    PTS_CUDA_TRY(cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    attr_set = true;
-  }
+  if (int rc = ensure_smem_attr((const void*)tree_attn_kernel, kSmemBytes)) return rc;
   const int groups = (max_qo_len * g + kGroupRows - 1) / kGroupRows;
   if (groups > 65535) return set_error(PTS_ERR_CAPACITY, "%d query rows per request is too many", max_qo_len);
   dim3 grid(num_kv_heads, batch, groups);

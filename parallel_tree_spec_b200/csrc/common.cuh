@@ -12,6 +12,15 @@ namespace pts {
 // Records a message for pts_last_error() and returns the code.
 int set_error(int code, const char* fmt, ...);
 
+// The unique id of the current CUDA context (cuCtxGetId); PTS_ERR_CUDA when
+// there is none.
+int current_context_id(unsigned long long* id);
+
+// Raises `func`'s dynamic shared-memory limit to `bytes` (and, if asked, its
+// preferred carveout to the maximum) in the current context.  Thread-safe;
+// the attribute call is made once per (context, kernel) and size.
+int ensure_smem_attr(const void* func, size_t bytes, bool max_carveout = false);
+
 #define PTS_CHECK_ARG(cond, ...)                                  \
   do {                                                            \
     if (!(cond)) return ::pts::set_error(PTS_ERR_INVALID, __VA_ARGS__); \

@@ -1,6 +1,12 @@
-// Error reporting for the C ABI (thread-local last message).
+// Error reporting for the C ABI (thread-local last message), and the
+// per-context bookkeeping the launchers share.
+#include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -14,6 +20,51 @@ int set_error(int code, const char* fmt, ...) {
   vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
   va_end(ap);
   return code;
+}
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+int current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = (CtxGetCurrentFn)f;
+    f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = (CtxGetIdFn)f;
+  });
+  if (!get_current || !get_id) return set_error(PTS_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return set_error(PTS_ERR_CUDA, "no current CUDA context");
+  if (get_id(ctx, id) != CUDA_SUCCESS) return set_error(PTS_ERR_CUDA, "cuCtxGetId failed");
+  return PTS_OK;
+}
+
+int ensure_smem_attr(const void* func, size_t bytes, bool max_carveout) {
+  static std::mutex mu;
+  static std::map<std::pair<unsigned long long, const void*>, size_t> done;
+  unsigned long long ctx = 0;
+  const bool keyed = current_context_id(&ctx) == PTS_OK;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(ctx, func);
+  if (keyed) {
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return PTS_OK;
+  }
+  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess)
+    return set_error(PTS_ERR_CUDA, "cudaFuncSetAttribute(%zu bytes): %s", bytes, cudaGetErrorString(e));
+  if (keyed) done[key] = bytes;
+  return PTS_OK;
 }
 
 }  // namespace pts

@@ -463,7 +463,7 @@ extern "C" int pts_kv_compact(void* kv_pool, int num_layers, int max_pages, int 
   cudaStream_t st = (cudaStream_t)stream;
   if (max_accepted > 0) {
     if (smem > 48 * 1024)
-      PTS_CUDA_TRY(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      if (int rc = ensure_smem_attr((const void*)kv_compact_kernel, smem)) return rc;
     if (2 * num_layers > 65535 || batch > 65535) return set_error(PTS_ERR_CAPACITY, "grid too large");
     const int64_t layer_bytes = (int64_t)max_pages * 2 * page_len * num_kv_heads * head_bytes;
     dim3 grid(num_kv_heads, 2 * num_layers, batch);

@@ -231,7 +231,7 @@ extern "C" int pts_select_pages(const float* key_sums, const int32_t* page_indpt
   p.max_sort = M;
   const size_t smem = (size_t)M * sizeof(unsigned long long);
   if (smem > 48 * 1024)
-    PTS_CUDA_TRY(cudaFuncSetAttribute(select_pages_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (int rc = ensure_smem_attr((const void*)select_pages_kernel, smem)) return rc;
   select_pages_kernel<<<batch * num_kv_heads, kSelThreads, smem, (cudaStream_t)stream>>>(p);
   return launch_status("select_pages_kernel");
 }

@@ -172,6 +172,26 @@ def accept_traversal(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
 
 
 # ------------------------------------------------- vocabulary-sharded acceptance
+def accept_row_stats(logits: torch.Tensor, row_indptr: torch.Tensor, parents: torch.Tensor, tokens: torch.Tensor,
+                     temperature: float = 1.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(argmax [rows] int32, Mb [rows] float32) that the most recent bf16
+    acceptance call on the current stream computed for these inputs (same
+    logits, trees and temperature, no top-p): each row's argmax of its rounded
+    softmax and each node's probability under its parent's row."""
+    dev, row_indptr, parents, tokens = _accept_common(logits, row_indptr, parents, tokens)
+    if logits.dtype != torch.bfloat16:
+        raise ValueError("accept_row_stats takes bf16 logits")
+    R, V = logits.shape
+    B = row_indptr.numel() - 1
+    ws = workspace(dev, "accept", _lib.lib().pts_accept_workspace_size(R, V))
+    am = torch.empty(R, dtype=torch.int32, device=dev)
+    mb = torch.empty(R, dtype=torch.float32, device=dev)
+    _lib.call("pts_accept_export_row_stats", ws.data_ptr(), ws.numel(), logits.data_ptr(), logits.stride(0),
+              row_indptr.data_ptr(), parents.data_ptr(), tokens.data_ptr(), B, R, V, float(temperature),
+              am.data_ptr(), mb.data_ptr(), _stream(dev))
+    return am, mb
+
+
 def accept_shard_partials(logits_shard: torch.Tensor, vocab_offset: int, row_indptr: torch.Tensor,
                           parents: torch.Tensor, tokens: torch.Tensor, temperature: float = 1.0):
     """Step 1 of the sharded acceptance: ``logits_shard`` [rows, Vs] bf16 is

@@ -33,7 +33,7 @@ import torch
 from . import kernels as K
 from .attention_wrapper import BeFlashinferWrapper
 from .cache_manager import KvCachePool, RequestKvCache, getKvCacheBatchPosition
-from .tree import Tree
+from .tree import Tree, tree_columns
 
 
 @dataclass
@@ -115,21 +115,47 @@ def _rows(logits: torch.Tensor) -> torch.Tensor:
     return x
 
 
-def _tree_columns(trees: Sequence[Tree], device):
-    cols = [t.as_arrays() for t in trees]
+_staging = {}
+
+
+def _pinned(device, n: int) -> torch.Tensor:
+    """A pinned host staging buffer per device, grown on demand.  Before it is
+    refilled, the host waits for the copy that last read it."""
+    key = str(device)
+    entry = _staging.get(key)
+    if entry is not None and entry[1] is not None:
+        entry[1].synchronize()
+    if entry is None or entry[0].numel() < n:
+        entry = (torch.empty(max(n, 4096), dtype=torch.int32, pin_memory=True), None)
+        _staging[key] = entry
+    return entry[0]
+
+
+def _copied(device, d: torch.Tensor) -> None:
+    """Mark the staging buffer of ``device`` as read by the copy just enqueued."""
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(d.device))
+    _staging[str(device)] = (_staging[str(device)][0], ev)
+
+
+def _tree_columns(trees: Sequence, device):
+    """Row pointers, parents, tokens and draft probabilities of a batch of
+    trees (read through ``get_tree_data()``), moved to ``device`` in one copy."""
+    cols = [tree_columns(t) for t in trees]
     sizes = [c[0].shape[0] for c in cols]
     indptr = np.zeros(len(trees) + 1, dtype=np.int32)
     indptr[1:] = np.cumsum(sizes)
-    host = torch.empty(len(trees) + 1 + 3 * int(indptr[-1]), dtype=torch.int32, pin_memory=True)
+    B, T = len(trees), int(indptr[-1])
+    total = B + 1 + 3 * T
+    host = _pinned(device, total)
     h = host.numpy()
-    T = int(indptr[-1])
-    h[: len(trees) + 1] = indptr
-    o = len(trees) + 1
+    h[: B + 1] = indptr
+    o = B + 1
     h[o:o + T] = np.concatenate([c[0] for c in cols])
     h[o + T:o + 2 * T] = np.concatenate([c[1] for c in cols])
     h[o + 2 * T:o + 3 * T] = np.concatenate([c[2] for c in cols]).view(np.int32)
-    d = host.to(device, non_blocking=True)
-    B = len(trees)
+    d = host[:total].to(device, non_blocking=True)
+    _copied(device, d)
     return (d[: B + 1], d[o:o + T], d[o + T:o + 2 * T], d[o + 2 * T:o + 3 * T].view(torch.float32), max(sizes))
 
 

@@ -9,7 +9,7 @@ from oracle import attention as att
 from parallel_tree_spec_b200 import cache_manager as cm
 from parallel_tree_spec_b200 import verification as ver
 from parallel_tree_spec_b200 import workload as wl
-from parallel_tree_spec_b200.tree import Tree
+from parallel_tree_spec_b200.tree import Tree, TreeNode, tree_columns
 
 
 def test_tree_mask_matches_reference_golden(mask_golden):
@@ -27,7 +27,7 @@ def test_tree_columns_depths_and_children():
     rng = np.random.default_rng(5)
     w = wl.make_tree(rng, 4, 5, 1000)
     t = Tree.from_arrays(w.parents, w.tokens, w.draft_probs)
-    par, tok, prob, _ = t.as_arrays()
+    par, tok, prob, _ = tree_columns(t)
     assert np.array_equal(par, w.parents) and np.array_equal(tok, w.tokens)
     assert np.allclose(prob[1:], w.draft_probs[1:])
     data = t.get_tree_data()
@@ -49,11 +49,62 @@ def test_tree_add_nodes_levels():
     t = Tree(7)
     t.add_nodes(torch.tensor([[[11, 12]]]), torch.tensor([[[0.6, 0.3]]]), torch.tensor([[[0, 0]]]))
     t.add_nodes(torch.tensor([[[21, 22, 23]]]), torch.tensor([[[0.5, 0.2, 0.9]]]), torch.tensor([[[0, 1, 1]]]))
-    par, tok, _, _ = t.as_arrays()
+    par, tok, _, _ = tree_columns(t)
     assert par.tolist() == [-1, 0, 0, 1, 2, 2]
     assert tok.tolist() == [7, 11, 12, 21, 22, 23]
     assert t.available_leaves == [3, 4, 5]
     assert t.find_child_index(2, 23) == 5
+
+
+def test_tree_grown_like_the_reference_producer():
+    """The reference's beam search grows trees by hand: it appends to
+    ``tree.nodes``, extends a parent's ``children`` and bumps
+    ``tree.current_size`` (beam_search.py:441-447,570-579).  The columns,
+    the mask and the node accessors follow those edits."""
+    t = Tree(torch.tensor(5))
+    for tok in (10, 11):
+        i = t.current_size
+        t.nodes[0].children.append(i)
+        t.nodes.append(TreeNode(parent=0, token_id=tok, cumulative_probability=0.25, depth=1))
+        t.current_size += 1
+    t.available_leaves = [1, 2]
+    t.add_nodes(torch.tensor([[[20, 21]]]), torch.tensor([[[0.5, 0.125]]]), torch.tensor([[[1, 1]]]))
+    i = t.current_size
+    t.nodes[3].children.append(i)
+    t.nodes.append(TreeNode(parent=3, token_id=30, cumulative_probability=0.75, depth=3))
+    t.current_size += 1
+    par, tok, prob, dep = tree_columns(t)
+    assert par.tolist() == [-1, 0, 0, 2, 2, 3]
+    assert tok.tolist() == [5, 10, 11, 20, 21, 30]
+    assert prob.tolist() == [1.0, 0.25, 0.25, 0.5, 0.125, 0.75]
+    assert dep.tolist() == [0, 1, 1, 2, 2, 3]
+    assert t.find_child_index(2, 21) == 4 and t.get_node(5).token_id == 30
+    assert t.get_children_ids(2).tolist() == [20, 21]
+    assert np.array_equal(t.create_attention_mask(prefix_length=3)[0, 0].numpy(), att.tree_mask(par, 3))
+
+
+class _ForeignTree:
+    """A tree of another class that offers only the reference's interface
+    (``nodes``, ``current_size``, ``get_tree_data``), as the reference's own
+    ``Tree`` does."""
+
+    def __init__(self, parents, tokens):
+        self.current_size = len(parents)
+        self._p, self._t = list(parents), list(tokens)
+
+    def get_tree_data(self, skip_nodes: int = 0):
+        n = len(self._p)
+        return {"token_ids": torch.tensor(self._t, dtype=torch.long),
+                "cumulative_probabilities": torch.full((n,), 0.5, dtype=torch.float32),
+                "depths": torch.tensor(wl.DraftTree(np.asarray(self._p), np.asarray(self._t),
+                                                    np.ones(n, np.float32)).depths()),
+                "parent_indices": torch.tensor(self._p, dtype=torch.long)}
+
+
+def test_tree_columns_read_any_tree_through_get_tree_data():
+    par, tok, prob, dep = tree_columns(_ForeignTree([-1, 0, 0, 1], [4, 5, 6, 7]))
+    assert par.dtype == np.int32 and par.tolist() == [-1, 0, 0, 1]
+    assert tok.tolist() == [4, 5, 6, 7] and prob.tolist() == [0.5] * 4 and dep.tolist() == [0, 1, 1, 2]
 
 
 def test_tree_errors():

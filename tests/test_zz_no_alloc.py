@@ -31,18 +31,23 @@ def _inputs(seed, n_trees, vocab):
     return x, dev(indptr), dev(par), dev(tok), dev(dp), trees
 
 
-def test_noalloc_matches_workspace_entry_point_on_two_calls():
+@pytest.mark.parametrize("top_p,do_sample", [(1.0, 0), (0.9, 0), (1.0, 1), (0.9, 1)])
+def test_noalloc_matches_workspace_entry_point_on_two_calls(top_p, do_sample):
+    """Plain traversal, the top-p target and the sampled bonus: the last three
+    run the statistics, nucleus, walk and bonus kernels on the shared array."""
     V = 128256
     x, ind, par, tok, dp, trees = _inputs(21, 6, V)
     B, R, N = len(trees), x.shape[0], max(t.size for t in trees)
-    ref_t, ref_h, ref_c = K.accept_traversal(x, ind, par, tok, dp, temperature=0.9, seed=77, offset=3, max_nodes=N)
+    ref_t, ref_h, ref_c = K.accept_traversal(x, ind, par, tok, dp, temperature=0.9, top_p=top_p,
+                                             do_sample=bool(do_sample), seed=77, offset=3, max_nodes=N)
     lib = _lib.lib()
     for _ in range(2):
         ot = torch.full((B, N), -5, dtype=torch.int32, device=DEV)
         oh = torch.full((B, N), -5, dtype=torch.int32, device=DEV)
         oc = torch.full((B, 4), -5, dtype=torch.int32, device=DEV)
         rc = lib.pts_accept_traversal_noalloc(x.data_ptr(), x.stride(0), ind.data_ptr(), par.data_ptr(),
-                                              tok.data_ptr(), dp.data_ptr(), B, R, V, N, -1, 0.9, 1.0, 0, 77, 3,
+                                              tok.data_ptr(), dp.data_ptr(), B, R, V, N, -1, 0.9, top_p, do_sample,
+                                              77, 3,
                                               ot.data_ptr(), oh.data_ptr(), oc.data_ptr(), N,
                                               torch.cuda.current_stream().cuda_stream)
         assert rc == 0, lib.pts_last_error().decode()
