@@ -57,6 +57,10 @@ constexpr float kEps32 = 1e-8f;
 constexpr double kEps = 1e-8;
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Pools with at most this many (layer, K/V, head) rows per token are
+// compacted by the walks themselves; larger ones by the compaction kernel.
+constexpr int kFusedCompactMaxRows = 32;
+
 struct RowStat {
   float m;
   float s;
@@ -2415,9 +2419,23 @@ static int set_compact(AcceptParams& p, const pts_kv_compact_args* c) {
                 "bad compaction shape");
   PTS_CHECK_ARG((c->head_dim * c->elem_bytes) % 16 == 0, "head_dim * elem_bytes must be a multiple of 16");
   PTS_CHECK_ARG(((uintptr_t)c->kv_pool & 15) == 0, "pool must be 16-byte aligned");
-  p.compact = 1;
+  // The walks copy their request's rows one warp at a time, which pays for
+  // pools of a few (layer, K/V, head) rows per token.  Larger pools (many
+  // layers) are compacted by the grid-wide compaction kernel right after the
+  // acceptance launch, in the same call.
+  p.compact = 2 * c->num_layers * c->num_kv_heads <= kFusedCompactMaxRows ? 1 : 0;
   p.cp = *c;
   return PTS_OK;
+}
+
+// After a successful acceptance launch: the compaction that set_compact left
+// to the grid-wide kernel, if any.
+static int finish_compact(int rc, const AcceptParams& p, const pts_kv_compact_args* c, cudaStream_t stream) {
+  if (rc != PTS_OK || !c || p.compact) return rc;
+  return pts_kv_compact(c->kv_pool, c->num_layers, c->max_pages, c->page_len, c->num_kv_heads, c->head_dim,
+                        c->elem_bytes, c->page_indptr, c->page_indices, p.out_hidden, p.out_stride, p.out_counts, 4,
+                        c->offsets, p.batch, min(p.out_stride, p.max_nodes), c->new_kv_len, c->new_last_page_len,
+                        (pts_stream_t)stream);
 }
 
 extern "C" int pts_accept_greedy(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
@@ -2453,7 +2471,8 @@ extern "C" int pts_accept_greedy_compact(const uint16_t* logits, int64_t row_str
   p.out_tokens = out_tokens;
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
-  return accept_launch(p, 0, 1.0f, workspace, workspace_bytes, (cudaStream_t)stream);
+  return finish_compact(accept_launch(p, 0, 1.0f, workspace, workspace_bytes, (cudaStream_t)stream), p, compact,
+                        (cudaStream_t)stream);
 }
 
 extern "C" int pts_accept_traversal(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
@@ -2498,8 +2517,11 @@ extern "C" int pts_accept_traversal_compact(const uint16_t* logits, int64_t row_
   p.out_tokens = out_tokens;
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
-  if (top_p >= 1.0f && !do_sample) return accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream);
-  return accept_traversal_extended(p, temperature, top_p, do_sample, workspace, workspace_bytes, (cudaStream_t)stream);
+  const int rc = (top_p >= 1.0f && !do_sample)
+                     ? accept_launch(p, 1, temperature, workspace, workspace_bytes, (cudaStream_t)stream)
+                     : accept_traversal_extended(p, temperature, top_p, do_sample, workspace, workspace_bytes,
+                                                 (cudaStream_t)stream);
+  return finish_compact(rc, p, compact, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
