@@ -76,9 +76,8 @@ def _grow_tree(tokens, probs):
                                    depth=1))
         tree.current_size += 1
     tree.available_leaves = [1, 2]
-    tree.add_nodes(torch.from_numpy(np.asarray(tokens[3:7]))[None, None],                 # tree.py:78-121
-                  torch.from_numpy(np.asarray(probs[3:7]))[None, None],
-                   torch.tensor([[[0, 0, 1, 1]]]))
+    tree.add_nodes(torch.from_numpy(np.asarray(tokens[3:7]))[None, None],            # tree.py:78-121
+                   torch.from_numpy(np.asarray(probs[3:7]))[None, None], torch.tensor([[[0, 0, 1, 1]]]))
     for i in range(7, 15):                                   # beam_search.py:570-579
         parent = 3 + (i - 7) // 2
         new_idx = tree.current_size
