@@ -147,6 +147,34 @@ __device__ __forceinline__ uint64_t block_visibility(const AttnParams& p, const 
   return v;
 }
 
+// block_visibility with the row's first two mask words held in registers
+// (trees of up to 128 rows); wider masks read the rest from memory.
+__device__ __forceinline__ uint64_t block_visibility_reg(const AttnParams& p, const uint64_t* mrow, uint64_t w0,
+                                                         uint64_t w1, int node, int kv0, int kv_len, int prefix) {
+  const int np = prefix - kv0;
+  if (np >= kBlockN) return ~0ull;
+  uint64_t v = np > 0 ? low_bits(np) : 0ull;
+  const int c0 = max(np, 0);
+  const int cend = min(kBlockN, kv_len - kv0);
+  if (c0 < cend) {
+    const int tn0 = kv0 + c0 - prefix;                           // tree slot of bit c0
+    uint64_t bits;
+    if (p.mask_bits == nullptr) {
+      bits = low_bits(max(0, min(64, node - tn0 + 1)));
+    } else {
+      const int w = tn0 >> 6, sh = tn0 & 63;
+      auto word = [&](int k) -> uint64_t {
+        if (k >= p.mask_words) return 0ull;
+        return k == 0 ? w0 : k == 1 ? w1 : __ldg(mrow + k);
+      };
+      const uint64_t lo = word(w), hi = word(w + 1);
+      bits = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;
+    }
+    v |= (bits & low_bits(cend - c0)) << c0;
+  }
+  return v;
+}
+
 // Byte offset of (row, 16-byte chunk) in a 128-byte-swizzled [rows x 64] tile.
 __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
@@ -202,7 +230,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   if (warp == 0) {
-    for (int i = lane; i < min(n_pages, kMaxSmemPages); i += 32) spages[i] = p.page_indices[p0 + i];
+    // eight independent loads per lane in flight
+    const int staged = min(n_pages, kMaxSmemPages);
+    for (int i0 = 0; i0 < staged; i0 += 256) {
+      int32_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        v[u] = i < staged ? __ldg(p.page_indices + p0 + i) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        if (i < staged) spages[i] = v[u];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -295,6 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = active_tile && (t * 128 + r_local) < tensor_rows;
     const int node = R / p.g, hh = R % p.g;
     const uint64_t* mrow = p.mask_bits ? p.mask_bits + (int64_t)(q0 + node) * p.mask_words : nullptr;
+    const uint64_t mw0 = (valid && mrow) ? __ldg(mrow) : 0ull;
+    const uint64_t mw1 = (valid && mrow && p.mask_words > 1) ? __ldg(mrow + 1) : 0ull;
     const uint32_t prow = smem_u32(smem + kOffP + 2 * t * kPBytes) + r_local * 128;   // this row of P_t, buffer 0
     const uint32_t pswz = (uint32_t)(r_local & 7);
     if (active_tile) {
@@ -350,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // visibility: whole block for prefix blocks, else per slot
       const int kv0 = j * kBlockN;
       if (!valid || kv0 + kBlockN > prefix) {
-        const uint64_t vis = valid ? block_visibility(p, mrow, node, kv0, kv_len, prefix) : 0ull;
+        const uint64_t vis = valid ? block_visibility_reg(p, mrow, mw0, mw1, node, kv0, kv_len, prefix) : 0ull;
 #pragma unroll
         for (int c = 0; c < kBlockN; ++c)
           if (!((vis >> c) & 1ull)) sr[c] = __float_as_uint(-INFINITY);
