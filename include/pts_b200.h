@@ -219,6 +219,39 @@ int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride,
                                  int32_t* out_hidden, int32_t* out_counts, int out_stride,
                                  pts_stream_t stream);
 
+/* ------------------------------------------------------------------ lm_head
+ * The target's lm_head over the tree rows, logits = hidden x weight^T
+ * (flashinfer/modeling_llama.py:104, `self.lm_head(hidden_states[...])`):
+ * hidden [num_rows, hidden_size] and weight [vocab, hidden_size] bf16, rows
+ * contiguous, hidden_size a multiple of 64; fp32 accumulation on the tensor
+ * cores, every logit rounded to bf16 as the model's bf16 output is.
+ *
+ * pts_lmhead_logits writes the bf16 logits [num_rows, logits_stride].
+ *
+ * pts_lmhead_accept runs the same GEMM without writing the logits: its
+ * epilogue reduces every 256-column tile of a row to the acceptance
+ * statistics (max, sum of exp(x - max), first index of the max; each node's
+ * token logit under its parent row; for rows whose max could tie under
+ * bf16 rounding, the tile's largest distinct values with their first
+ * indices), the tiles are merged per row, and the walks of pts_accept_greedy
+ * (traversal = 0) or pts_accept_traversal (traversal = 1, top-p 1, no bonus
+ * sampling; Philox stream as there) run from the merged statistics.  Same
+ * outputs as pts_lmhead_logits followed by the bf16 acceptance on those
+ * logits.  A request containing a row whose rounding tie the candidate lists
+ * cannot settle (more tied distinct values in one tile than it keeps, for
+ * example a near-constant row) gets out_counts[b*4] = -4: redo it from
+ * pts_lmhead_logits and the acceptance.  Workspace:
+ * pts_lmhead_workspace_size. */
+int pts_lmhead_logits(const void* hidden, const void* weight, int num_rows, int vocab, int hidden_size,
+                      void* logits, int64_t logits_stride, pts_stream_t stream);
+size_t pts_lmhead_workspace_size(int num_rows, int vocab);
+int pts_lmhead_accept(const void* hidden, const void* weight, int num_rows, int vocab, int hidden_size,
+                      const int32_t* row_indptr, const int32_t* parents, const int32_t* tokens,
+                      const float* draft_probs, int batch, int max_nodes, int64_t eos_token_id,
+                      int traversal, float temperature, uint64_t philox_seed, uint64_t philox_offset,
+                      int32_t* out_tokens, int32_t* out_hidden, int32_t* out_counts, int out_stride,
+                      void* workspace, size_t workspace_bytes, pts_stream_t stream);
+
 /* ------------------------------------------------------------- sparse page sets
  * Long-prefix requests restricted to a page subset per KV head.  The
  * reference selects important pages (q . k scores aggregated per page, top-k

@@ -50,6 +50,10 @@ SIGNATURES = {
                                                f32, f32, C.c_int, u64, u64, vp, vp, vp, C.c_int, vp]),
     "pts_accept_export_row_stats": (C.c_int, [vp, sz, vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, f32, vp, vp,
                                               vp]),
+    "pts_lmhead_logits": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, i64, vp]),
+    "pts_lmhead_workspace_size": (sz, [C.c_int, C.c_int]),
+    "pts_lmhead_accept": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, i64,
+                                    C.c_int, f32, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
     "pts_accept_shard_partials": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,
                                             vp, sz, vp]),
     "pts_accept_merge_shards": (C.c_int, [vp, vp, C.c_int, C.c_int, vp, vp, vp]),

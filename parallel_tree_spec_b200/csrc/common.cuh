@@ -1,6 +1,7 @@
 // Shared helpers for the B200 tree-verification kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -20,6 +21,11 @@ int current_context_id(unsigned long long* id);
 // preferred carveout to the maximum) in the current context.  Thread-safe;
 // the attribute call is made once per (context, kernel) and size.
 int ensure_smem_attr(const void* func, size_t bytes, bool max_carveout = false);
+
+// A bf16 TMA tensor map of `rank` dimensions with 128-byte swizzle (zero fill
+// out of bounds); dims innermost first, strides of dims 1.. in bytes.
+int encode_tiled_bf16_sw128(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims,
+                            const cuuint64_t* strides_bytes, const cuuint32_t* box);
 
 #define PTS_CHECK_ARG(cond, ...)                                  \
   do {                                                            \

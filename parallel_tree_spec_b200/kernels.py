@@ -192,6 +192,72 @@ def accept_row_stats(logits: torch.Tensor, row_indptr: torch.Tensor, parents: to
     return am, mb
 
 
+# ------------------------------------------------------------------ lm_head
+def _lmhead_args(hidden: torch.Tensor, weight: torch.Tensor):
+    dev = _need_cuda(hidden, weight)
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("hidden and weight must be bf16")
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden [rows, H] and weight [vocab, H] with the same H")
+    return dev, hidden.contiguous(), weight.contiguous()
+
+
+def lmhead_logits(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """bf16 logits [rows, vocab] = hidden x weight^T on the tensor cores."""
+    dev, hidden, weight = _lmhead_args(hidden, weight)
+    R, H = hidden.shape
+    V = weight.shape[0]
+    out = torch.empty(R, V, dtype=torch.bfloat16, device=dev)
+    _lib.call("pts_lmhead_logits", hidden.data_ptr(), weight.data_ptr(), R, V, H, out.data_ptr(), out.stride(0),
+              _stream(dev))
+    return out
+
+
+def lmhead_accept(hidden: torch.Tensor, weight: torch.Tensor, row_indptr: torch.Tensor, parents: torch.Tensor,
+                  tokens: torch.Tensor, draft_probs: Optional[torch.Tensor] = None, method: str = "exact",
+                  eos_token_id: Optional[int] = None, temperature: float = 1.0, seed: int = 0, offset: int = 0,
+                  max_nodes: Optional[int] = None, fallback: bool = True):
+    """Acceptance straight from the hidden states: the lm_head GEMM with the
+    acceptance statistics in its epilogue (no logits in memory), then the
+    walks.  Returns (tokens, hidden, counts) like accept_greedy /
+    accept_traversal.  With ``fallback`` a request whose rounding tie could
+    not be settled from the statistics (counts = -4) is redone from
+    materialised logits."""
+    dev, hidden, weight = _lmhead_args(hidden, weight)
+    row_indptr, parents, tokens = _i32(row_indptr, "indptr"), _i32(parents, "parents"), _i32(tokens, "tokens")
+    _need_cuda(hidden, row_indptr, parents, tokens)
+    if method not in ("exact", "traversal"):
+        raise ValueError(f"Unknown verification method: {method!r} (expected 'traversal' or 'exact')")
+    trav = method == "traversal"
+    if trav:
+        if draft_probs is None:
+            raise ValueError("traversal needs draft_probs")
+        draft_probs = draft_probs.to(torch.float32).contiguous()
+    R, H = hidden.shape
+    V = weight.shape[0]
+    B = row_indptr.numel() - 1
+    mn = min(int(max_nodes) if max_nodes is not None else R, _lib.PTS_MAX_TREE_NODES)
+    ot = torch.empty(B, mn, dtype=torch.int32, device=dev)
+    oh = torch.empty(B, mn, dtype=torch.int32, device=dev)
+    oc = torch.empty(B, 4, dtype=torch.int32, device=dev)
+    ws = workspace(dev, "lmhead", _lib.lib().pts_lmhead_workspace_size(R, V))
+    _lib.call("pts_lmhead_accept", hidden.data_ptr(), weight.data_ptr(), R, V, H, row_indptr.data_ptr(),
+              parents.data_ptr(), tokens.data_ptr(), draft_probs.data_ptr() if trav else None, B, mn,
+              -1 if eos_token_id is None else int(eos_token_id), 1 if trav else 0, float(temperature),
+              int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), ot.data_ptr(), oh.data_ptr(), oc.data_ptr(),
+              ot.shape[1], ws.data_ptr(), ws.numel(), _stream(dev))
+    if fallback and bool((oc[:, 0] == -4).any()):
+        x = lmhead_logits(hidden, weight)
+        if trav:
+            rt, rh, rc = accept_traversal(x, row_indptr, parents, tokens, draft_probs, eos_token_id=eos_token_id,
+                                          temperature=temperature, seed=seed, offset=offset, max_nodes=mn)
+        else:
+            rt, rh, rc = accept_greedy(x, row_indptr, parents, tokens, eos_token_id=eos_token_id, max_nodes=mn)
+        redo = oc[:, 0] == -4
+        ot[redo], oh[redo], oc[redo] = rt[redo], rh[redo], rc[redo]
+    return ot, oh, oc
+
+
 def accept_shard_partials(logits_shard: torch.Tensor, vocab_offset: int, row_indptr: torch.Tensor,
                           parents: torch.Tensor, tokens: torch.Tensor, temperature: float = 1.0):
     """Step 1 of the sharded acceptance: ``logits_shard`` [rows, Vs] bf16 is
