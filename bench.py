@@ -581,6 +581,8 @@ def run_b200(a):
         sub["traversal_top_p_0.9"] = mode_record(a, W, device, "traversal", 0.9, sub_steps, peak)
         if world == 1:
             sub["config3_path"] = config3_record(a, device, sub_steps, peak)
+            sub["lmhead"] = lmhead_record(a, device, 10, tpeak)
+            sub["config4_sparse"] = sparse_record(a, device, sub_steps, peak)
         else:
             sub["tp"] = tp_record(a, world, rank, device, sub_steps)
             sub["strong"] = strong_record(a, world, rank, device, sub_steps)
@@ -879,6 +881,77 @@ def config3_record(a, dev, steps, peak):
             "accept_len_mean": float(oc[:, 2].float().mean().item())}
 
 
+def lmhead_record(a, dev, steps, tpeak):
+    """The lm_head of the benchmark step's 16 x 65 tree rows (hidden 4096,
+    vocabulary 128256, bf16, random weights) followed by traversal acceptance
+    at T=1.0, three ways: torch.matmul (cuBLAS) writing the logits + the
+    acceptance kernel; this library's tcgen05 GEMM writing the logits + the
+    acceptance kernel; the same GEMM with the acceptance statistics in its
+    epilogue (no logits in memory) + the walks (pts_lmhead_accept)."""
+    import torch
+    from parallel_tree_spec_b200 import kernels as K
+    from parallel_tree_spec_b200 import workload as wl
+
+    B, H, V = a.batch, 4096, a.vocab
+    rng = np.random.default_rng(a.seed + 41)
+    trees = [wl.make_tree(rng, a.width, a.depth, V) for _ in range(B)]
+    n = trees[0].size
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    d = lambda v: torch.as_tensor(np.ascontiguousarray(v), device=dev)
+    ind, par, tok, dp = d(indptr), d(par), d(tok), d(dp)
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 43)
+    hidden = torch.randn(B * n, H, generator=g, device=dev).to(torch.bfloat16)
+    weight = (torch.randn(V, H, generator=g, device=dev) * (3.0 / H ** 0.5)).to(torch.bfloat16)
+    flops = 2.0 * B * n * V * H
+
+    def cublas(ev=None):
+        x = torch.matmul(hidden, weight.t())
+        if ev is not None:
+            ev[0].record()
+        K.accept_traversal(x, ind, par, tok, dp, seed=5, offset=0, max_nodes=n)
+
+    def unfused(ev=None):
+        x = K.lmhead_logits(hidden, weight)
+        if ev is not None:
+            ev[0].record()
+        K.accept_traversal(x, ind, par, tok, dp, seed=5, offset=0, max_nodes=n)
+
+    def fused(ev=None):
+        K.lmhead_accept(hidden, weight, ind, par, tok, dp, method="traversal", seed=5, offset=0, max_nodes=n,
+                        fallback=False)
+        if ev is not None:
+            ev[0].record()
+
+    out = {"workload": f"lm_head of {B} x {n} tree rows (hidden {H}, vocabulary {V}, bf16) + traversal "
+                       f"acceptance T=1.0", "flops": flops, "unit": "us"}
+    for name, fn in (("cublas_gemm_then_accept", cublas), ("gemm_then_accept", unfused),
+                     ("fused_gemm_statistics", fused)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        starts = []
+        for _ in range(steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            em = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn([em])
+            e1.record()
+            starts.append((e0, em, e1))
+        torch.cuda.synchronize()
+        total = statistics.mean(e0.elapsed_time(e1) for e0, em, e1 in starts) * 1e3
+        gemm = statistics.mean(e0.elapsed_time(em) for e0, em, e1 in starts) * 1e3
+        rec = {"total_us": total}
+        if name != "fused_gemm_statistics":
+            rec["gemm_us"] = gemm
+            rec["accept_us"] = total - gemm
+        rec["tensor_frac_of_total"] = flops / (total * 1e-6) / 1e12 / tpeak
+        out[name] = rec
+    out["tensor_peak_tflops"] = tpeak
+    return out
+
+
 def strong_record(a, world, rank, dev, steps):
     """Strong scaling of the batch-sharded step: the 16 requests of the
     benchmark workload split over the ranks (16/N each).  At N >= 4 a rank's KV
@@ -943,7 +1016,7 @@ def run_tp(a):
 
 
 # ---------------------------------------------------------------- long-context sparse step
-def run_sparse(a):
+def sparse_record(a, dev, steps, peak):
     """Long-context verification step: 8 requests with 32768-token prefixes
     and 129-row trees (width 16, depth 8), Hq=32 / Hkv=8.  The per-KV-head
     page sets (first 4 + 64 highest root-query . key-sum scores + last 8
@@ -956,9 +1029,6 @@ def run_sparse(a):
     from parallel_tree_spec_b200 import workload as wl
     from parallel_tree_spec_b200._lib import check
 
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     L = _lib.lib()
     B, P, Hq, Hkv, D, pl, V = 8, 32768, 32, 8, 128, 16, a.vocab
     rng = np.random.default_rng(a.seed + 11)
@@ -1028,39 +1098,44 @@ def run_sparse(a):
         if ev is not None:
             ev[2].record()
 
-    for _ in range(max(3, a.warmup)):
+    for _ in range(3):
         one()
-    torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(a.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local).start()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    start.record()
-    for i in range(a.steps):
-        one(evs[i])
-    end.record()
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    sampler.stop()
-    el = start.elapsed_time(end)
+    el, evs = time_steps(one, steps)
     attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
     acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
     groups = (n * (Hq // Hkv) + 263) // 264
     kv_bytes = B * Hkv * groups * sel_pages * pl * D * 2 * 2
-    rec = {
-        "metric": "tree-verify steps/s, long-context sparse (per-KV-head page sets)",
-        "value": a.steps / (el / 1e3), "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": el / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": f"long-context sparse tree-verify step: B={B} requests, prefix {P}, tree rows {n} "
-                               f"(width 16, depth 8), Hq={Hq}, Hkv={Hkv}, D=128, page 16, {sel_pages} pages per KV "
-                               f"head (4 first + 64 top + 8 last + tree pages), vocab {V}, greedy, one layer"},
-        "tokens_per_s": a.steps / (el / 1e3) * B * n,
-        "kernels_us": {"tree_attn_head_pages": attn, "accept": acc, "select_once": select_us},
-        "attention_kv_gbs": kv_bytes / (attn * 1e-6) / 1e9,
-        "clocks": sampler.summary(t0, t1),
+    return {
+        "workload": f"long-context sparse tree-verify step: B={B} requests, prefix {P}, tree rows {n} (width 16, "
+                    f"depth 8), Hq={Hq}, Hkv={Hkv}, D=128, page 16, {sel_pages} pages per KV head (4 first + 64 top + "
+                    f"8 last + tree pages), vocab {V}, greedy with compaction, one layer",
+        "value": steps / (el / 1e3), "unit": UNIT, "steps": steps, "ms_per_step": el / steps,
+        "tokens_per_s": steps / (el / 1e3) * B * n,
+        "kernels_us": {"tree_attn_head_pages": attn, "accept_with_compaction": acc, "select_once": select_us},
+        "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s",
+                     "attention_kv_gbs": kv_bytes / (attn * 1e-6) / 1e9,
+                     "attention_frac": kv_bytes / (attn * 1e-6) / 1e9 / peak,
+                     "accept_frac": T * V * 2 / (acc * 1e-6) / 1e9 / peak},
     }
+
+
+def run_sparse(a):
+    """``--sparse``: the long-context step alone, one JSON line."""
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peak, _ = measured_peaks()
+    sampler = ClockSampler(local).start()
+    t0 = time.perf_counter()
+    r = sparse_record(a, dev, a.steps, peak)
+    t1 = time.perf_counter()
+    sampler.stop()
+    rec = {"metric": "tree-verify steps/s, long-context sparse (per-KV-head page sets)", "value": r["value"],
+           "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": r["ms_per_step"],
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded)", "config": {"workload": r["workload"]}, "tokens_per_s": r["tokens_per_s"],
+           "kernels_us": r["kernels_us"], "roofline": r["roofline"], "clocks": sampler.summary(t0, t1)}
     print(json.dumps(rec), flush=True)
     return 0
 

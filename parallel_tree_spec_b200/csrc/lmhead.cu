@@ -12,10 +12,12 @@
 //   warp 1     MMA issuer (M=128 N=256 K=16 per instruction, A and B from shared
 //              memory) into one of two TMEM accumulators (256 columns each), so
 //              the epilogue of tile i overlaps the main loop of tile i+1;
-//   warps 2-5  epilogue, one thread per row: every accumulator is rounded to
-//              bf16 first (the value the model's bf16 logits would hold), then
-//              scaled by 1/T and rounded again as the acceptance scales logits.
-// Statistics mode writes per (row, vocabulary tile): the partial (sum of
+//   warps 2-9  epilogue, two threads per row (warps 2-5 the first 128 columns of
+//              the tile, warps 6-9 the other 128): every accumulator is rounded
+//              to bf16 first (the value the model's bf16 logits would hold),
+//              then scaled by 1/T and rounded again as the acceptance scales
+//              logits.
+// Statistics mode writes per (row, 128-column half tile): the partial (sum of
 // exp(x - m_t) in fp64, m_t, first index of m_t) in the acceptance kernel's
 // format; the node token logits (each node's token under its parent row, from
 // the one tile holding the token); and, for tiles whose max could take part in
@@ -40,7 +42,9 @@ namespace {
 using namespace sm100;
 
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kThreads = 192;                          // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kThreads = 320;                          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kSub = 128;                              // columns of a tile one epilogue thread reduces
 constexpr uint32_t kABytes = kBM * kBK * 2;            // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;            // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -81,13 +85,14 @@ struct __align__(8) LmBars {
 struct LmParams {
   int M, V, K;
   int m_tiles, n_tiles, tiles, k_blocks;
+  int n_sub;                   // 128-column partials per row (two per tile)
   int mode;                    // 0 statistics, 1 logits
   int use_temp;
   float inv_temp;
   uint16_t* logits;            // mode 1: [M, logits_stride] bf16
   int64_t logits_stride;
-  LmPart* parts;               // mode 0: [M][n_tiles]
-  Cand* cands;                 // mode 0: [M][n_tiles][kCand]
+  LmPart* parts;               // mode 0: [M][n_sub]
+  Cand* cands;                 // mode 0: [M][n_sub][kCand]
   const int32_t* child_ptr;    // [M+1]: row r's children, sorted by token
   const int32_t* child_tok;
   const int32_t* child_node;
@@ -95,9 +100,15 @@ struct LmParams {
   int* err;
 };
 
+// Round-to-nearest-even to bf16 for the finite accumulators (no NaN path).
+__device__ __forceinline__ float rne_bf16(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return __uint_as_float((u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u);
+}
+
 __device__ __forceinline__ float scaled_logit(const LmParams& p, float acc) {
-  float x = round_to_bf16(acc);
-  if (p.use_temp) x = round_to_bf16(__fmul_rn(x, p.inv_temp));
+  float x = rne_bf16(acc);
+  if (p.use_temp) x = rne_bf16(__fmul_rn(x, p.inv_temp));
   return x;
 }
 
@@ -122,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars.acc_full[b], 1);
-      mbar_init(&bars.acc_empty[b], 4);
+      mbar_init(&bars.acc_empty[b], kEpiWarps);
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
@@ -207,8 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     mbar_wait(&bars.drain, 0);
   } else {
-    // ------------------------------------------------------------ epilogue: one thread per row
+    // ------------------------------------------------------------ epilogue: two threads per row
     const int quarter = warp & 3;                        // TMEM lanes 32q .. 32q+31
+    const int sub = (warp - 2) >> 2;                     // this thread's 128 columns of a tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++i) {
@@ -226,13 +238,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mt * kBM + quarter * 32 + lane;
       const bool valid = row < p.M;
-      const int n0 = nt * kBN;
-      const int ncols = min(kBN, p.V - n0);
-      const uint32_t acc = tmem + lane_base + 256 * buf;
+      const int n0 = nt * kBN + sub * kSub;              // first column of this thread's half tile
+      const int ncols = max(0, min(kSub, p.V - n0));
+      const uint32_t acc = tmem + lane_base + 256 * buf + sub * kSub;
       if (p.mode == 1) {
         // logits: bf16 of every accumulator
         uint16_t* out = p.logits + (int64_t)row * p.logits_stride + n0;
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < kSub / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(acc + 32 * c, r);
           tmem_ld_wait();
@@ -255,21 +267,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        // pass 1: the tile's max of the scaled bf16 logits and its first index
+        // pass 1: the half tile's max of the scaled bf16 logits and its first index
         float m_t = -INFINITY;
         int i_t = INT_MAX;
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < kSub / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(acc + 32 * c, r);
           tmem_ld_wait();
+          // four interleaved (max, first index) chains, merged in index order
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          int ix[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX};
 #pragma unroll
           for (int v = 0; v < 32; ++v) {
             const float x = scaled_logit(p, __uint_as_float(r[v]));
-            if (32 * c + v < ncols && x > m_t) {
-              m_t = x;
-              i_t = n0 + 32 * c + v;
+            if (32 * c + v < ncols && x > mx[v & 3]) {
+              mx[v & 3] = x;
+              ix[v & 3] = n0 + 32 * c + v;
             }
           }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (mx[k] > m_t || (mx[k] == m_t && ix[k] < i_t)) {
+              m_t = mx[k];
+              i_t = ix[k];
+            }
         }
         // pass 2: the sum of exp(x - m_t), the children's token logits and the
         // candidate values of the rounding-tie rule
@@ -281,13 +302,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ce = valid ? p.child_ptr[row + 1] : 0;
         while (cp < ce && p.child_tok[cp] < n0) ++cp;
         int next_tok = cp < ce ? p.child_tok[cp] : INT_MAX;
+        const int last_col = n0 + ncols;                 // children at or past it belong to another half tile
         const float mlog = (m_t == -INFINITY) ? 0.0f : m_t * kLog2e;
         double s_t = 0.0;
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < kSub / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(acc + 32 * c, r);
           tmem_ld_wait();
           float q0 = 0.0f, q1 = 0.0f, q2 = 0.0f, q3 = 0.0f;
+          const bool tok_here = next_tok < n0 + 32 * c + 32 && next_tok < last_col;
+          const bool cand_here = keep;
 #pragma unroll
           for (int v = 0; v < 32; ++v) {
             const int col = 32 * c + v;
@@ -298,14 +322,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             else if ((v & 3) == 1) q1 += e;
             else if ((v & 3) == 2) q2 += e;
             else q3 += e;
-            if (in && n0 + col == next_tok) {
+            if (tok_here && in && n0 + col == next_tok) {
               do {
                 p.tok_logit[p.child_node[cp]] = x;
                 ++cp;
                 next_tok = cp < ce ? p.child_tok[cp] : INT_MAX;
               } while (n0 + col == next_tok);
             }
-            if (keep && in && x > cl[kCand - 1].v) {
+            if (cand_here && in && x > cl[kCand - 1].v) {
               // insert a new distinct value (a repeat keeps its first index)
               bool present = false;
 #pragma unroll
@@ -326,13 +350,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           s_t += (double)((q0 + q1) + (q2 + q3));
         }
         if (valid) {
+          const int slot = nt * 2 + sub;
           LmPart part;
           part.s = (m_t == -INFINITY) ? 0.0 : s_t;
           part.m = m_t;
           part.idx = i_t;
-          p.parts[(int64_t)row * p.n_tiles + nt] = part;
+          p.parts[(int64_t)row * p.n_sub + slot] = part;
           if (keep) {
-            Cand* dst = p.cands + ((int64_t)row * p.n_tiles + nt) * kCand;
+            Cand* dst = p.cands + ((int64_t)row * p.n_sub + slot) * kCand;
 #pragma unroll
             for (int k = 0; k < kCand; ++k) dst[k] = cl[k];
           }
@@ -441,9 +466,9 @@ __device__ __forceinline__ float prev_bf16(float x) {
 __global__ void lmhead_merge_kernel(const LmParams p, RowStatOut* out, int* unresolved) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (row >= p.M) return;
-  const LmPart* parts = p.parts + (int64_t)row * p.n_tiles;
-  const int per = (p.n_tiles + 31) / 32;
-  const int t0 = lane * per, t1 = min(p.n_tiles, t0 + per);
+  const LmPart* parts = p.parts + (int64_t)row * p.n_sub;
+  const int per = (p.n_sub + 31) / 32;
+  const int t0 = lane * per, t1 = min(p.n_sub, t0 + per);
   LmPart acc{0.0, -INFINITY, INT_MAX};
   for (int t = t0; t < t1; ++t) acc = merge_part(acc, parts[t]);
   // lanes in order: lane 0 takes lane 1's run, then lane 2's ...
@@ -468,7 +493,7 @@ __global__ void lmhead_merge_kernel(const LmParams p, RowStatOut* out, int* unre
       // a tile whose max is <= -4 holds no value that can tie; one whose max
       // is >= 4 cannot belong to a tied row (ties need |m| < 2)
       if (!(parts[t].m > -kCandRange && parts[t].m < kCandRange)) continue;
-      const Cand* cl = p.cands + ((int64_t)row * p.n_tiles + t) * kCand;
+      const Cand* cl = p.cands + ((int64_t)row * p.n_sub + t) * kCand;
       bool full = true;
       float last = INFINITY;
       for (int k = 0; k < kCand; ++k) {
@@ -505,12 +530,12 @@ __global__ void mark_unresolved_kernel(const int32_t* row_indptr, const int* unr
 
 size_t lm_ws_layout(int M, int V, size_t* off_parts, size_t* off_cands, size_t* off_child, size_t* off_stats,
                     size_t* off_tok, size_t* off_unres) {
-  const int n_tiles = (V + kBN - 1) / kBN;
+  const int n_sub = 2 * ((V + kBN - 1) / kBN);
   size_t o = 0;
   *off_parts = o;
-  o = align_up(o + (size_t)M * n_tiles * sizeof(LmPart), 256);
+  o = align_up(o + (size_t)M * n_sub * sizeof(LmPart), 256);
   *off_cands = o;
-  o = align_up(o + (size_t)M * n_tiles * kCand * sizeof(Cand), 256);
+  o = align_up(o + (size_t)M * n_sub * kCand * sizeof(Cand), 256);
   *off_child = o;                                        // child_ptr [M+1], child_tok [M], child_node [M]
   o = align_up(o + (size_t)(3 * M + 1) * sizeof(int32_t), 256);
   *off_stats = o;
@@ -557,6 +582,7 @@ int lmhead_launch(const void* hidden, const void* weight, int M, int V, int K, L
   p.K = K;
   p.m_tiles = (M + kBM - 1) / kBM;
   p.n_tiles = (V + kBN - 1) / kBN;
+  p.n_sub = 2 * p.n_tiles;
   p.tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = K / kBK;
   if (int rc = ensure_smem_attr((const void*)lmhead_kernel, kSmemBytes)) return rc;
