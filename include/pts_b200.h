@@ -43,6 +43,16 @@ typedef struct CUstream_st* pts_stream_t; /* cudaStream_t */
 const char* pts_last_error(void);
 int pts_version(void);
 
+/* Failure handling (no counterpart in the reference).  Every wait of this
+ * library's kernels on other warps, other CTAs or in-flight copies is bounded:
+ * after the limit (SM clock cycles, default 4e9, about 2 s at the top clock)
+ * the kernel records an error, drains its own tensor-core work and copies,
+ * frees its TMEM and returns, so the CUDA context stays usable.
+ * pts_set_wait_limit sets the limit for launches made after it, process-wide
+ * (cycles <= 0 restores the default), and returns the previous limit; a small
+ * limit makes waits run out on purpose, to test the error paths. */
+long long pts_set_wait_limit(long long cycles);
+
 /* ------------------------------------------------------------------ acceptance
  * Fused acceptance: one pass over the bf16 logits computes, per row, the max,
  * the fp32 sum of exp(x - max), and the argmax of the bf16-rounded softmax
@@ -402,6 +412,11 @@ int pts_tree_mask_from_bool(const uint8_t* mask, const int32_t* qo_indptr, const
  * 131-144, 250-252).  head_dim 128, page_len 16, Hq/Hkv = 4 in this build. */
 size_t pts_tree_attn_workspace_size(int batch, int total_q, int num_qo_heads, int head_dim,
                                     int max_kv_len);
+/* The error word pts_tree_attn_run* leave in `workspace` when a CTA gave up
+ * waiting (0: none; nonzero: which wait).  Synchronises the stream, copies the
+ * word to *status and clears it in the workspace. */
+int pts_tree_attn_check(void* workspace, int* status, pts_stream_t stream);
+
 int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_indptr,
                       const int32_t* page_indptr, const int32_t* page_indices,
                       const int32_t* last_page_len, const uint64_t* mask_bits, int mask_words,

@@ -37,6 +37,8 @@ class KvCompactArgs(C.Structure):
 SIGNATURES = {
     "pts_last_error": (C.c_char_p, []),
     "pts_version": (C.c_int, []),
+    "pts_set_wait_limit": (C.c_longlong, [C.c_longlong]),
+    "pts_tree_attn_check": (C.c_int, [vp, vp, vp]),
     "pts_accept_workspace_size": (sz, [C.c_int, C.c_int]),
     "pts_accept_greedy": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, vp, vp, vp,
                                     C.c_int, vp, sz, vp]),

@@ -100,6 +100,7 @@ struct AttnParams {
   int max_pages;
   float scale_log2;
   int* err;
+  long long wait_limit;    // SM clocks a progress wait may take before the CTA gives up
 };
 
 __device__ __forceinline__ void record_abort(Bars& bars, const AttnParams& p, int code) {
@@ -273,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }                                                                                                       \
     __syncwarp();                                                                                           \
   } while (0)
-      bool ok = mbar_wait(&bars.q_ready, 0) && mbar_wait(&bars.kv_full[0], 0);
+      bool ok = mbar_wait(&bars.q_ready, 0, p.wait_limit) && mbar_wait(&bars.kv_full[0], 0, p.wait_limit);
       if (!ok && lane == 0) record_abort(bars, p, 21);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
@@ -288,8 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s1 = (ss + 1) % kStages;
           if (j + 1 < n_blocks) {
             // scores of block j+1 once K(j+1) is staged and S_t(j) has been read
-            const bool w_ok = mbar_wait(&bars.kv_full[s1], ((j + 1) / kStages) & 1) &&
-                              mbar_wait(&bars.s_free[t], j & 1) && !aborted(bars);
+            const bool w_ok = mbar_wait(&bars.kv_full[s1], ((j + 1) / kStages) & 1, p.wait_limit) &&
+                              mbar_wait(&bars.s_free[t], j & 1, p.wait_limit) && !aborted(bars);
             if (!__all_sync(0xffffffffu, w_ok)) {
               if (lane == 0) record_abort(bars, p, 23);
               ok = false;
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             PTS_QK(s1);
           }
-          const bool w_ok = mbar_wait(&bars.p_full[t], j & 1) && !aborted(bars);
+          const bool w_ok = mbar_wait(&bars.p_full[t], j & 1, p.wait_limit) && !aborted(bars);
           if (!__all_sync(0xffffffffu, w_ok)) {
             if (lane == 0) record_abort(bars, p, 24);
             ok = false;
@@ -374,9 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n_blocks && (ok || turns); ++j) {
       const bool wait_turn = turns && (t == 1 || j > 0);
       const bool pass_turn = turns && !(t == 1 && j == n_blocks - 1);
-      if (ok && aborted(bars)) ok = false;
+      // warp-uniform decisions only: the warp's later steps are collectives
+      if (ok && __any_sync(0xffffffffu, aborted(bars))) ok = false;
       if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars.s_full[t], j & 1));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars.s_full[t], j & 1, p.wait_limit));
         if (!ok) record_abort(bars, p, 31);
       }
       if (!ok) {                                        // the turns only
@@ -447,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O_t may be rescaled once its last update, PV_t(j-1), has completed
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars.p_empty[t][(j - 1) & 1], ((j - 1) >> 1) & 1));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars.p_empty[t][(j - 1) & 1], ((j - 1) >> 1) & 1, p.wait_limit));
         if (!ok) {
           record_abort(bars, p, 35);
           continue;
@@ -469,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bars.p_full[t]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && mbar_wait(&bars.o_full[t], 0)) {
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars.o_full[t], 0, p.wait_limit))) {
       tc_fence_after();
       const float inv = (valid && l_sum > 0.0f) ? 1.0f / l_sum : 0.0f;
       uint16_t* orow = p.out + ((int64_t)(q0 + node) * p.Hq + h * p.g + hh) * kD;
@@ -504,7 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int mi = lane >> 3, rr = lane & 7;               // ldmatrix: matrix / row supplied by this lane
     auto produce = [&](int blk) -> bool {
       const int s = blk % kStages;
-      const bool w_ok = mbar_wait_lazy(&bars.kv_empty[s], ((blk / kStages) + 1) & 1, 200) && !aborted(bars);
+      const bool w_ok =
+          mbar_wait_lazy(&bars.kv_empty[s], ((blk / kStages) + 1) & 1, 200, p.wait_limit) && !aborted(bars);
       if (!__all_sync(0xffffffffu, w_ok)) return false;
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars.kv_full[s], kStageBytes / kSyncWarps);
@@ -565,10 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!rem) continue;
       const int s = j % kStages;
-      if (!mbar_wait(&bars.kv_full[s], (j / kStages) & 1) || aborted(bars)) {
-        ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars.kv_full[s], (j / kStages) & 1, p.wait_limit) && !aborted(bars));
+      if (!ok) break;
       const uint32_t kb = kv_s + s * kStageBytes, vb = kb + 2 * kKvHalf;
       // S^T (16 tokens x 8 rows), two accumulation chains
       float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -749,6 +750,15 @@ using namespace pts;
 
 extern "C" size_t pts_tree_attn_workspace_size(int, int, int, int, int) { return 256; }
 
+extern "C" int pts_tree_attn_check(void* workspace, int* status, pts_stream_t stream) {
+  PTS_CHECK_ARG(workspace && status, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  PTS_CUDA_TRY(cudaMemcpyAsync(status, workspace, sizeof(int), cudaMemcpyDeviceToHost, st));
+  PTS_CUDA_TRY(cudaStreamSynchronize(st));
+  if (*status != 0) PTS_CUDA_TRY(cudaMemsetAsync(workspace, 0, sizeof(int), st));
+  return PTS_OK;
+}
+
 static int tree_attn_launch(const void* q, const void* kv_layer, const int32_t* qo_indptr,
                             const int32_t* page_indptr, const int32_t* page_indices, const int32_t* last_page_len,
                             const uint64_t* mask_bits, int mask_words, void* out, int batch, int total_q,
@@ -799,6 +809,7 @@ static int tree_attn_launch(const void* q, const void* kv_layer, const int32_t* 
   p.max_pages = max_pages;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.err = (int*)workspace;
+  p.wait_limit = wait_limit_cycles();
   if (int rc = ensure_smem_attr((const void*)tree_attn_kernel, kSmemBytes)) return rc;
   const int groups = (max_qo_len * g + kGroupRows - 1) / kGroupRows;
   if (groups > 65535) return set_error(PTS_ERR_CAPACITY, "%d query rows per request is too many", max_qo_len);

@@ -13,6 +13,11 @@ namespace pts {
 // Records a message for pts_last_error() and returns the code.
 int set_error(int code, const char* fmt, ...);
 
+// SM clocks a kernel's progress waits (on other warps, other CTAs or copies)
+// may take before the kernel gives up and reports an error; set process-wide
+// with pts_set_wait_limit.
+long long wait_limit_cycles();
+
 // The unique id of the current CUDA context (cuCtxGetId); PTS_ERR_CUDA when
 // there is none.
 int current_context_id(unsigned long long* id);

@@ -4,6 +4,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -13,6 +14,11 @@
 namespace pts {
 
 static thread_local char g_last_error[512] = "";
+
+constexpr long long kDefaultWaitLimit = 4000000000ll;     // SM clocks, about 2 s at the top clock
+static std::atomic<long long> g_wait_limit{kDefaultWaitLimit};
+
+long long wait_limit_cycles() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -96,3 +102,8 @@ int encode_tiled_bf16_sw128(CUtensorMap* map, int rank, const void* base, const 
 extern "C" const char* pts_last_error(void) { return pts::g_last_error; }
 
 extern "C" int pts_version(void) { return 1; }
+
+extern "C" long long pts_set_wait_limit(long long cycles) {
+  const long long v = cycles > 0 ? cycles : pts::kDefaultWaitLimit;
+  return pts::g_wait_limit.exchange(v);
+}

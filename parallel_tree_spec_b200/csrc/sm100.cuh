@@ -74,9 +74,11 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           long long timeout_cycles = 4000000000ll) {
   if (mbar_try_wait(bar, parity)) return true;
+  // the suspend hint (ns) stays well below the limit, so a short limit runs out
+  const uint32_t hint = timeout_cycles >= 200000000ll ? 100000u : (uint32_t)max(timeout_cycles / 4, 1ll);
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
     if (clock64() - t0 > timeout_cycles) return false;
   }
 }

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -594,7 +595,31 @@ def tree_attention(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr: torch.Ten
               mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T,
               int(max_qo_len), int(max_kv_len), Hq, Hkv, D, pl, P, scale, q.element_size(), ws.data_ptr(),
               ws.numel(), _stream(dev))
+    if _CHECK_ATTENTION:
+        check_attention(dev)
     return out
+
+
+# PTS_B200_CHECK=1: read the attention kernels' error word after every call
+# (synchronises the stream; for debugging).
+_CHECK_ATTENTION = os.environ.get("PTS_B200_CHECK", "0") not in ("", "0")
+
+
+def check_attention(device: Optional[torch.device] = None) -> None:
+    """Raise if an attention launch on the current stream gave up waiting
+    (pts_tree_attn_check: synchronises the stream, then clears the error)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    ws = workspace(dev, "attn", 256)
+    status = C.c_int(0)
+    _lib.call("pts_tree_attn_check", ws.data_ptr(), C.addressof(status), _stream(dev))
+    if status.value != 0:
+        raise RuntimeError(f"tree attention gave up waiting (error {status.value}); its output is not valid")
+
+
+def set_wait_limit(cycles: int) -> int:
+    """Process-wide limit (SM clocks) on the kernels' waits; <= 0 restores the
+    default.  Returns the previous limit."""
+    return int(_lib.lib().pts_set_wait_limit(int(cycles)))
 
 
 # ------------------------------------------------------------ sparse page sets

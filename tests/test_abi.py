@@ -54,3 +54,14 @@ def test_every_entry_rejects_null_pointers_on_the_host():
         assert rc == _lib.PTS_ERR_INVALID, (name, rc, lib.pts_last_error())
         checked += 1
     assert checked >= 20
+
+
+def test_wait_limit_setting_round_trips():
+    """pts_set_wait_limit returns the previous limit; <= 0 restores the default
+    (host-side only, no launch)."""
+    lib = _lib.lib()
+    default = lib.pts_set_wait_limit(0)
+    assert default > 10 ** 8
+    assert lib.pts_set_wait_limit(5000) == default
+    assert lib.pts_set_wait_limit(-1) == 5000
+    assert lib.pts_set_wait_limit(0) == default

@@ -148,3 +148,16 @@ def test_reference_error_types():
         ver.verify_tree_traversal(t, x)
     with pytest.raises(ValueError):
         ver.verify_tree_exact(t, x, root_ind=1)
+
+
+def test_acceptance_timeout_and_malformed_counts_map_to_exceptions():
+    """A walk that gave up waiting for its rows reports count -3 and a
+    malformed tree -1; the host turns them into RuntimeError / ValueError."""
+    ot = torch.zeros(2, 4, dtype=torch.int32)
+    oh = torch.zeros(2, 4, dtype=torch.int32)
+    oc = torch.tensor([[1, 1, 0, 0], [-3, 0, 0, 0]], dtype=torch.int32)
+    with pytest.raises(RuntimeError):
+        ver._results(ot, oh, oc, None)
+    oc[1, 0] = -1
+    with pytest.raises(ValueError):
+        ver._results(ot, oh, oc, None)
