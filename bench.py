@@ -583,6 +583,7 @@ def run_b200(a):
             sub["config3_path"] = config3_record(a, device, sub_steps, peak)
             sub["lmhead"] = lmhead_record(a, device, 10, tpeak)
             sub["config4_sparse"] = sparse_record(a, device, sub_steps, peak)
+            sub["flashinfer_attention"] = flashinfer_record(a, W, device, 20, k_attn * 1e6)
         else:
             sub["tp"] = tp_record(a, world, rank, device, sub_steps)
             sub["strong"] = strong_record(a, world, rank, device, sub_steps)
@@ -950,6 +951,46 @@ def lmhead_record(a, dev, steps, tpeak):
         out[name] = rec
     out["tensor_peak_tflops"] = tpeak
     return out
+
+
+def flashinfer_record(a, W, dev, steps, ours_us):
+    """The reference's own attention kernel on the benchmark workload: FlashInfer's
+    BatchPrefillWithPagedKVCacheWrapper with the tree masks as a custom boolean
+    mask (flashinfer/attention_wrapper.py:131-144,250-252), the same queries and
+    paged cache; its time beside this library's kernel, and the largest output
+    difference.  None where FlashInfer cannot be imported or built."""
+    import torch
+    from parallel_tree_spec_b200._lib import check
+    st = Step(a, W, dev)                                      # the tree rows' K/V back in place, fresh output
+    check(st.prep[0](*st.prep[1]), "prepare+append")
+    check(st.attn[0](*st.attn[1]), "attention")
+    try:
+        import flashinfer
+        from oracle import attention as oatt
+        mask = torch.cat([torch.from_numpy(oatt.tree_mask(t.parents, a.prefix).reshape(-1)) for t in W["trees"]])
+        ws = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+        w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, kv_layout="NHD")
+        w.plan(W["qo_indptr"], W["page_indptr"], W["page_indices"], W["last_page_len"], a.hq, a.hkv, 128, 16,
+               custom_mask=mask.to(dev), q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+               sm_scale=1.0 / math.sqrt(128))
+        o = w.run(W["q"], W["layer"])
+    except Exception as e:
+        return {"unavailable": str(e)[:200]}
+    ref_out = W["out"].float()
+    diff = float((o.float() - ref_out).abs().max())
+    for _ in range(3):
+        w.run(W["q"], W["layer"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        w.run(W["q"], W["layer"])
+    e1.record()
+    torch.cuda.synchronize()
+    fi_us = e0.elapsed_time(e1) / steps * 1e3
+    return {"kernel": f"flashinfer {flashinfer.__version__} BatchPrefillWithPagedKVCacheWrapper, custom_mask",
+            "flashinfer_us": fi_us, "tree_attn_us": ours_us, "speedup": fi_us / ours_us,
+            "max_abs_diff_vs_tree_attn": diff}
 
 
 def strong_record(a, world, rank, dev, steps):
