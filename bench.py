@@ -66,6 +66,8 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
                     help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["lmhead", "config3", "sparse", "flashinfer"], default=None,
+                    help="run one sub-record alone and print it (for profiling one kernel on a small footprint)")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (other acceptance modes, the config-3 path, tensor-parallel and "
                          "strong-scaling steps)")
@@ -1181,10 +1183,38 @@ def run_sparse(a):
     return 0
 
 
+def run_only(a):
+    """``--only NAME``: one sub-record of the N=1 run, alone."""
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peak, _ = measured_peaks()
+    tpeak, _ = measured_tensor_peak()
+    steps = max(3, min(a.steps, 50))
+    if a.only == "lmhead":
+        rec = lmhead_record(a, dev, steps, tpeak)
+    elif a.only == "config3":
+        rec = config3_record(a, dev, steps, peak)
+    elif a.only == "sparse":
+        rec = sparse_record(a, dev, steps, peak)
+    else:
+        W = build_workload(a, dev, a.seed)
+        st = Step(a, W, dev)
+        for _ in range(3):
+            st.run()
+        el, evs = time_steps(st.run, steps)
+        rec = flashinfer_record(a, W, dev, steps, statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3)
+    print(json.dumps({"only": a.only, **rec}), flush=True)
+    return 0
+
+
 def main(argv=None):
     a = parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.only:
+        return run_only(a)
     if a.sparse:
         return run_sparse(a)
     if a.tp:
