@@ -3,7 +3,11 @@
 Run in a container that has the reference checked out (it is not needed
 afterwards; the committed fixtures travel instead):
 
-    python tests/golden/gen_golden.py [--ref /root/reference/src]
+    python tests/golden/gen_golden.py --ref <checkout>/src
+    PTS_REFERENCE_SRC=<checkout>/src python tests/golden/gen_golden.py
+
+where ``<checkout>/src`` is the directory holding the reference's
+``parallel_tree_spec`` package.
 
 For every case the inputs are regenerated from seeds by
 ``parallel_tree_spec_b200.workload`` (NumPy, machine independent); the
@@ -242,9 +246,13 @@ def mask_cases(Tree):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/src")
+    ap.add_argument("--ref", default=os.environ.get("PTS_REFERENCE_SRC"),
+                    help="directory holding the reference's parallel_tree_spec package "
+                         "(default: $PTS_REFERENCE_SRC)")
     ap.add_argument("--f32-only", action="store_true")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set PTS_REFERENCE_SRC")
     sys.path.insert(0, args.ref)
     from parallel_tree_spec.tree import Tree
     from parallel_tree_spec import verification

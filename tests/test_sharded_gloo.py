@@ -10,6 +10,10 @@
   unsharded kernels in test_gpu_tp.py.
 * ``bench.over_ranks``: the max / min over ranks behind the benchmark's
   slowest-rank timing.
+* A rank that leaves before the exchange: the other rank's
+  ``gather_shards`` ends with an error within the process group's short
+  timeout instead of waiting for good (the failure is made on the host; no
+  kernel is involved).
 """
 import datetime
 import socket
@@ -105,6 +109,34 @@ def _free_port():
 @pytest.mark.timeout(300)
 def test_sharded_exchange_and_rank_reductions_two_gloo_ranks():
     mp.start_processes(_rank_main, args=(_free_port(),), nprocs=WORLD, start_method="spawn", join=True)
+
+
+def _leaver_main(rank, port):
+    import time
+    # a long rendezvous timeout (spawned ranks import torch at different speeds), a short one for the exchange
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=120))
+    group = dist.new_group(list(range(WORLD)), timeout=datetime.timedelta(seconds=5))
+    dist.barrier()
+    if rank == 1:
+        dist.destroy_process_group()                     # leaves between steps, before the exchange
+        return
+    from parallel_tree_spec_b200.kernels import gather_shards
+    t0 = time.monotonic()
+    try:
+        gather_shards(torch.arange(8, dtype=torch.int32), group)
+    except Exception:                                    # gloo: peer closed or timed out
+        raised = True
+    else:
+        raised = False
+    elapsed = time.monotonic() - t0
+    assert raised, "the exchange completed without its peer"
+    assert elapsed < 60.0, elapsed
+
+
+@pytest.mark.timeout(300)
+def test_exchange_with_a_rank_that_left_raises_instead_of_waiting():
+    mp.start_processes(_leaver_main, args=(_free_port(),), nprocs=WORLD, start_method="spawn", join=True)
 
 
 def test_gather_shards_without_a_process_group_is_one_shard():
