@@ -6,16 +6,16 @@
 // remaining up to 8 rows (for example the 65th node of a 65-node tree with 4
 // heads per KV head) run on mma.sync from the same staged K/V.
 //
-// Per 64-token KV block (four 16-token pages), 14 warps:
-//   warps 10-13       TMA producers: warp 10 + w loads page w of the block (K
-//                     and V, two 64-column halves each, 128-byte swizzle) into
-//                     a 4-stage ring three blocks ahead of the consumers, so the
-//                     copies are spread over the four schedulers; with
-//                     remainder rows they then compute those for the current
-//                     block, transposed on mma.sync m16n8k16: S^T = K Q^T (16
-//                     tokens x 8 rows per warp), P^T handed to the next MMA by
-//                     movmatrix, O^T += V^T P^T, each warp with its own running
-//                     max/sum, the four partials merged at the end;
+// Per 64-token KV block (four 16-token pages), 16 warps:
+//   warp 14           TMA producer: lane w loads page w of the block (K and V,
+//                     two 64-column halves each, 128-byte swizzle) into a
+//                     4-stage ring as soon as a stage is free;
+//   warps 10-13       remainder rows (when there are any): warp 10 + w takes
+//                     page w of every block, transposed on mma.sync m16n8k16:
+//                     S^T = K Q^T (16 tokens x 8 rows per warp), P^T handed to
+//                     the next MMA by movmatrix, O^T += V^T P^T, each warp with
+//                     its own running max/sum, the four partials merged at the
+//                     end;
 //   warps 1 and 0     one MMA issuer per tile: S_t = Q_t K^T with Q_t resident in
 //                     TMEM (A from TMEM, M=128, N=64, K=128), O_t += P_t V with
 //                     P_t in shared memory (M=128, N=128, K=64).  The scores of
@@ -28,8 +28,11 @@
 //                     rescaled in TMEM only when the max grows by more than
 //                     2^8), writes P_t as bf16 into one of two shared-memory
 //                     buffers in the MMA's 128-byte-swizzled layout, and at the
-//                     end normalises O_t.
-// TMEM (512 columns): Q_t at 64t, S_t at 128 + 64t, O_t at 256 + 128t.
+//                     end normalises O_t;
+//   warp 15           idle.
+// TMEM (512 columns): Q_t at 64t, S_t at 128 + 64t, O_t at 256 + 128t.  Q and
+// the output pass through the tile's P buffers so that their global accesses
+// are whole rows (512 contiguous bytes per warp instruction).
 //
 // The tree mask: KV slots below kv_len - N are the prefix (always visible);
 // slot kv_len - N + j is visible to row i when bit j of i's mask is set.
@@ -53,9 +56,10 @@ constexpr int kD = 128;
 constexpr int kTensorRows = 256;      // two 128-row tiles
 constexpr int kSyncRows = 8;          // remainder rows on mma.sync (the N of its MMAs)
 constexpr int kGroupRows = kTensorRows + kSyncRows;
-constexpr int kThreads = 448;         // warps 0-1 MMA, 2-9 softmax, 10-13 TMA producers + remainder rows
+constexpr int kThreads = 512;         // warps 0-1 MMA, 2-9 softmax, 10-13 remainder rows, 14 TMA, 15 idle
 constexpr int kSyncWarps = 4;
-constexpr int kMaxSmemPages = 2048;   // page-table entries staged in shared memory
+constexpr int kRemWarp0 = 10;
+constexpr int kProducerWarp = 14;
 constexpr uint32_t kKvHalf = kBlockN * 128;                   // [64 tokens x 64 dims] bf16
 constexpr uint32_t kStageBytes = 4 * kKvHalf;                 // K0 K1 V0 V1
 constexpr uint32_t kPBytes = 128 * kBlockN * 2;               // one P buffer: [128 rows x 64 tokens] bf16
@@ -80,8 +84,7 @@ constexpr uint32_t kOffKV = 0;
 constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;        // 1024-aligned (swizzle atoms)
 constexpr uint32_t kOffMerge = kOffP + 4 * kPBytes;                // remainder partials of warps 11-13
 constexpr uint32_t kMergeFloats = 36;                             // per lane: 32 O + 2 m + 2 l
-constexpr uint32_t kOffPages = kOffMerge + (kSyncWarps - 1) * 32 * kMergeFloats * 4;
-constexpr uint32_t kOffBars = kOffPages + kMaxSmemPages * 4;
+constexpr uint32_t kOffBars = kOffMerge + (kSyncWarps - 1) * 32 * kMergeFloats * 4;
 constexpr uint32_t kSmemBytes = kOffBars + 1024 + 1024;       // bars + alignment slack
 static_assert(kOffP % 1024 == 0, "P tiles must sit on 1024-byte swizzle atoms");
 static_assert(kSmemBytes <= 232448, "shared memory above the 227 KB per-CTA limit");
@@ -186,7 +189,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   Bars& bars = *reinterpret_cast<Bars*>(smem + kOffBars);
-  int32_t* spages = (int32_t*)(smem + kOffPages);
 
   const int h = blockIdx.x, b = blockIdx.y, group = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars.q_ready, 4 * n_tiles);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars.kv_full[s], kSyncWarps);          // one expect_tx arrival per producer warp
+      mbar_init(&bars.kv_full[s], 4);                   // one expect_tx arrival per producer lane (page)
       mbar_init(&bars.kv_empty[s], n_tiles + (sync_rows > 0 ? kSyncWarps : 0));
     }
     for (int t = 0; t < 2; ++t) {
@@ -229,23 +231,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(&bars.tmem, 512);
     tmem_relinquish();
-  }
-  if (warp == 0) {
-    // eight independent loads per lane in flight
-    const int staged = min(n_pages, kMaxSmemPages);
-    for (int i0 = 0; i0 < staged; i0 += 256) {
-      int32_t v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + 32 * u + lane;
-        v[u] = i < staged ? __ldg(p.page_indices + p0 + i) : 0;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + 32 * u + lane;
-        if (i < staged) spages[i] = v[u];
-      }
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -336,21 +321,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int R = row0 + t * 128 + r_local;             // request-local query row
     const bool active_tile = t < n_tiles;
     const bool valid = active_tile && (t * 128 + r_local) < tensor_rows;
-    const int node = R / p.g, hh = R % p.g;
+    const int node = R / p.g;
     const uint64_t* mrow = p.mask_bits ? p.mask_bits + (int64_t)(q0 + node) * p.mask_words : nullptr;
     const uint64_t mw0 = (valid && mrow) ? __ldg(mrow) : 0ull;
     const uint64_t mw1 = (valid && mrow && p.mask_words > 1) ? __ldg(mrow + 1) : 0ull;
     const uint32_t prow = smem_u32(smem + kOffP + 2 * t * kPBytes) + r_local * 128;   // this row of P_t, buffer 0
     const uint32_t pswz = (uint32_t)(r_local & 7);
     if (active_tile) {
-      // this row's query into TMEM columns 64t.. (two bf16 per column)
-      const uint16_t* qrow = p.q + ((int64_t)(q0 + node) * p.Hq + h * p.g + hh) * kD;
+      // The warp's 32 query rows: loaded two rows (512 contiguous bytes) per
+      // instruction into this tile's P buffers (free until block 0's scores),
+      // chunk c of a row at position c ^ (row & 15); then each thread moves its
+      // own row into TMEM columns 64t.. (two bf16 per column).
+      const uint32_t qbuf = smem_u32(smem + kOffP + 2 * t * kPBytes);
+      const int rows_valid = min(32, tensor_rows - (t * 128 + quarter * 32));
+      const uint32_t chunk = (uint32_t)(lane & 15);
+      uint4 qv[16];                                      // all sixteen loads in flight before any store
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rw = 2 * i + (lane >> 4);
+        const int Rw = row0 + t * 128 + quarter * 32 + rw;
+        qv[i] = rw < rows_valid
+                    ? __ldg((const uint4*)(p.q + ((int64_t)(q0 + Rw / p.g) * p.Hq + h * p.g + Rw % p.g) * kD) + chunk)
+                    : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rl = quarter * 32 + 2 * i + (lane >> 4);
+        st_shared_v4(qbuf + (uint32_t)rl * 256u + ((chunk ^ (uint32_t)(rl & 15)) << 4), qv[i].x, qv[i].y, qv[i].z,
+                     qv[i].w);
+      }
+      __syncwarp();
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t r[32];
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          uint4 x = valid ? *(const uint4*)(qrow + half * 64 + 8 * v) : make_uint4(0, 0, 0, 0);
+          const uint32_t chunk = (uint32_t)(half * 8 + v);
+          const uint4 x = ld_shared_v4(qbuf + (uint32_t)r_local * 256u + ((chunk ^ (uint32_t)(r_local & 15)) << 4));
           r[4 * v + 0] = x.x;
           r[4 * v + 1] = x.y;
           r[4 * v + 2] = x.z;
@@ -473,49 +480,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     if (ok && __all_sync(0xffffffffu, mbar_wait(&bars.o_full[t], 0, p.wait_limit))) {
       tc_fence_after();
+      // Each row goes to this tile's P buffers (free: every MMA of the tile has
+      // completed) as 16 chunks of 16 bytes, chunk c at position c ^ (row & 15)
+      // so that a warp's stores hit distinct banks; the warp then writes its
+      // 32 rows out two rows (512 contiguous bytes) per instruction.
       const float inv = (valid && l_sum > 0.0f) ? 1.0f / l_sum : 0.0f;
-      uint16_t* orow = p.out + ((int64_t)(q0 + node) * p.Hq + h * p.g + hh) * kD;
+      const uint32_t obuf = smem_u32(smem + kOffP + 2 * t * kPBytes);
+      const uint32_t swz = (uint32_t)(r_local & 15);
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t o[32];
         tmem_ld32(tmem + lane_base + kColO + 128 * t + 32 * cb, o);
         tmem_ld_wait();
-        if (valid) {
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv);
-            v.y = pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv);
-            v.z = pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv);
-            v.w = pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv);
-            *(uint4*)(orow + cb * 32 + c) = v;
-          }
+        for (int c = 0; c < 32; c += 8) {
+          const uint32_t chunk = (uint32_t)(cb * 4 + c / 8);
+          st_shared_v4(obuf + (uint32_t)r_local * 256u + ((chunk ^ swz) << 4),
+                       pack_bf16x2(__uint_as_float(o[c]) * inv, __uint_as_float(o[c + 1]) * inv),
+                       pack_bf16x2(__uint_as_float(o[c + 2]) * inv, __uint_as_float(o[c + 3]) * inv),
+                       pack_bf16x2(__uint_as_float(o[c + 4]) * inv, __uint_as_float(o[c + 5]) * inv),
+                       pack_bf16x2(__uint_as_float(o[c + 6]) * inv, __uint_as_float(o[c + 7]) * inv));
+        }
+      }
+      __syncwarp();
+      const int rows_valid = min(32, tensor_rows - (t * 128 + quarter * 32));   // valid rows are a prefix
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int rw = 2 * i + (lane >> 4);                // row of this warp's 32
+        if (rw < rows_valid) {
+          const int rl = quarter * 32 + rw;
+          const uint32_t chunk = (uint32_t)(lane & 15);
+          const uint4 v = ld_shared_v4(obuf + (uint32_t)rl * 256u + ((chunk ^ (uint32_t)(rl & 15)) << 4));
+          const int Rw = row0 + t * 128 + rl;
+          *(uint4*)(p.out + ((int64_t)(q0 + Rw / p.g) * p.Hq + h * p.g + Rw % p.g) * kD + chunk * 8) = v;
         }
       }
     } else if (ok) {
       record_abort(bars, p, 32);
     }
-  } else {
-    // ------------------------------------------------------------ TMA producers + remainder rows
-    // Warp 10 + w loads page w of every block (K and V, both 64-column halves)
-    // kAhead blocks in front of the consumers, so the TMA traffic is spread
-    // over the four schedulers; with remainder rows it then computes them for
-    // the current block (mma.sync, transposed).
-    const int wr = warp - 10;                              // this warp's page / 16 tokens of every block
-    const bool rem = sync_rows > 0;
-    const int gq = lane >> 2, tq = lane & 3;               // fragment group / thread in group
-    const int mi = lane >> 3, rr = lane & 7;               // ldmatrix: matrix / row supplied by this lane
+  } else if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ TMA producer
+    // Lane w < 4 loads page w of every block (K and V, both 64-column halves)
+    // into the 4-stage ring as soon as the stage is free.  The page indices
+    // come in windows of eight blocks (lane l holds slot 32k + l of window k),
+    // the next window loading while the current one is used.
+    const int w = lane & 3;
+    auto window = [&](int k) -> int {
+      const int slot = 32 * k + lane;
+      const int phys = slot < n_pages ? __ldg(p.page_indices + p0 + slot) : p.max_pages;
+      return (phys >= 0 && phys < p.max_pages) ? phys : p.max_pages;   // invalid: zero fill
+    };
+    int win_cur = window(0), win_next = window(1);
     auto produce = [&](int blk) -> bool {
       const int s = blk % kStages;
       const bool w_ok =
           mbar_wait_lazy(&bars.kv_empty[s], ((blk / kStages) + 1) & 1, 200, p.wait_limit) && !aborted(bars);
       if (!__all_sync(0xffffffffu, w_ok)) return false;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bars.kv_full[s], kStageBytes / kSyncWarps);
-        const int slot = (kBlockN / kPage) * blk + wr;
-        const int phys = slot >= n_pages ? p.max_pages                                   // OOB -> zero fill
-                         : (slot < kMaxSmemPages ? spages[slot] : p.page_indices[p0 + slot]);
-        const int page = (phys >= 0 && phys < p.max_pages) ? phys : p.max_pages;
-        uint8_t* st = smem + kOffKV + s * kStageBytes + wr * (kPage * 128);
+      const int page = __shfl_sync(0xffffffffu, win_cur, (blk & 7) * 4 + w);
+      if (lane < 4) {
+        mbar_arrive_expect_tx(&bars.kv_full[s], kStageBytes / 4);
+        uint8_t* st = smem + kOffKV + s * kStageBytes + lane * (kPage * 128);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           tma_load_4d(st + half * kKvHalf, &kv_map, &bars.kv_full[s], half * 64, h, 0, 2 * page);
@@ -523,8 +546,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      if ((blk & 7) == 7) {
+        win_cur = win_next;
+        win_next = window((blk >> 3) + 2);
+      }
       return true;
     };
+    bool ok = true;
+    int produced = 0;
+    for (int blk = 0; ok && blk < n_blocks; ++blk) {
+      ok = produce(blk);
+      if (ok) produced = blk + 1;
+    }
+    if (!ok && lane == 0) record_abort(bars, p, 41);
+    // the copies this warp issued must land before the CTA can exit
+    for (int blk = max(0, produced - kStages); blk < produced; ++blk)
+      mbar_wait(&bars.kv_full[blk % kStages], (blk / kStages) & 1);
+  } else if (warp >= kRemWarp0 && warp < kRemWarp0 + kSyncWarps && sync_rows > 0) {
+    // ------------------------------------------------------------ remainder rows
+    // Warp kRemWarp0 + wr computes the remainder rows against page wr (16
+    // tokens) of every block on mma.sync, transposed: S^T = K Q^T, P^T handed
+    // to the next MMA by movmatrix, O^T += V^T P^T; the four partials are
+    // merged at the end.
+    const int wr = warp - kRemWarp0;
+    const int gq = lane >> 2, tq = lane & 3;               // fragment group / thread in group
+    const int mi = lane >> 3, rr = lane & 7;               // ldmatrix: matrix / row supplied by this lane
     // Q^T as the B operand: column gq is remainder row gq
     uint32_t qb[8][2];
     {
@@ -553,20 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
     const uint32_t kv_s = smem_u32(smem + kOffKV);
-    constexpr int kAhead = kStages - 1;
     bool ok = true;
-    int produced = 0;
-    for (int blk = 0; ok && blk < min(kAhead, n_blocks); ++blk) {
-      ok = produce(blk);
-      if (ok) produced = blk + 1;
-    }
     for (int j = 0; ok && j < n_blocks; ++j) {
-      if (j + kAhead < n_blocks) {
-        ok = produce(j + kAhead);
-        if (!ok) break;
-        produced = j + kAhead + 1;
-      }
-      if (!rem) continue;
       const int s = j % kStages;
       ok = __all_sync(0xffffffffu, mbar_wait(&bars.kv_full[s], (j / kStages) & 1, p.wait_limit) && !aborted(bars));
       if (!ok) break;
@@ -596,32 +630,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c = 16 * wr + gq + 8 * (e >> 1);
         x[e] = ((vis[e & 1] >> c) & 1ull) && rvalid[e & 1] ? (sa[e] + sb[e]) * p.scale_log2 : -INFINITY;
       }
-      float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
+      // Lazy rescale, as in the tiles: the subtracted max moves (and O and
+      // the sums are rescaled) only when some score of the block exceeds it
+      // by more than 2^8; otherwise no row max is taken at all.
+      const bool grow = x[0] > m_run[0] + kRescaleThreshold || x[2] > m_run[0] + kRescaleThreshold ||
+                        x[1] > m_run[1] + kRescaleThreshold || x[3] > m_run[1] + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, grow)) {
+        float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
 #pragma unroll
-      for (int off = 4; off <= 16; off <<= 1) {
-        mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
-        mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], off));
-      }
-      float alpha[2], msub[2];
+        for (int off = 4; off <= 16; off <<= 1) {
+          mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
+          mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], off));
+        }
+        float alpha[2];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const float nm = fmaxf(m_run[i], mx[i]);
-        alpha[i] = (m_run[i] == -INFINITY) ? 0.0f : fast_exp2(m_run[i] - nm);
-        m_run[i] = nm;
-        msub[i] = nm == -INFINITY ? 0.0f : nm;
+        for (int i = 0; i < 2; ++i) {
+          const float nm = fmaxf(m_run[i], mx[i]);
+          alpha[i] = (m_run[i] == -INFINITY) ? 0.0f : fast_exp2(m_run[i] - nm);
+          m_run[i] = nm;
+          l_run[i] *= alpha[i];
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][0] *= alpha[0];
+          o[mt][1] *= alpha[1];
+          o[mt][2] *= alpha[0];
+          o[mt][3] *= alpha[1];
+        }
       }
+      const float msub[2] = {m_run[0] == -INFINITY ? 0.0f : m_run[0], m_run[1] == -INFINITY ? 0.0f : m_run[1]};
       float ex[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) ex[e] = fast_exp2(x[e] - msub[e & 1]);
-      l_run[0] = l_run[0] * alpha[0] + ex[0] + ex[2];
-      l_run[1] = l_run[1] * alpha[1] + ex[1] + ex[3];
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        o[mt][0] *= alpha[0];
-        o[mt][1] *= alpha[1];
-        o[mt][2] *= alpha[0];
-        o[mt][3] *= alpha[1];
-      }
+      l_run[0] += ex[0] + ex[2];
+      l_run[1] += ex[1] + ex[3];
       // P^T as the B operand: (token 2tq.., row gq) by transposing the 8x8 blocks
       const uint32_t pb0 = movmatrix_trans(pack_bf16x2(ex[0], ex[1]));
       const uint32_t pb1 = movmatrix_trans(pack_bf16x2(ex[2], ex[3]));
@@ -636,11 +678,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.kv_empty[s]);
     }
-    if (!ok && lane == 0) record_abort(bars, p, 41);
-    // the copies this warp issued must land before the CTA can exit
-    for (int blk = max(0, produced - kStages); blk < produced; ++blk)
-      mbar_wait(&bars.kv_full[blk % kStages], (blk / kStages) & 1);
-    if (rem) {
+    if (!ok && lane == 0) record_abort(bars, p, 42);
+    {
 #pragma unroll
     for (int off = 4; off <= 16; off <<= 1) {
       l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
@@ -693,15 +732,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        if (!rvalid[i]) continue;
-        const int R = row0 + kTensorRows + 2 * tq + i;
-        uint16_t* orow = p.out + ((int64_t)(q0 + R / p.g) * p.Hq + h * p.g + R % p.g) * kD;
         const float inv = L[i] > 0.0f ? 1.0f / L[i] : 0.0f;
+        L[i] = inv;
+      }
+      // the 8 rows through shared memory (the merge area, read above by this
+      // warp only), then two rows (512 contiguous bytes) per store instruction
+      __syncwarp();
+      uint16_t* ostage = (uint16_t*)(smem + kOffMerge);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          const uint32_t lo = pack_bf16x2(o[mt][i] * inv, o[mt][2 + i] * inv);
-          orow[16 * mt + gq] = (uint16_t)(lo & 0xffffu);
-          orow[16 * mt + gq + 8] = (uint16_t)(lo >> 16);
+          const uint32_t lo = pack_bf16x2(o[mt][i] * L[i], o[mt][2 + i] * L[i]);
+          ostage[(2 * tq + i) * kD + 16 * mt + gq] = (uint16_t)(lo & 0xffffu);
+          ostage[(2 * tq + i) * kD + 16 * mt + gq + 8] = (uint16_t)(lo >> 16);
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < kSyncRows / 2; ++i) {
+        const int r = 2 * i + (lane >> 4);
+        if (r < sync_rows) {
+          const int R = row0 + kTensorRows + r;
+          const uint4 v = *(const uint4*)(ostage + r * kD + (lane & 15) * 8);
+          *(uint4*)(p.out + ((int64_t)(q0 + R / p.g) * p.Hq + h * p.g + R % p.g) * kD + (lane & 15) * 8) = v;
         }
       }
     }

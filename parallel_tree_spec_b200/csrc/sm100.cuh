@@ -52,6 +52,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (returns at once).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // try_wait that lets the hardware park the thread for up to `hint_ns` while the
 // phase is incomplete (it resumes as soon as the phase completes), so waiting
 // warps do not take issue slots from the warps that share their scheduler.
@@ -73,9 +86,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // kept with clock64, which is cheap to read in the polling loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           long long timeout_cycles = 4000000000ll) {
-  if (mbar_try_wait(bar, parity)) return true;
+  // A plain try_wait may park the thread for a hardware-chosen time, so a
+  // short limit (failure tests) starts with the non-blocking test instead.
+  const bool long_limit = timeout_cycles >= 200000000ll;
+  if (long_limit ? mbar_try_wait(bar, parity) : mbar_test_wait(bar, parity)) return true;
   // the suspend hint (ns) stays well below the limit, so a short limit runs out
-  const uint32_t hint = timeout_cycles >= 200000000ll ? 100000u : (uint32_t)max(timeout_cycles / 4, 1ll);
+  const uint32_t hint = long_limit ? 100000u : (uint32_t)max(timeout_cycles / 4, 1ll);
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, hint)) return true;
@@ -88,10 +104,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 // Gives up after `timeout_cycles` SM clocks like mbar_wait.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
                                                long long timeout_cycles = 4000000000ll) {
-  if (mbar_try_wait(bar, parity)) return true;
+  const bool long_limit = timeout_cycles >= 200000000ll;
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (long_limit ? mbar_try_wait(bar, parity) : mbar_test_wait(bar, parity)) return true;
     if (clock64() - t0 > timeout_cycles) return false;
   }
 }
@@ -101,9 +117,10 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
 // (a producer several stages in front), where reacting late costs nothing.
 __device__ __forceinline__ bool mbar_wait_lazy(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
                                                long long timeout_cycles = 4000000000ll) {
+  const bool long_limit = timeout_cycles >= 200000000ll;
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (long_limit ? mbar_try_wait(bar, parity) : mbar_test_wait(bar, parity)) return true;
     if (clock64() - t0 > timeout_cycles) return false;
     __nanosleep(sleep_ns);
   }
@@ -363,6 +380,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t saddr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr)
+               : "memory");
+  return v;
 }
 
 }  // namespace sm100
