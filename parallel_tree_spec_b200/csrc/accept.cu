@@ -1966,7 +1966,8 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
 //                      first index whose running sum exceeds the target.
 
 constexpr int kToppThreads = 512;
-constexpr int kToppWindow = 4;           // coarse bins (256 values each) counted per pass
+constexpr int kToppFirstWindow = 256;    // distinct values counted by the first pass (two binades)
+constexpr int kToppMaxWindow = 4096;     // later passes widen the window up to this
 
 // Order-preserving 16-bit key of a bf16 value (-0 folded onto +0).
 __device__ __forceinline__ uint32_t bf16_key(uint32_t bits) {
@@ -1982,79 +1983,164 @@ __device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uin
   return __float_as_uint(load_scaled(p, row, e)) >> 16;
 }
 
-// One CTA per row: counts of every distinct value in a window of kToppWindow
-// coarse bins below the row max (16-byte loads where rows are aligned), then
-// the cumulative mass from the top; the window moves down until the mass
-// reaches top_p * s.
+// One CTA per row.  Each pass counts the occurrences of every distinct value
+// in a window of keys below the previous one (the first window holds the row
+// max and the 255 values below it; later windows are wider), then takes the
+// cumulative mass from the top, sum of count(v) * expf(v - m) in descending
+// value order in fp64, until it reaches top_p * s.
+//
+// The cumulative sums are taken as a parallel prefix over the window.  That
+// equals the ordered fp64 sum whenever no partial sum rounds: every term is a
+// multiple of the ulp u of the smallest term involved (an integer times an fp32
+// value of at least that size), so every partial sum is exact while it stays
+// below 2^53 u.  The pass checks that bound (with a margin far above its own
+// rounding) and otherwise walks the window in order on one thread, as the rule
+// states.
 __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p, float top_p, float* thresh,
                                                              float* mass) {
-  __shared__ uint32_t cnt[kToppWindow * 256];
-  __shared__ int s_done;
-  __shared__ float s_t, s_m;
-  const int row = blockIdx.x, tid = threadIdx.x;
+  __shared__ uint32_t cnt[kToppMaxWindow];               // index i: key hi_key - i (descending values)
+  __shared__ double wtot[kToppThreads / 32];
+  __shared__ int s_cross, s_last, s_done;
+  __shared__ float s_t;
+  __shared__ double s_cum, s_pre;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowStat rs = p.row_ws[row];
   const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
   const double target = (double)top_p * (double)rs.s;
-  const int top_coarse = (int)(bf16_key(__float_as_uint(rs.m) >> 16) >> 8);
   const bool vec = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
-  double cum = 0.0;                       // thread 0's running mass over the windows
-  if (tid == 0) s_done = 0;
-  for (int hi_c = top_coarse; hi_c >= 0; hi_c -= kToppWindow) {
-    const int lo_c = max(0, hi_c - kToppWindow + 1);
-    const uint32_t lo_key = (uint32_t)lo_c << 8, hi_key = ((uint32_t)hi_c << 8) | 0xffu;
-    for (int i = tid; i < kToppWindow * 256; i += kToppThreads) cnt[i] = 0u;
+  auto term = [&](int hi_key, int i, uint32_t c) -> double {
+    return (double)c * (double)expf(key_bf16((uint32_t)(hi_key - i)) - rs.m);
+  };
+  if (tid == 0) {
+    s_cum = 0.0;
+    s_t = -INFINITY;
+    s_done = 0;
+  }
+  int width = kToppFirstWindow;
+  for (int hi_key = (int)bf16_key(__float_as_uint(rs.m) >> 16); hi_key >= 0;
+       hi_key -= width, width = min(2 * width, kToppMaxWindow)) {
+    const int lo_key = max(0, hi_key - width + 1);
+    const int n = hi_key - lo_key + 1;
+    // a value is counted when its key is in [lo_key, hi_key]; the float test
+    // is a cheap superset of that (it merges -0 and +0), the key test decides
+    const float vlo = key_bf16((uint32_t)lo_key), vhi = key_bf16((uint32_t)hi_key);
+    for (int i = tid; i < n; i += kToppThreads) cnt[i] = 0u;
+    if (tid == 0) {
+      s_cross = INT_MAX;
+      s_last = -1;
+    }
     __syncthreads();
-    auto count = [&](uint32_t bits) {
-      const uint32_t k = bf16_key(bits);
-      if (k >= lo_key && k <= hi_key) atomicAdd(&cnt[k - lo_key], 1u);
+    auto count1 = [&](uint32_t bits) {
+      const float a = __uint_as_float(bits << 16);
+      if (a >= vlo && a <= vhi) {
+        const int k = (int)bf16_key(bits);
+        if (k >= lo_key && k <= hi_key) atomicAdd(&cnt[hi_key - k], 1u);
+      }
     };
     int e_tail = 0;
     if (vec) {
-      // 16-byte loads, four in flight per thread before any is counted
       const int nv = p.vocab / 8;
       for (int v0 = tid; v0 < nv; v0 += 4 * kToppThreads) {
         uint4 x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int vi = v0 + u * kToppThreads;
-          x[u] = vi < nv ? ld_stream(rp + (int64_t)vi * 8) : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+          x[u] = vi < nv ? ld_stream(rp + (int64_t)vi * 8)
+                         : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);   // -inf: never counted
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          if (v0 + u * kToppThreads >= nv) continue;
           uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (p.use_temp) w[j] = scale_pair(w[j], p.inv_temp);
-            count(w[j] & 0xffffu);
-            count(w[j] >> 16);
+          for (int k = 0; k < 4; ++k) {
+            if (p.use_temp) w[k] = scale_pair(w[k], p.inv_temp);
+            count1(w[k] & 0xffffu);
+            count1(w[k] >> 16);
           }
         }
       }
       e_tail = nv * 8;
     }
-    for (int e = e_tail + tid; e < p.vocab; e += kToppThreads) count(scaled_bits(p, rp, e));
+    for (int e = e_tail + tid; e < p.vocab; e += kToppThreads) count1(scaled_bits(p, rp, e));
+    __syncthreads();
+    // per-thread sums over entries [i0, i0 + E), then a block-wide exclusive prefix
+    const int E = (n + kToppThreads - 1) / kToppThreads;
+    const int i0 = min(tid * E, n), i1 = min(i0 + E, n);
+    double loc = 0.0;
+    for (int i = i0; i < i1; ++i)
+      if (cnt[i]) loc += term(hi_key, i, cnt[i]);
+    double inc = loc;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const double o = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += o;
+    }
+    if (lane == 31) wtot[warp] = inc;
+    __syncthreads();
+    double pre = s_cum + inc - loc;
+    for (int w = 0; w < warp; ++w) pre += wtot[w];
+    int my_cross = INT_MAX, my_last = -1;
+    double my_pre = 0.0;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t c = cnt[i];
+      if (!c) continue;
+      pre += term(hi_key, i, c);
+      my_last = i;
+      if (pre >= target) {
+        my_cross = i;
+        my_pre = pre;
+        break;
+      }
+    }
+    if (my_cross != INT_MAX) atomicMin(&s_cross, my_cross);
+    if (my_last >= 0) atomicMax(&s_last, my_last);
+    __syncthreads();
+    if (my_cross != INT_MAX && my_cross == s_cross) s_pre = my_pre;
     __syncthreads();
     if (tid == 0) {
-      for (int k = (int)hi_key; k >= (int)lo_key; --k) {
-        const uint32_t c = cnt[k - (int)lo_key];
-        if (!c) continue;
-        const float v = key_bf16((uint32_t)k);
-        cum += (double)c * (double)expf(v - rs.m);
-        if (cum >= target) {
-          s_done = 1;
-          s_t = v;
-          break;
-        }
+      const bool crossed = s_cross != INT_MAX;
+      double reach = s_cum;                              // the largest partial sum involved
+      if (crossed) {
+        reach = s_pre;
+      } else {
+        for (int w = 0; w < kToppThreads / 32; ++w) reach += wtot[w];
       }
-      s_m = (float)cum;
+      const int small_i = crossed ? s_cross : s_last;    // the smallest term involved
+      bool exact = true;
+      if (small_i >= 0) {
+        int ex = 0;
+        const float small = expf(key_bf16((uint32_t)(hi_key - small_i)) - rs.m);
+        frexpf(small, &ex);                              // small = f 2^ex, f in [0.5, 1)
+        exact = small >= 1.17549435e-38f && reach < ldexp(1.0, 30 + (ex - 1)) * (1.0 - 1e-9);
+      }
+      if (exact) {
+        s_cum = reach;
+        if (crossed) {
+          s_t = key_bf16((uint32_t)(hi_key - s_cross));
+          s_done = 1;
+        }
+      } else {
+        // the rule's own order
+        double cum = s_cum;
+        for (int i = 0; i < n; ++i) {
+          const uint32_t c = cnt[i];
+          if (!c) continue;
+          cum += term(hi_key, i, c);
+          if (cum >= target) {
+            s_t = key_bf16((uint32_t)(hi_key - i));
+            s_done = 1;
+            break;
+          }
+        }
+        s_cum = cum;
+      }
     }
     __syncthreads();
     if (s_done) break;
   }
   if (tid == 0) {
-    thresh[row] = s_done ? s_t : -INFINITY;   // the whole row when rounding keeps the mass below the target
-    mass[row] = s_m;
+    thresh[row] = s_t;                       // -inf: the whole row, when rounding keeps the mass below the target
+    mass[row] = (float)s_cum;
   }
 }
 
