@@ -453,6 +453,38 @@ int pts_tree_attn_run_head_pages(const void* q, const void* kv_layer, const int3
                                  int page_len, int max_pages, float sm_scale, void* workspace,
                                  size_t workspace_bytes, pts_stream_t stream);
 
+/* --------------------------------------------------------- draft beam search
+ * The draft's beam search builds the tree the path verifies
+ * (beam_search.py:315-616).  Two of its device steps:
+ *
+ * pts_beam_select replaces the per-step scoring and selection
+ *   probs = torch.softmax(logits[:, -1, :] / T, dim=-1)
+ *   flat  = (cum[:, None] + torch.log(probs + 1e-10)).reshape(-1)
+ *   scores, ids = flat.topk(K);  step_prob = probs[ids // V, ids % V]
+ * (beam_search.py:549-561), and, with cum_log_probs NULL, the first step's
+ * torch.softmax(logits / T).topk(K) (:432-433): logits [rows, row_stride]
+ * (elem_bytes 2: bf16, rounded as torch's bf16 arithmetic rounds; 4: fp32),
+ * the k best scores (k <= 16, rows <= 32) in descending order into out_score,
+ * their flat indices row * vocab + token into out_index and their p into
+ * out_prob.  Ties go to the smaller flat index (torch leaves their order
+ * unspecified).  workspace: pts_beam_select_workspace_size(rows, k) bytes. */
+size_t pts_beam_select_workspace_size(int rows, int k);
+int pts_beam_select(const void* logits, int64_t row_stride, int elem_bytes, int rows, int vocab,
+                    float temperature, const float* cum_log_probs, int k, float* out_score,
+                    int64_t* out_index, float* out_prob, void* workspace, size_t workspace_bytes,
+                    pts_stream_t stream);
+
+/* Copy-on-write page copies of one decode step, _copy_block's
+ *   cache_data[:, new_page, :, :off] = cache_data[:, src_page, :, :off]
+ * (beam_search.py:92-96) for num_pairs (src_pages[i] -> dst_pages[i]) pairs
+ * in one launch: the first `tokens` slots of every layer, keys and values, of
+ * a pool laid out [num_layers, max_pages, 2, page_len, row_bytes]
+ * (row_bytes = num_kv_heads * head_dim * element size, a multiple of 16).
+ * Pairs naming a page outside [0, max_pages) are skipped. */
+int pts_kv_copy_pages(void* kv_pool, int num_layers, int max_pages, int page_len, int row_bytes,
+                      const int32_t* src_pages, const int32_t* dst_pages, int num_pairs, int tokens,
+                      pts_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

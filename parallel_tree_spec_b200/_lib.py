@@ -54,6 +54,9 @@ SIGNATURES = {
                                               vp]),
     "pts_lmhead_logits": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, i64, vp]),
     "pts_lmhead_workspace_size": (sz, [C.c_int, C.c_int]),
+    "pts_beam_select_workspace_size": (sz, [C.c_int, C.c_int]),
+    "pts_beam_select": (C.c_int, [vp, i64, C.c_int, C.c_int, C.c_int, f32, vp, C.c_int, vp, vp, vp, vp, sz, vp]),
+    "pts_kv_copy_pages": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp]),
     "pts_lmhead_accept": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, i64,
                                     C.c_int, f32, u64, u64, vp, vp, vp, C.c_int, vp, sz, vp]),
     "pts_accept_shard_partials": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, f32, vp, vp,

@@ -67,6 +67,13 @@ class BeFlashinferWrapper:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self._plan = None
 
+    def init_cuda_graph_decode(self, K: int, max_num_pages: int, device: torch.device):
+        """``attention_wrapper.py:95-107`` rebuilds FlashInfer's decode wrapper
+        over fixed index buffers before graph capture.  The kernels here read
+        the page tables on the device and keep no host plan state a graph
+        would freeze, so there is nothing to rebuild."""
+        return None
+
     # ------------------------------------------------------------------ plan
     def prepareAttention(self, mode: str, batch_position: KvCacheBatchPosition, page_len: int, pos_encoding_mode,
                          dtype: torch.dtype, attention_mask: Optional[torch.Tensor] = None):

@@ -680,3 +680,51 @@ def tree_attention_head_pages(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr
               mask_bits.shape[1] if mask_bits is not None else 1, out.data_ptr(), B, T, int(max_qo_len),
               int(max_kv_len), Hq, Hkv, D, pl, P, scale, ws.data_ptr(), ws.numel(), _stream(dev))
     return out
+
+
+# ------------------------------------------------------------ draft beam search
+def beam_select(logits: torch.Tensor, k: int, temperature: float = 1.0,
+                cum_log_probs: Optional[torch.Tensor] = None):
+    """The beam search's per-step selection (``beam_search.py:549-561``):
+    the k best of ``cum[:, None] + log(softmax(logits / T) + 1e-10)`` over the
+    flattened [rows, vocab] scores, or with ``cum_log_probs`` None the k best
+    probabilities of the rows (the first step, ``:432-433``).  Returns
+    (scores fp32 [k], flat indices int64 [k], probabilities fp32 [k]), best
+    first, ties to the smaller flat index."""
+    dev = _need_cuda(logits)
+    if logits.dim() != 2 or logits.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("logits must be a 2-D bf16 or fp32 tensor [rows, vocab]")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    rows, vocab = logits.shape
+    cum_ptr = None
+    if cum_log_probs is not None:
+        _need_cuda(logits, cum_log_probs)
+        cum_log_probs = cum_log_probs.to(torch.float32).contiguous()
+        if cum_log_probs.numel() != rows:
+            raise ValueError("cum_log_probs needs one value per row")
+        cum_ptr = cum_log_probs.data_ptr()
+    score = torch.empty(k, dtype=torch.float32, device=dev)
+    index = torch.empty(k, dtype=torch.int64, device=dev)
+    prob = torch.empty(k, dtype=torch.float32, device=dev)
+    nbytes = _lib.lib().pts_beam_select_workspace_size(rows, k)
+    ws = workspace(dev, "beam", max(nbytes, 256))
+    _lib.call("pts_beam_select", logits.data_ptr(), logits.stride(0), logits.element_size(), rows, vocab,
+              float(temperature), cum_ptr, k, score.data_ptr(), index.data_ptr(), prob.data_ptr(), ws.data_ptr(),
+              ws.numel(), _stream(dev))
+    return score, index, prob
+
+
+def kv_copy_pages(cache_data: torch.Tensor, src_pages: torch.Tensor, dst_pages: torch.Tensor, tokens: int) -> None:
+    """Copy-on-write copies of one decode step (``beam_search.py:92-96``):
+    ``cache_data[:, dst, :, :tokens] = cache_data[:, src, :, :tokens]`` for
+    every pair, in one launch.  ``cache_data``: the pool [L, P, 2, page, H, D]."""
+    dev = _need_cuda(cache_data, src_pages, dst_pages)
+    if cache_data.dim() != 6 or not cache_data.is_contiguous():
+        raise ValueError("cache_data must be a contiguous [layers, pages, 2, page_len, heads, dim] tensor")
+    L, P, _, page_len, H, D = cache_data.shape
+    src, dst = _i32(src_pages, "src_pages"), _i32(dst_pages, "dst_pages")
+    if src.numel() != dst.numel():
+        raise ValueError("src_pages and dst_pages differ in length")
+    _lib.call("pts_kv_copy_pages", cache_data.data_ptr(), L, P, page_len, H * D * cache_data.element_size(),
+              src.data_ptr(), dst.data_ptr(), src.numel(), int(tokens), _stream(dev))
