@@ -2030,7 +2030,17 @@ __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p
       s_last = -1;
     }
     __syncthreads();
+    // A window of positive values (the usual case) is a contiguous range of
+    // bf16 bit patterns [lo_bits, hi_bits] that no negative value reaches, and
+    // its key is bits | 0x8000: one unsigned compare decides, no key math.
+    const bool pos_window = vlo > 0.0f;
+    const uint32_t lo_bits = __float_as_uint(vlo) >> 16, span = (__float_as_uint(vhi) >> 16) - lo_bits;
+    const uint32_t hi_bits = lo_bits + span;
     auto count1 = [&](uint32_t bits) {
+      if (pos_window) {
+        if (bits - lo_bits <= span) atomicAdd(&cnt[hi_bits - bits], 1u);
+        return;
+      }
       const float a = __uint_as_float(bits << 16);
       if (a >= vlo && a <= vhi) {
         const int k = (int)bf16_key(bits);
