@@ -66,7 +66,7 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-time-budget", type=float, default=90.0,
                     help="seconds after which the reference arm stops timing further steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["lmhead", "config3", "sparse", "flashinfer"], default=None,
+    ap.add_argument("--only", choices=["lmhead", "config3", "sparse", "flashinfer", "beam"], default=None,
                     help="run one sub-record alone and print it (for profiling one kernel on a small footprint)")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (other acceptance modes, the config-3 path, tensor-parallel and "
@@ -584,6 +584,7 @@ def run_b200(a):
         if world == 1:
             sub["config3_path"] = config3_record(a, device, sub_steps, peak)
             sub["lmhead"] = lmhead_record(a, device, 10, tpeak)
+            sub["beam_select"] = beam_record(a, device, 50)
             sub["config4_sparse"] = sparse_record(a, device, sub_steps, peak)
             sub["flashinfer_attention"] = flashinfer_record(a, W, device, 20, k_attn * 1e6)
         else:
@@ -882,6 +883,47 @@ def config3_record(a, dev, steps, peak):
                          "accept_frac": logit_bytes / (acc_us * 1e-6) / 1e9 / peak,
                          "step_frac": (kv_read + qo_bytes + append + logit_bytes) / (el / steps * 1e-3) / 1e9 / peak},
             "accept_len_mean": float(oc[:, 2].float().mean().item())}
+
+
+def beam_record(a, dev, steps):
+    """One decode step's candidate selection of the draft beam search
+    (beam_search.py:549-561) for 8 beams over the 128256-entry vocabulary
+    (bf16 logits, T = 1): the reference's torch chain (softmax, + 1e-10,
+    log, + the beams' cumulative scores, flattened topk, the picks'
+    probabilities) against pts_beam_select; the same picks either way."""
+    import torch
+    from parallel_tree_spec_b200 import kernels as K
+
+    Kb, V = 8, a.vocab
+    g = torch.Generator(device=dev)
+    g.manual_seed(a.seed + 51)
+    x = (torch.randn(Kb, V, generator=g, device=dev) * 3.0).to(torch.bfloat16)
+    cum = -torch.rand(Kb, generator=g, device=dev) * 4.0
+
+    def chain():
+        probs = torch.softmax(x / 1.0, dim=-1)
+        flat = (cum[:, None] + torch.log(probs + 1e-10)).reshape(-1)
+        sc, ids = flat.topk(Kb)
+        return sc, ids, probs.reshape(-1)[ids]
+
+    def fused():
+        return K.beam_select(x, Kb, 1.0, cum)
+
+    out = {"workload": f"beam-search selection: {Kb} beams x vocabulary {V}, bf16 logits, T=1.0", "unit": "us"}
+    for name, fn in (("torch_chain", chain), ("beam_select", fused)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name + "_us"] = e0.elapsed_time(e1) * 1e3 / steps
+    ref, got = chain(), fused()
+    out["same_picks"] = bool(torch.equal(ref[1], got[1]) and torch.equal(ref[0], got[0]))
+    return out
 
 
 def lmhead_record(a, dev, steps, tpeak):
@@ -1198,6 +1240,8 @@ def run_only(a):
         rec = config3_record(a, dev, steps, peak)
     elif a.only == "sparse":
         rec = sparse_record(a, dev, steps, peak)
+    elif a.only == "beam":
+        rec = beam_record(a, dev, steps)
     else:
         W = build_workload(a, dev, a.seed)
         st = Step(a, W, dev)
