@@ -5,11 +5,13 @@
 //   cum[beam] + log(bf16(p + 1e-10)),  p = softmax(logits[beam] / T) in bf16
 // and keeps the K best of the flattened [beams x vocab] scores (topk), each
 // with its p (the new node's probability); the first step keeps the K best
-// p of the prompt row.  Here one CTA per beam row takes the row max and the
-// fp64 sum of expf(x - m) (rounded to fp32, as the softmax's fp32 sum), then
-// scores the row and keeps its best k (score descending, index ascending)
-// in per-thread sorted lists merged across the CTA; a second launch merges
-// the rows' lists in flat-index order.  p = bf16(expf(x - m) / s), the log
+// p of the prompt row.  Each row is cut into slices, one CTA per (slice,
+// row), about two CTAs per SM over all rows: one launch takes the slices'
+// maxima, one the slices' fp64 sums of expf(x - m) with the row max, one
+// scores every slice against the row's (max, sum) -- the sum is the slices'
+// sums in slice order, rounded to fp32 -- and keeps the slice's best k (score
+// descending, index ascending) in per-thread sorted lists merged across the
+// CTA, and one CTA merges all slices' lists.  p = bf16(expf(x - m) / s), the log
 // and the sum are bf16-rounded, the add is an fp32 add -- torch's bf16
 // arithmetic.
 //
@@ -44,48 +46,89 @@ __device__ __forceinline__ float load_logit(const void* row, int e, int elem_byt
   return x;
 }
 
-// One CTA per beam row: the row's best k candidates, in order, into rows_out[row * k ..].
-__global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logits, int64_t row_stride, int elem_bytes,
-                                                               int vocab, float inv_t, int scale,
-                                                               const float* cum, int k, Cand* rows_out) {
-  __shared__ float red_m[kSelThreads / 32];
-  __shared__ double red_s[kSelThreads / 32];
-  __shared__ float s_m, s_s;
-  __shared__ Cand heads[kSelThreads];
-  __shared__ int s_winner;
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const char* rp = (const char*)logits + (int64_t)row * row_stride * elem_bytes;
-  // row max
-  float m = -INFINITY;
-  for (int e = tid; e < vocab; e += kSelThreads) m = fmaxf(m, load_logit(rp, e, elem_bytes, inv_t, scale));
+// Block-wide max / fp64 sum of one value per thread (result in every thread).
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) red_m[warp] = m;
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   __syncthreads();
-  if (tid == 0) {
-    float mm = red_m[0];
-    for (int w = 1; w < kSelThreads / 32; ++w) mm = fmaxf(mm, red_m[w]);
-    s_m = mm;
-  }
+  if (lane == 0) red[warp] = v;
   __syncthreads();
-  m = s_m;
-  // fp64 sum of the fp32 exponentials, rounded to fp32
+  float r = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
+  return r;
+}
+
+// Each row is split into `chunks` slices, one CTA per (slice, row).
+struct Slice {
+  int e0, e1;
+};
+__device__ __forceinline__ Slice slice_of(int vocab, int chunks, int c) {
+  const int per = (vocab + chunks - 1) / chunks;
+  return Slice{min(c * per, vocab), min(c * per + per, vocab)};
+}
+
+// Pass 1: each slice's max.
+__global__ void __launch_bounds__(kSelThreads) beam_max_kernel(const void* logits, int64_t row_stride,
+                                                               int elem_bytes, int vocab, int chunks, float inv_t,
+                                                               int scale, float* part_m) {
+  __shared__ float red[kSelThreads / 32];
+  const int c = blockIdx.x, row = blockIdx.y;
+  const char* rp = (const char*)logits + (int64_t)row * row_stride * elem_bytes;
+  const Slice sl = slice_of(vocab, chunks, c);
+  float m = -INFINITY;
+  for (int e = sl.e0 + threadIdx.x; e < sl.e1; e += kSelThreads)
+    m = fmaxf(m, load_logit(rp, e, elem_bytes, inv_t, scale));
+  m = block_max(m, red);
+  if (threadIdx.x == 0) part_m[row * chunks + c] = m;
+}
+
+// Pass 2: each slice's fp64 sum of expf(x - m) with the row max m.
+__global__ void __launch_bounds__(kSelThreads) beam_sum_kernel(const void* logits, int64_t row_stride,
+                                                               int elem_bytes, int vocab, int chunks, float inv_t,
+                                                               int scale, const float* part_m, double* part_s) {
+  __shared__ double red[kSelThreads / 32];
+  const int c = blockIdx.x, row = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const char* rp = (const char*)logits + (int64_t)row * row_stride * elem_bytes;
+  float m = -INFINITY;
+  for (int q = 0; q < chunks; ++q) m = fmaxf(m, part_m[row * chunks + q]);
+  const Slice sl = slice_of(vocab, chunks, c);
   double sum = 0.0;
-  for (int e = tid; e < vocab; e += kSelThreads) sum += (double)expf(load_logit(rp, e, elem_bytes, inv_t, scale) - m);
+  for (int e = sl.e0 + threadIdx.x; e < sl.e1; e += kSelThreads)
+    sum += (double)expf(load_logit(rp, e, elem_bytes, inv_t, scale) - m);
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) red_s[warp] = sum;
+  if (lane == 0) red[warp] = sum;
   __syncthreads();
-  if (tid == 0) {
-    double ss = 0.0;
-    for (int w = 0; w < kSelThreads / 32; ++w) ss += red_s[w];
-    s_s = (float)ss;
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kSelThreads / 32; ++w) t += red[w];
+    part_s[row * chunks + c] = t;
   }
-  __syncthreads();
-  const float s = s_s;
-  const float c = cum ? cum[row] : 0.0f;
+}
+
+// Pass 3: each slice's best k candidates, in order, into lists[(row * chunks + c) * k ..].
+__global__ void __launch_bounds__(kSelThreads) beam_slice_kernel(const void* logits, int64_t row_stride,
+                                                                 int elem_bytes, int vocab, int chunks, float inv_t,
+                                                                 int scale, const float* part_m, const double* part_s,
+                                                                 const float* cum, int k, Cand* lists) {
+  __shared__ float red_m[kSelThreads / 32];
+  __shared__ int red_i[2 * (kSelThreads / 32)];
+  __shared__ Cand heads[kSelThreads];
+  __shared__ int s_winner;
+  const int c = blockIdx.x, row = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const char* rp = (const char*)logits + (int64_t)row * row_stride * elem_bytes;
+  float m = -INFINITY;
+  double ss = 0.0;
+  for (int q = 0; q < chunks; ++q) {                   // the row's max and sum, slices in order
+    m = fmaxf(m, part_m[row * chunks + q]);
+    ss += part_s[row * chunks + q];
+  }
+  const float s = (float)ss;
+  const float cr = cum ? cum[row] : 0.0f;
+  const Slice sl = slice_of(vocab, chunks, c);
   // this thread's best k, sorted (visited in ascending index, so a later
-  // element ties never displace an earlier one)
+  // equal score never displaces an earlier one)
   float ls[kMaxSel];
   int li[kMaxSel];
   float lp[kMaxSel];
@@ -96,7 +139,7 @@ __global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logit
     lp[q] = 0.0f;
   }
   float worst = -INFINITY;                             // ls[k - 1], kept in a register
-  for (int e = tid; e < vocab; e += kSelThreads) {
+  for (int e = sl.e0 + tid; e < sl.e1; e += kSelThreads) {
     const float x = load_logit(rp, e, elem_bytes, inv_t, scale);
     float p = __fdiv_rn(expf(x - m), s);
     if (elem_bytes == 2) p = round_to_bf16(p);
@@ -106,15 +149,13 @@ __global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logit
       if (elem_bytes == 2) a = round_to_bf16(a);
       float l = logf(a);
       if (elem_bytes == 2) l = round_to_bf16(l);
-      score = __fadd_rn(c, l);
+      score = __fadd_rn(cr, l);
     } else {
       score = p;
     }
-    const int idx = row * vocab + e;
-    if (!(score > worst)) continue;                     // strictly better than this thread's k-th
-    // insert, keeping the list sorted
+    if (!(score > worst)) continue;                    // strictly better than this thread's k-th
     float cs = score, cp = p;
-    int ci = idx;
+    int ci = row * vocab + e;
 #pragma unroll
     for (int q = 0; q < kMaxSel; ++q) {
       if (q < k && before(cs, ci, ls[q], li[q])) {
@@ -145,7 +186,6 @@ __global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logit
         hp = lp[q];
       }
     heads[tid] = Cand{hs, hi, hp};
-    // warp best
     float bs = hs;
     int bi = hi, bt = tid;
 #pragma unroll
@@ -161,24 +201,21 @@ __global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logit
     }
     if (lane == 0) {
       red_m[warp] = bs;
-      ((int*)red_s)[2 * warp] = bi;
-      ((int*)red_s)[2 * warp + 1] = bt;
+      red_i[2 * warp] = bi;
+      red_i[2 * warp + 1] = bt;
     }
     __syncthreads();
     if (tid == 0) {
       float ws = red_m[0];
-      int wi = ((int*)red_s)[0], wt = ((int*)red_s)[1];
-      for (int w = 1; w < kSelThreads / 32; ++w) {
-        const float os = red_m[w];
-        const int oi = ((int*)red_s)[2 * w];
-        if (before(os, oi, ws, wi)) {
-          ws = os;
-          wi = oi;
-          wt = ((int*)red_s)[2 * w + 1];
+      int wi = red_i[0], wt = red_i[1];
+      for (int w = 1; w < kSelThreads / 32; ++w)
+        if (before(red_m[w], red_i[2 * w], ws, wi)) {
+          ws = red_m[w];
+          wi = red_i[2 * w];
+          wt = red_i[2 * w + 1];
         }
-      }
       s_winner = wt;
-      rows_out[(int64_t)row * k + r] = heads[wt];
+      lists[((int64_t)row * chunks + c) * k + r] = heads[wt];
     }
     __syncthreads();
     if (tid == s_winner) ++head;
@@ -186,16 +223,20 @@ __global__ void __launch_bounds__(kSelThreads) beam_row_kernel(const void* logit
   }
 }
 
-// One CTA: merges the rows' sorted lists into the k best overall.
-__global__ void __launch_bounds__(32) beam_merge_kernel(const Cand* rows_in, int rows, int k, float* out_score,
-                                                        int64_t* out_index, float* out_prob) {
-  const int lane = threadIdx.x;
-  int head = 0;                                        // lane r < rows follows row r's list
+// One CTA: merges n_lists sorted lists of k (thread i follows list i) into
+// the k best overall.
+__global__ void __launch_bounds__(1024) beam_merge_kernel(const Cand* lists, int n_lists, int k, float* out_score,
+                                                          int64_t* out_index, float* out_prob) {
+  __shared__ float red_m[32];
+  __shared__ int red_i[64];
+  __shared__ int s_winner;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int head = 0;
   for (int r = 0; r < k; ++r) {
     float bs = -INFINITY;
-    int bi = INT_MAX, bl = lane;
-    if (lane < rows && head < k) {
-      const Cand c = rows_in[(int64_t)lane * k + head];
+    int bi = INT_MAX, bt = tid;
+    if (tid < n_lists && head < k) {
+      const Cand c = lists[(int64_t)tid * k + head];
       bs = c.score;
       bi = c.idx;
     }
@@ -203,21 +244,39 @@ __global__ void __launch_bounds__(32) beam_merge_kernel(const Cand* rows_in, int
     for (int o = 16; o; o >>= 1) {
       const float os = __shfl_xor_sync(0xffffffffu, bs, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      const int ot = __shfl_xor_sync(0xffffffffu, bt, o);
       if (before(os, oi, bs, bi)) {
         bs = os;
         bi = oi;
-        bl = ol;
+        bt = ot;
       }
     }
-    if (lane == bl && lane < rows && head < k) {
-      const Cand c = rows_in[(int64_t)lane * k + head];
+    if (lane == 0) {
+      red_m[warp] = bs;
+      red_i[2 * warp] = bi;
+      red_i[2 * warp + 1] = bt;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float ws = red_m[0];
+      int wi = red_i[0], wt = red_i[1];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (before(red_m[w], red_i[2 * w], ws, wi)) {
+          ws = red_m[w];
+          wi = red_i[2 * w];
+          wt = red_i[2 * w + 1];
+        }
+      s_winner = wt;
+    }
+    __syncthreads();
+    if (tid == s_winner && tid < n_lists && head < k) {
+      const Cand c = lists[(int64_t)tid * k + head];
       out_score[r] = c.score;
       out_index[r] = c.idx;
       out_prob[r] = c.prob;
       ++head;
     }
-    __syncwarp();
+    __syncthreads();
   }
 }
 
@@ -239,9 +298,35 @@ __global__ void kv_copy_pages_kernel(char* pool, int64_t layer_bytes, int64_t pa
 
 using namespace pts;
 
+namespace pts {
+namespace {
+// slices per row: about two CTAs per SM of a B200 over all rows, at most 1024 lists to merge
+int beam_chunks(int rows) { return max(1, min(1024 / rows, (296 + rows - 1) / rows)); }
+
+struct BeamWs {
+  float* part_m;
+  double* part_s;
+  Cand* lists;
+  size_t bytes;
+};
+BeamWs beam_ws(void* base, int rows, int k) {
+  const int n = rows * beam_chunks(rows);
+  char* b = (char*)base;
+  BeamWs w;
+  const size_t om = 0, os = align_up(om + (size_t)n * sizeof(float), 256),
+               ol = align_up(os + (size_t)n * sizeof(double), 256);
+  w.part_m = (float*)(b + om);
+  w.part_s = (double*)(b + os);
+  w.lists = (Cand*)(b + ol);
+  w.bytes = align_up(ol + (size_t)n * k * sizeof(Cand), 256);
+  return w;
+}
+}  // namespace
+}  // namespace pts
+
 extern "C" size_t pts_beam_select_workspace_size(int rows, int k) {
   if (rows <= 0 || k <= 0) return 0;
-  return align_up((size_t)rows * k * sizeof(Cand), 256);
+  return beam_ws(nullptr, rows, k).bytes;
 }
 
 extern "C" int pts_beam_select(const void* logits, int64_t row_stride, int elem_bytes, int rows, int vocab,
@@ -255,15 +340,23 @@ extern "C" int pts_beam_select(const void* logits, int64_t row_stride, int elem_
   PTS_CHECK_ARG(k <= rows * vocab, "k above the number of candidates");
   if (k > kMaxSel || rows > 32) return set_error(PTS_ERR_UNSUPPORTED, "beam width %d / %d rows (this build: 16 / 32)", k, rows);
   if ((int64_t)rows * vocab > INT_MAX) return set_error(PTS_ERR_CAPACITY, "rows x vocab above 2^31");
-  if (workspace_bytes < pts_beam_select_workspace_size(rows, k))
-    return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", workspace_bytes,
-                     pts_beam_select_workspace_size(rows, k));
+  const BeamWs w = beam_ws(workspace, rows, k);
+  if (workspace_bytes < w.bytes)
+    return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu", workspace_bytes, w.bytes);
   cudaStream_t st = (cudaStream_t)stream;
   const float inv_t = 1.0f / temperature;
-  beam_row_kernel<<<rows, kSelThreads, 0, st>>>(logits, row_stride, elem_bytes, vocab, inv_t, temperature != 1.0f,
-                                                 cum_log_probs, k, (Cand*)workspace);
-  if (int rc = launch_status("beam_row_kernel")) return rc;
-  beam_merge_kernel<<<1, 32, 0, st>>>((const Cand*)workspace, rows, k, out_score, out_index, out_prob);
+  const int scale = temperature != 1.0f;
+  const int chunks = beam_chunks(rows);
+  const dim3 grid(chunks, rows);
+  beam_max_kernel<<<grid, kSelThreads, 0, st>>>(logits, row_stride, elem_bytes, vocab, chunks, inv_t, scale, w.part_m);
+  if (int rc = launch_status("beam_max_kernel")) return rc;
+  beam_sum_kernel<<<grid, kSelThreads, 0, st>>>(logits, row_stride, elem_bytes, vocab, chunks, inv_t, scale, w.part_m,
+                                                 w.part_s);
+  if (int rc = launch_status("beam_sum_kernel")) return rc;
+  beam_slice_kernel<<<grid, kSelThreads, 0, st>>>(logits, row_stride, elem_bytes, vocab, chunks, inv_t, scale,
+                                                   w.part_m, w.part_s, cum_log_probs, k, w.lists);
+  if (int rc = launch_status("beam_slice_kernel")) return rc;
+  beam_merge_kernel<<<1, 1024, 0, st>>>(w.lists, rows * chunks, k, out_score, out_index, out_prob);
   return launch_status("beam_merge_kernel");
 }
 
