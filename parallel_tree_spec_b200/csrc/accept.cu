@@ -1433,8 +1433,20 @@ __device__ __forceinline__ Part shfl_part(const Part& x, int src_lane_xor) {
   return o;
 }
 
+// Zeroes the workspace's counters and flags ahead of an acceptance launch
+// (launched as a programmatic dependent: it waits for the previous kernel,
+// which may be an acceptance on the same workspace, before writing).
+__global__ void zero_ws_kernel(uint32_t* ws, size_t words) {
+  pdl_trigger();
+  pdl_wait();
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += (size_t)gridDim.x * blockDim.x)
+    ws[i] = 0u;
+}
+
 __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const AcceptParams p, const StreamPlan plan) {
   extern __shared__ __align__(128) uint8_t sm[];
+  pdl_trigger();
+  pdl_wait();                           // launched as a programmatic dependent: nothing is read before this
   uint8_t* ring = sm;
   StreamCtl& ctl = *reinterpret_cast<StreamCtl*>(sm + kSCtlOff);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1907,7 +1919,13 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   p.use_temp = (temperature != 1.0f);
   p.inv_temp = 1.0f / temperature;
   p.vec_ok = (((uintptr_t)p.logits & 15) == 0) && (p.row_stride % 8 == 0);
-  PTS_CUDA_TRY(cudaMemsetAsync(ws + orc, 0, need - orc, stream));
+  {
+    const size_t words = (need - orc) / 4;
+    const size_t want = (words + 255) / 256;
+    const int blocks = (int)(want < 148 ? want : 148);
+    PTS_CUDA_TRY(launch_pdl(zero_ws_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, stream,
+                            (uint32_t*)(ws + orc), words));
+  }
   const int sms = stream_sm_count();
   int dev = 0;
   PTS_CUDA_TRY(cudaGetDevice(&dev));
@@ -1936,7 +1954,8 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
         ((kSWalkOff + walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + order_smem_bytes(plan, p.batch);
     if (ssmem <= kMaxDynSmem) {
       if (int rc = ensure_smem_attr((const void*)accept_stream_kernel, ssmem)) return rc;
-      accept_stream_kernel<<<plan.G + plan.walkers, kSThreads, ssmem, stream>>>(p, plan);
+      PTS_CUDA_TRY(launch_pdl(accept_stream_kernel, dim3(plan.G + plan.walkers), dim3(kSThreads), ssmem, stream, p,
+                              plan));
       return launch_status("accept_stream_kernel");
     }
   }

@@ -192,6 +192,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int h = blockIdx.x, b = blockIdx.y, group = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // launched as a programmatic dependent: resident early, reads nothing before
+  // the previous kernel (the tree preparation and K/V append) has completed
+  pdl_wait();
   const int q0 = p.qo_indptr[b];
   const int n_nodes = p.qo_indptr[b + 1] - q0;
   const int rows = n_nodes * p.g;
@@ -868,7 +871,7 @@ static int tree_attn_launch(const void* q, const void* kv_layer, const int32_t* 
   const int groups = (max_qo_len * g + kGroupRows - 1) / kGroupRows;
   if (groups > 65535) return set_error(PTS_ERR_CAPACITY, "%d query rows per request is too many", max_qo_len);
   dim3 grid(num_kv_heads, batch, groups);
-  tree_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(p, kv_map);
+  PTS_CUDA_TRY(launch_pdl(tree_attn_kernel, grid, dim3(kThreads), kSmemBytes, (cudaStream_t)stream, p, kv_map));
   return launch_status("tree_attn_kernel");
 }
 

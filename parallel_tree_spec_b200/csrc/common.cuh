@@ -52,6 +52,31 @@ inline int launch_status(const char* what) {
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may be
+// scheduled while the stream's previous kernel is still running (once every
+// CTA of that kernel has called pdl_trigger or exited); it runs its setup and
+// then calls pdl_wait, which returns when the previous kernel has completed
+// and its memory is visible.  Nothing before pdl_wait may read or write memory
+// that earlier work in the stream writes or reads.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t b16) {
   return __uint_as_float(b16 << 16);
 }

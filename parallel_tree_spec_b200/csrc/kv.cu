@@ -246,6 +246,8 @@ __global__ void tree_prepare_append_kernel(const int32_t* __restrict__ parents, 
                                            int max_pages, RopeArgs rope) {
   __shared__ int16_t sp[PTS_MAX_TREE_NODES];
   __shared__ int32_t sq[kPrepSmemIndptr + 1];
+  pdl_trigger();                                       // the attention launch may get its SMs ready
+  pdl_wait();                                          // the previous step's writes (compaction) are done
   if ((int)blockIdx.x < batch) {
     const int b = blockIdx.x;
     const int base = qo_indptr[b], n = qo_indptr[b + 1] - base;
@@ -532,10 +534,11 @@ extern "C" int pts_tree_prepare_append(const int32_t* parents, const int32_t* qo
                 "token strides must be multiples of 16 bytes");
   PTS_CHECK_ARG((((uintptr_t)k | (uintptr_t)v | (uintptr_t)kv_layer) & 15) == 0, "pointers must be 16-byte aligned");
   PTS_CHECK_ARG((int64_t)batch + num_tokens <= 0x7fffffff, "too many blocks");
-  tree_prepare_append_kernel<false, 2><<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
-      parents, qo_indptr, seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
-      (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer, page_indptr,
-      page_indices, row_bytes, page_len, max_pages, RopeArgs{});
+  PTS_CUDA_TRY(launch_pdl(tree_prepare_append_kernel<false, 2>, dim3(batch + num_tokens), dim3(128), 0,
+                          (cudaStream_t)stream, parents, qo_indptr, seq_lens, batch, mask_words, mask_bits,
+                          batch_indices, positions, (const char*)k, (const char*)v, (int64_t)k_token_stride * elem_bytes,
+                          (int64_t)v_token_stride * elem_bytes, (char*)kv_layer, page_indptr, page_indices, row_bytes,
+                          page_len, max_pages, RopeArgs{}));
   return launch_status("tree_prepare_append_kernel");
 }
 
@@ -573,10 +576,10 @@ extern "C" int pts_tree_prepare_append_rope(const int32_t* parents, const int32_
   r.cs_stride = cos_sin_token_stride * elem_bytes;
   r.head_dim = head_dim;
   auto kernel = elem_bytes == 2 ? tree_prepare_append_kernel<true, 2> : tree_prepare_append_kernel<true, 4>;
-  kernel<<<batch + num_tokens, 128, 0, (cudaStream_t)stream>>>(
-      parents, qo_indptr, seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
-      (const char*)v, k_token_stride * elem_bytes, v_token_stride * elem_bytes, (char*)kv_layer, page_indptr,
-      page_indices, row_bytes, page_len, max_pages, r);
+  PTS_CUDA_TRY(launch_pdl(kernel, dim3(batch + num_tokens), dim3(128), 0, (cudaStream_t)stream, parents, qo_indptr,
+                          seq_lens, batch, mask_words, mask_bits, batch_indices, positions, (const char*)k,
+                          (const char*)v, (int64_t)k_token_stride * elem_bytes, (int64_t)v_token_stride * elem_bytes,
+                          (char*)kv_layer, page_indptr, page_indices, row_bytes, page_len, max_pages, r));
   return launch_status("tree_prepare_append_kernel");
 }
 
