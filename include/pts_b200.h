@@ -409,13 +409,29 @@ int pts_tree_mask_from_bool(const uint8_t* mask, const int32_t* qo_indptr, const
  * sees slots up to kv_len_b - N_b + i: prefill and decode).  kv_len_b = (page_indptr[b+1]-page_indptr[b]-1) *
  * page_len + last_page_len[b].  Replaces BatchPrefillWithPagedKVCacheWrapper
  * plan/run with custom_mask, causal=False (flashinfer/attention_wrapper.py:
- * 131-144, 250-252).  head_dim 128, page_len 16, Hq/Hkv = 4 in this build. */
+ * 131-144, 250-252).  head_dim 128, page_len 16, Hq/Hkv = 4 in this build.
+ *
+ * Workspace: zeroed before its first use, 256-byte aligned, used by one
+ * stream at a time.  With at least pts_tree_attn_workspace_size bytes (about
+ * 40 MB on a 148-SM part: two partial-result slots per SM) the kernel may run
+ * the balanced schedule -- one CTA per SM over equal ranges of 64-token KV
+ * blocks, units cut by a range merged by their last CTA -- and leaves the
+ * workspace zeroed again after every complete launch; with 256 bytes it runs
+ * one CTA per (request, KV head, group of 264 query rows). */
 size_t pts_tree_attn_workspace_size(int batch, int total_q, int num_qo_heads, int head_dim,
                                     int max_kv_len);
 /* The error word pts_tree_attn_run* leave in `workspace` when a CTA gave up
  * waiting (0: none; nonzero: which wait).  Synchronises the stream, copies the
- * word to *status and clears it in the workspace. */
+ * word to *status and clears it in the workspace, together with the counters
+ * and flags of split units that an abandoned balanced launch left behind. */
 int pts_tree_attn_check(void* workspace, int* status, pts_stream_t stream);
+/* Process-wide choice of the attention schedule: 0 (the default) chooses per
+ * launch from its sizes (balanced ranges only where units would leave many
+ * SMs idle, e.g. a few long requests), 1 always one CTA per unit, 2 balanced
+ * ranges whenever the workspace allows.  Returns the previous choice, or -1
+ * for a value outside 0-2.  No counterpart in the reference (FlashInfer plans
+ * its own split-KV schedule inside BatchPrefillWithPagedKVCacheWrapper.plan). */
+int pts_tree_attn_set_schedule(int mode);
 
 int pts_tree_attn_run(const void* q, const void* kv_layer, const int32_t* qo_indptr,
                       const int32_t* page_indptr, const int32_t* page_indices,

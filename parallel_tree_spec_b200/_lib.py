@@ -39,6 +39,7 @@ SIGNATURES = {
     "pts_version": (C.c_int, []),
     "pts_set_wait_limit": (C.c_longlong, [C.c_longlong]),
     "pts_tree_attn_check": (C.c_int, [vp, vp, vp]),
+    "pts_tree_attn_set_schedule": (C.c_int, [C.c_int]),
     "pts_accept_workspace_size": (sz, [C.c_int, C.c_int]),
     "pts_accept_greedy": (C.c_int, [vp, i64, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, i64, vp, vp, vp,
                                     C.c_int, vp, sz, vp]),

@@ -105,6 +105,10 @@ struct AcceptParams {
   // KV compaction of the accepted paths by the walks (pts_accept_*_compact)
   int compact;
   pts_kv_compact_args cp;
+  // stream order export (top-p): position -> row, and the rows' flags of the
+  // next pass cleared
+  int32_t* order_out;
+  unsigned* order_done;
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -1607,6 +1611,21 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
     }
   }
   __syncthreads();
+  if (p.order_out && streams) {
+    // the order for the next pass (every position once over the CTAs), and
+    // its per-row flags cleared
+    for (int k = tid; k < plan.whole_rows(c); k += kSThreads) {
+      const int r = mine[k];
+      p.order_out[c + k * plan.G] = r;
+      p.order_done[r] = 0u;
+    }
+    if (c == 0)
+      for (int i = tid; i < plan.num_rows - plan.split_first_row; i += kSThreads) {
+        const int r = split[i];
+        p.order_out[plan.split_first_row + i] = r;
+        p.order_done[r] = 0u;
+      }
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer

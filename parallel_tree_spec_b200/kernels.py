@@ -622,6 +622,19 @@ def set_wait_limit(cycles: int) -> int:
     return int(_lib.lib().pts_set_wait_limit(int(cycles)))
 
 
+ATTN_SCHEDULE_AUTO, ATTN_SCHEDULE_PER_UNIT, ATTN_SCHEDULE_BALANCED = 0, 1, 2
+
+
+def set_attention_schedule(mode: int) -> int:
+    """Process-wide attention schedule (pts_tree_attn_set_schedule): 0 chooses
+    per launch, 1 one CTA per (request, KV head, row group), 2 balanced block
+    ranges over one CTA per SM.  Returns the previous choice."""
+    prev = int(_lib.lib().pts_tree_attn_set_schedule(int(mode)))
+    if prev < 0:
+        raise ValueError(f"attention schedule {mode}: expected 0, 1 or 2")
+    return prev
+
+
 # ------------------------------------------------------------ sparse page sets
 def page_key_sums(kv_layer: torch.Tensor, page_ids: torch.Tensor) -> torch.Tensor:
     """Per page and KV head the fp32 sum of its keys: [n, Hkv, D] float32

@@ -40,6 +40,10 @@ def test_host_side_argument_checks_need_no_gpu():
     assert lib.pts_accept_workspace_size(1040, 128256) > 0
 
 
+# entries that set a process-wide choice and return the previous one
+_SETTERS = {"pts_tree_attn_set_schedule"}
+
+
 def test_every_entry_rejects_null_pointers_on_the_host():
     """Every status-returning entry, given null pointers and sizes of 1,
     returns PTS_ERR_INVALID from its host-side checks, before any CUDA call
@@ -47,7 +51,7 @@ def test_every_entry_rejects_null_pointers_on_the_host():
     lib = _lib.lib()
     checked = 0
     for name, (res, args) in sorted(_lib.SIGNATURES.items()):
-        if res is not C.c_int or not args:
+        if res is not C.c_int or not args or name in _SETTERS:
             continue
         vals = [None if a is C.c_void_p else 1.0 if a in (C.c_float, C.c_double) else 1 for a in args]
         rc = getattr(lib, name)(*vals)
@@ -65,3 +69,14 @@ def test_wait_limit_setting_round_trips():
     assert lib.pts_set_wait_limit(5000) == default
     assert lib.pts_set_wait_limit(-1) == 5000
     assert lib.pts_set_wait_limit(0) == default
+
+
+def test_attention_schedule_setting_round_trips():
+    """pts_tree_attn_set_schedule returns the previous choice and rejects values
+    outside 0-2 with -1 (host-side only, no launch)."""
+    lib = _lib.lib()
+    prev = lib.pts_tree_attn_set_schedule(1)
+    assert prev in (0, 1, 2)
+    assert lib.pts_tree_attn_set_schedule(2) == 1
+    assert lib.pts_tree_attn_set_schedule(7) == -1
+    assert lib.pts_tree_attn_set_schedule(prev) == 2
