@@ -1906,7 +1906,7 @@ size_t ws_layout(int num_rows, int vocab, size_t* off_parts, size_t* off_rows, s
 }
 
 int accept_launch(AcceptParams p, int traversal, float temperature, void* workspace, size_t ws_bytes,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, bool* streamed = nullptr) {
   PTS_CHECK_ARG(p.logits && p.row_indptr && p.parents && p.tokens, "null input pointer");
   PTS_CHECK_ARG(p.parts_out ? (p.tok_logit_out != nullptr) : (p.out_tokens && p.out_hidden && p.out_counts),
                 "null output pointer");
@@ -1975,6 +1975,7 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
       if (int rc = ensure_smem_attr((const void*)accept_stream_kernel, ssmem)) return rc;
       PTS_CUDA_TRY(launch_pdl(accept_stream_kernel, dim3(plan.G + plan.walkers), dim3(kSThreads), ssmem, stream, p,
                               plan));
+      if (streamed) *streamed = true;
       return launch_status("accept_stream_kernel");
     }
   }
@@ -2034,14 +2035,13 @@ __device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uin
 // below 2^53 u.  The pass checks that bound (with a margin far above its own
 // rounding) and otherwise walks the window in order on one thread, as the rule
 // states.
-__global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p, float top_p, float* thresh,
-                                                             float* mass) {
+__device__ void topp_row(const AcceptParams& p, float top_p, float* thresh, float* mass, int row) {
   __shared__ uint32_t cnt[kToppMaxWindow];               // index i: key hi_key - i (descending values)
   __shared__ double wtot[kToppThreads / 32];
   __shared__ int s_cross, s_last, s_done;
   __shared__ float s_t;
   __shared__ double s_cum, s_pre;
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowStat rs = p.row_ws[row];
   const uint16_t* rp = p.logits + (int64_t)row * p.row_stride;
   const double target = (double)top_p * (double)rs.s;
@@ -2189,6 +2189,54 @@ __global__ void __launch_bounds__(kToppThreads) topp_kernel(const AcceptParams p
   if (tid == 0) {
     thresh[row] = s_t;                       // -inf: the whole row, when rounding keeps the mass below the target
     mass[row] = (float)s_cum;
+  }
+}
+
+// The nucleus pass with the walks running alongside it.  CTAs 0 .. walkers-1
+// walk request b = blockIdx.x lazily (warp 0 walks, warp 1 expands the nodes
+// whose rows are done), as the streaming kernel's walker CTAs do; the other
+// CTAs take the rows in the order `order` lists (the row-statistics pass's
+// stream order: internal rows by depth-first rank first), compute each row's
+// nucleus and raise its flag in `done`, which p.row_done points at.  A walk
+// waits only for the rows it descends through, so it ends shortly after its
+// last such row instead of after the whole pass.
+__global__ void __launch_bounds__(kToppThreads) topp_walk_kernel(const AcceptParams p, float top_p, float* thresh,
+                                                                 float* mass, const int32_t* order, unsigned* done,
+                                                                 int walkers) {
+  extern __shared__ __align__(128) uint8_t wsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if ((int)blockIdx.x < walkers) {
+    if (warp > 1) return;
+    const WalkSmem w = walk_smem(wsm, p.max_nodes);
+    volatile int* ctl = reinterpret_cast<volatile int*>(wsm + ((walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15));
+    const int b = blockIdx.x;
+    if (warp == 0) {
+      const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
+      const bool go = walk_request<true>(p, b, lo, n, w, WarpGroup{}, nullptr);
+      if (lane == 0) {
+        ctl[0] = go ? b : -2;
+        ctl[1] = 0;
+      }
+      named_barrier(1, 64);
+      if (go) walk_traversal_warp<true>(p, b, lo, n, w);
+      if (p.compact) compact_request_warp(p, b);
+      if (lane == 0) ctl[1] = 1;
+    } else {
+      named_barrier(1, 64);
+      const int bb = ctl[0];
+      if (bb >= 0) {
+        const int lo = p.row_indptr[bb];
+        expand_request(p, lo, p.row_indptr[bb + 1] - lo, w, ctl + 1);
+      }
+    }
+    return;
+  }
+  const int k = blockIdx.x - walkers;
+  const int row = order ? order[k] : k;
+  topp_row(p, top_p, thresh, mass, row);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(done + row), "r"(1u) : "memory");
   }
 }
 
@@ -2427,7 +2475,9 @@ __global__ void walk_merged_kernel(const AcceptParams p, const int* ties, int sh
 // (no walks), then the nuclei, then the walks from the finished statistics,
 // then the bonus draws.  The nucleus thresholds and masses follow the main
 // workspace.
-size_t topp_ws_bytes(int num_rows) { return align_up((size_t)num_rows * 8, 256); }
+// Top-p region after the main workspace: per row the nucleus threshold and
+// mass, the stream order of the statistics pass and the nucleus-done flags.
+size_t topp_ws_bytes(int num_rows) { return align_up((size_t)num_rows * 16, 256); }
 
 int accept_traversal_extended(AcceptParams p, float temperature, float top_p, int do_sample, void* workspace,
                               size_t ws_bytes, cudaStream_t stream) {
@@ -2437,13 +2487,23 @@ int accept_traversal_extended(AcceptParams p, float temperature, float top_p, in
   if (!workspace || ws_bytes < need + (topp ? topp_ws_bytes(p.num_rows) : 0))
     return set_error(PTS_ERR_CAPACITY, "workspace of %zu bytes, need %zu (top-p adds %zu)", ws_bytes, need,
                      topp_ws_bytes(p.num_rows));
+  char* ws = (char*)workspace;
+  float* th = (float*)(ws + need);
+  float* ms = th + p.num_rows;
+  int32_t* order = (int32_t*)(ms + p.num_rows);
+  unsigned* done = (unsigned*)(order + p.num_rows);
   AcceptParams stats = p;
   stats.no_walk = 1;
-  int rc = accept_launch(stats, 1, temperature, workspace, ws_bytes, stream);
+  if (topp) {
+    // the streaming pass lists its row order and clears the nucleus flags
+    stats.order_out = order;
+    stats.order_done = done;
+  }
+  bool streamed = false;
+  int rc = accept_launch(stats, 1, temperature, workspace, ws_bytes, stream, &streamed);
   if (rc) return rc;
   // the launch above filled in the workspace pointers and the scaling
   AcceptParams q = p;
-  char* ws = (char*)workspace;
   q.part_ws = (Part*)(ws + opt);
   q.row_ws = (RowStat*)(ws + orw);
   q.row_ctr = (unsigned*)(ws + orc);
@@ -2455,13 +2515,22 @@ int accept_traversal_extended(AcceptParams p, float temperature, float top_p, in
   q.inv_temp = 1.0f / temperature;
   q.stats_ready = 1;
   if (topp) {
-    float* th = (float*)(ws + need);
-    float* ms = th + p.num_rows;
-    topp_kernel<<<p.num_rows, kToppThreads, 0, stream>>>(q, top_p, th, ms);
-    rc = launch_status("topp_kernel");
-    if (rc) return rc;
+    // the nuclei, with the walks following the rows they need as they finish
+    if (!streamed) PTS_CUDA_TRY(cudaMemsetAsync(done, 0, (size_t)p.num_rows * sizeof(unsigned), stream));
     q.topp_thresh = th;
     q.topp_mass = ms;
+    q.row_done = done;
+    q.stats_ready = 0;
+    const size_t smem = ((walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + 16;
+    if (smem > kMaxDynSmem - 20 * 1024) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
+    if (int rc = ensure_smem_attr((const void*)topp_walk_kernel, smem)) return rc;
+    topp_walk_kernel<<<p.batch + p.num_rows, kToppThreads, smem, stream>>>(q, top_p, th, ms,
+                                                                           streamed ? order : nullptr, done, p.batch);
+    rc = launch_status("topp_walk_kernel");
+    if (rc || !do_sample) return rc;
+    q.stats_ready = 1;
+    sample_bonus_kernel<<<p.batch, 1024, 0, stream>>>(q);
+    return launch_status("sample_bonus_kernel");
   }
   const size_t smem = walk_smem_bytes(p.max_nodes);
   if (smem > kMaxDynSmem) return set_error(PTS_ERR_CAPACITY, "walk state of %zu bytes", smem);
@@ -2871,8 +2940,8 @@ int noalloc_scratch(void** out) {
 // the one array (its counters are cleared at the start of every call), so two
 // calls whose kernels overlap on the same GPU (for example on two streams at
 // once) race and must be serialised by the caller.  Sizes whose scratch
-// exceeds 2 MiB (about 292 bytes per tree row at a 262144-entry vocabulary,
-// so about 7000 rows there) are rejected with PTS_ERR_CAPACITY.
+// exceeds 2 MiB (about 300 bytes per tree row at a 262144-entry vocabulary,
+// so about 6900 rows there) are rejected with PTS_ERR_CAPACITY.
 extern "C" int pts_accept_traversal_noalloc(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
                                             const int32_t* parents, const int32_t* tokens, const float* draft_probs,
                                             int batch, int num_rows, int vocab, int max_nodes, int64_t eos_token_id,
