@@ -1300,8 +1300,8 @@ __host__ __device__ inline size_t order_smem_bytes(const StreamPlan& pl, int bat
   const size_t base = (size_t)pl.mask_words * 4 + (((size_t)pl.whole_rows_per_cta * 2 + 15) & ~(size_t)15) +
                       (((size_t)(pl.num_rows - pl.split_first_row) * 2 + 15) & ~(size_t)15) + 32 * 4 +
                       (batch < kSmemIndptr ? (size_t)(batch + 1) * 4 : 0);
-  return pl.dfs ? ((base + 7) & ~(size_t)7) + (size_t)pl.num_rows * 12 + (size_t)batch * 4 +
-                       (size_t)(kDfsMaxNodes + 1) * 4 + 16
+  return pl.dfs ? ((base + 7) & ~(size_t)7) + (size_t)pl.num_rows * 14 + (size_t)batch * 4 +
+                       (size_t)(kDfsMaxNodes + 1) * 8 + 32
                  : base;
 }
 
@@ -1477,6 +1477,9 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   int16_t* orank = spar + plan.num_rows;                         // internal rows: preorder rank
   int* rank_base = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(orank + plan.num_rows) + 3) & ~(uintptr_t)3);
   // rank_base[k]: the internal rows of rank below k over all requests (sum of min(nint, k))
+  uint32_t* gtmask = reinterpret_cast<uint32_t*>(rank_base + kDfsMaxNodes + 1);
+  // gtmask[k] (batches of at most 32): bit b set when request b has more than k internal rows
+  int16_t* rreq = reinterpret_cast<int16_t*>(gtmask + kDfsMaxNodes + 1);   // dfs: the request of each row
 
   if (tid == 0) {
     for (int i = 0; i < kSSlots; ++i) {
@@ -1492,15 +1495,23 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   }
   // ---- stream order (every streaming CTA computes it for its own rows) -------
   if (streams) {
+    // this thread's first two parents load while the row_indptr copy lands
+    int pre[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) pre[u] = tid + u * kSThreads < plan.num_rows ? p.parents[tid + u * kSThreads] : -1;
     for (int i = tid; i < plan.mask_words; i += kSThreads) imask[i] = 0u;
     __syncthreads();
-    for (int j = tid; j < plan.num_rows; j += kSThreads) {
-      const int lo = request_first_row(indptr, p.batch, j);
-      const int pj = p.parents[j];
+    for (int j = tid, u = 0; j < plan.num_rows; j += kSThreads, ++u) {
+      const int b = request_index(indptr, p.batch, j);
+      const int lo = indptr[b];
+      const int pj = u < 2 ? pre[u] : p.parents[j];
       const bool has = j > lo && pj >= 0 && pj < j - lo;
       const int r = (j == lo) ? j : (has ? lo + pj : -1);
       if (r >= 0) atomicOr(&imask[r >> 5], 1u << (r & 31));
-      if (plan.dfs) spar[j] = (int16_t)(has ? pj : -1);
+      if (plan.dfs) {
+        spar[j] = (int16_t)(has ? pj : -1);
+        rreq[j] = (int16_t)b;
+      }
     }
     __syncthreads();
     if (plan.dfs) {
@@ -1558,8 +1569,14 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       __syncthreads();
       for (int k = tid; k <= kDfsMaxNodes; k += kSThreads) {
         int sum = 0;
-        for (int b2 = 0; b2 < p.batch; ++b2) sum += min(nint[b2], k);
+        uint32_t gt = 0u;
+        for (int b2 = 0; b2 < p.batch; ++b2) {
+          const int nb = nint[b2];
+          sum += min(nb, k);
+          if (b2 < 32 && nb > k) gt |= 1u << b2;
+        }
         rank_base[k] = sum;
+        gtmask[k] = gt;
       }
       __syncthreads();
     }
@@ -1592,7 +1609,7 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
       int q = in ? ib : n_int + (r - ib);
       if (in && plan.dfs) {
         // the internal rows go rank by rank, requests in order within a rank
-        const int b = request_index(indptr, p.batch, r);
+        const int b = rreq[r];
         const int k = orank[r];
         if (k <= kDfsMaxNodes) {
           q = rank_base[k];
@@ -1600,7 +1617,11 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
           q = 0;
           for (int b2 = 0; b2 < p.batch; ++b2) q += min(nint[b2], k);
         }
-        for (int b2 = 0; b2 < b; ++b2) q += nint[b2] > k ? 1 : 0;
+        if (p.batch <= 32 && k <= kDfsMaxNodes) {
+          q += __popc(gtmask[k] & ((1u << b) - 1u));
+        } else {
+          for (int b2 = 0; b2 < b; ++b2) q += nint[b2] > k ? 1 : 0;
+        }
       }
       ib += in;
       if (q < plan.split_first_row) {
