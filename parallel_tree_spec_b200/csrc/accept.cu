@@ -1743,23 +1743,36 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
                                                                       : -INFINITY;
       if (__any_sync(0xffffffffu, mt > w_m && mt >= cmax)) {
         const float wm = key_float(__reduce_max_sync(0xffffffffu, float_key(mt)));
-        // branchless scan from the last value to the first: the smallest index
-        // holding wm wins (padding is -inf and never equals the finite wm)
-        int fi = INT_MAX;
-#pragma unroll
-        for (int q = kSVec - 1; q >= 0; --q) {
-#pragma unroll
-          for (int j = 3; j >= 0; --j) {
-            const int e = base + (q * kSConsumers + ct) * 8 + 2 * j;
-            const uint32_t u = v[4 * q + j];
-            fi = (__uint_as_float(u & 0xffff0000u) == wm) ? e + 1 : fi;
-            fi = (__uint_as_float(u << 16) == wm) ? e : fi;
-          }
-        }
-        w_m = wm;
-        w_idx = (int)__reduce_min_sync(0xffffffffu, (unsigned)fi);
+        // claim the value first: a warp whose max is already below one
+        // another warp has claimed skips the scan (its max is not the
+        // segment's), so of the warps that raise their max on the same chunk
+        // only those at the running maximum scan
+        unsigned long long prev = 0ull;
         if (lane == 0)
-          atomicMax(&ctl.seg_max, ((unsigned long long)(unsigned)(seg + 1) << 32) | ((unsigned)float_key(wm) ^ 0x80000000u));
+          prev = atomicMax(&ctl.seg_max,
+                           ((unsigned long long)(unsigned)(seg + 1) << 32) | ((unsigned)float_key(wm) ^ 0x80000000u));
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        const float claimed =
+            (unsigned)(prev >> 32) == (unsigned)(seg + 1) ? key_float((int)((unsigned)prev ^ 0x80000000u)) : -INFINITY;
+        w_m = wm;
+        if (wm >= claimed) {
+          // branchless scan from the last value to the first: the smallest
+          // index holding wm wins (padding is -inf and never equals the finite wm)
+          int fi = INT_MAX;
+#pragma unroll
+          for (int q = kSVec - 1; q >= 0; --q) {
+#pragma unroll
+            for (int j = 3; j >= 0; --j) {
+              const int e = base + (q * kSConsumers + ct) * 8 + 2 * j;
+              const uint32_t u = v[4 * q + j];
+              fi = (__uint_as_float(u & 0xffff0000u) == wm) ? e + 1 : fi;
+              fi = (__uint_as_float(u << 16) == wm) ? e : fi;
+            }
+          }
+          w_idx = (int)__reduce_min_sync(0xffffffffu, (unsigned)fi);
+        } else {
+          w_idx = kNotCandidate;
+        }
       }
       if (seg_end) {
         // the warp's partial of the segment: sums relative to the warp max; the
