@@ -2056,6 +2056,72 @@ __device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uin
   return __float_as_uint(load_scaled(p, row, e)) >> 16;
 }
 
+// Counts a window of positive values over a row of nv 16-byte groups: every
+// bf16 bit pattern b in [hi - span, hi] adds one to cnt[hi - b].  Such a
+// window is one contiguous range of bit patterns that no negative value (and
+// no -inf padding) reaches, so i = hi - b (unsigned) is in the window exactly
+// when i <= span.  Every value takes one shared-memory increment, with no
+// branch: a value outside the window goes to slot span + 1 + lane past the
+// window (cnt holds 32 slots more than the widest window; they are never
+// read), one bank per lane, so those increments do not conflict with each
+// other.  (Increments predicated off instead measured slower.)  Two sets of
+// four groups per thread alternate: the next set's loads are in flight while
+// the current set is counted.
+template <int kGroups>
+__device__ __forceinline__ void load_groups(uint4 (&x)[kGroups], const uint16_t* rp, int v0, int nv) {
+#pragma unroll
+  for (int u = 0; u < kGroups; ++u) {
+    // groups past the row read as -inf (never counted); the load is
+    // predicated off for them rather than branched around
+    const int vi = v0 + u * kToppThreads;
+    const uint16_t* src = rp + (int64_t)min(vi, nv - 1) * 8;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\t"
+        "setp.lt.s32 q, %4, %5;\n\t"
+        "mov.b32 %0, 0xff80ff80;\n\tmov.b32 %1, 0xff80ff80;\n\t"
+        "mov.b32 %2, 0xff80ff80;\n\tmov.b32 %3, 0xff80ff80;\n\t"
+        "@q ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%6];\n\t}"
+        : "=r"(x[u].x), "=r"(x[u].y), "=r"(x[u].z), "=r"(x[u].w)
+        : "r"(vi), "r"(nv), "l"(src));
+  }
+}
+
+template <bool kTemp>
+__device__ __forceinline__ void count_pos_window(const uint16_t* rp, int nv, uint32_t hi, uint32_t span, float inv_t,
+                                                 uint32_t* cnt) {
+  constexpr int kGroups = 4;
+  const uint32_t dummy = span + 1u + (threadIdx.x & 31u);
+  auto count = [&](const uint4 (&x)[kGroups]) {
+#pragma unroll
+    for (int u = 0; u < kGroups; ++u) {
+      uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (kTemp) w[k] = scale_pair(w[k], inv_t);
+        atomicAdd(&cnt[min(hi - (w[k] & 0xffffu), dummy)], 1u);
+        atomicAdd(&cnt[min(hi - (w[k] >> 16), dummy)], 1u);
+      }
+    }
+  };
+  uint4 a[kGroups], b[kGroups];
+  constexpr int kStep = kGroups * kToppThreads;
+  int v0 = threadIdx.x;
+  if (v0 >= nv) return;
+  load_groups(a, rp, v0, nv);
+  for (;;) {
+    v0 += kStep;
+    const bool more_b = v0 < nv;
+    if (more_b) load_groups(b, rp, v0, nv);
+    count(a);
+    if (!more_b) break;
+    v0 += kStep;
+    const bool more_a = v0 < nv;
+    if (more_a) load_groups(a, rp, v0, nv);
+    count(b);
+    if (!more_a) break;
+  }
+}
+
 // One CTA per row.  Each pass counts the occurrences of every distinct value
 // in a window of keys below the previous one (the first window holds the row
 // max and the 255 values below it; later windows are wider), then takes the
@@ -2070,7 +2136,7 @@ __device__ __forceinline__ uint32_t scaled_bits(const AcceptParams& p, const uin
 // rounding) and otherwise walks the window in order on one thread, as the rule
 // states.
 __device__ void topp_row(const AcceptParams& p, float top_p, float* thresh, float* mass, int row) {
-  __shared__ uint32_t cnt[kToppMaxWindow];               // index i: key hi_key - i (descending values)
+  __shared__ uint32_t cnt[kToppMaxWindow + 32];               // index i: key hi_key - i (descending values)
   __shared__ double wtot[kToppThreads / 32];
   __shared__ int s_cross, s_last, s_done;
   __shared__ float s_t;
@@ -2120,7 +2186,15 @@ __device__ void topp_row(const AcceptParams& p, float top_p, float* thresh, floa
       }
     };
     int e_tail = 0;
-    if (vec) {
+    if (vec && pos_window) {
+      const int nv = p.vocab / 8;
+      if (p.use_temp) {
+        count_pos_window<true>(rp, nv, hi_bits, span, p.inv_temp, cnt);
+      } else {
+        count_pos_window<false>(rp, nv, hi_bits, span, p.inv_temp, cnt);
+      }
+      e_tail = nv * 8;
+    } else if (vec) {
       const int nv = p.vocab / 8;
       for (int v0 = tid; v0 < nv; v0 += 4 * kToppThreads) {
         uint4 x[4];
@@ -2234,7 +2308,9 @@ __device__ void topp_row(const AcceptParams& p, float top_p, float* thresh, floa
 // nucleus and raise its flag in `done`, which p.row_done points at.  A walk
 // waits only for the rows it descends through, so it ends shortly after its
 // last such row instead of after the whole pass.
-__global__ void __launch_bounds__(kToppThreads) topp_walk_kernel(const AcceptParams p, float top_p, float* thresh,
+// Two CTAs per SM (64 registers a thread): the nucleus rows need the warps more
+// than the walker CTAs need registers.
+__global__ void __launch_bounds__(kToppThreads, 2) topp_walk_kernel(const AcceptParams p, float top_p, float* thresh,
                                                                  float* mass, const int32_t* order, unsigned* done,
                                                                  int walkers) {
   extern __shared__ __align__(128) uint8_t wsm[];
