@@ -286,7 +286,7 @@ class Step:
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
-        self.launches_per_step = 3 if a.mode == "traversal" else 4
+        self.launches_per_step = 3
         pool, lay, P, x = W["pool"], W["layer"], W["page_indptr"], W["logits"]
         self.compact = _lib.KvCompactArgs(pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
                                           W["page_indices"].data_ptr(), W["offsets"].data_ptr(), None, None)
@@ -308,16 +308,13 @@ class Step:
             self.acc_tail = (W["ot"].data_ptr(), W["oh"].data_ptr(), W["oc"].data_ptr(), n, self.acc_ws.data_ptr(),
                              self.acc_ws.numel(), ctypes.byref(self.compact), s)
         else:
-            # greedy walks run on streaming CTAs and end with the stream, so the compaction's copies
-            # would lengthen the launch: it runs as its own launch here
-            self.acc = (L.pts_accept_greedy,
+            # greedy step: the walks reduce the rows on their accepted paths only (the path
+            # chain) and compact their requests' KV in the same launch
+            self.acc = (L.pts_accept_greedy_compact,
                         (x.data_ptr(), x.stride(0), W["qo_indptr"].data_ptr(), W["parents"].data_ptr(),
                          W["tokens"].data_ptr(), B, B * n, a.vocab, n, -1, W["ot"].data_ptr(), W["oh"].data_ptr(),
-                         W["oc"].data_ptr(), n, self.acc_ws.data_ptr(), self.acc_ws.numel(), s))
-            self.comp = (L.pts_kv_compact,
-                         (pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
-                          W["page_indices"].data_ptr(), W["oh"].data_ptr(), n, W["oc"].data_ptr(), 4,
-                          W["offsets"].data_ptr(), B, n, None, None, s))
+                         W["oc"].data_ptr(), n, self.acc_ws.data_ptr(), self.acc_ws.numel(),
+                         ctypes.byref(self.compact), s))
 
     def run(self, ev=None):
         from parallel_tree_spec_b200._lib import check
@@ -331,8 +328,7 @@ class Step:
             check(self.L.pts_accept_traversal_compact(*self.acc_head, self.step_index, *self.acc_tail),
                   "accept+compact")
         else:
-            check(self.acc[0](*self.acc[1]), "accept")
-            check(self.comp[0](*self.comp[1]), "compact")
+            check(self.acc[0](*self.acc[1]), "accept+compact")
         if ev is not None:
             ev[2].record()
         self.step_index += 1
@@ -508,12 +504,14 @@ def mode_record(a, W, device, mode, top_p, steps, peak):
     attn = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
     acc = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
     ab = algorithmic_bytes(b)
+    if mode == "greedy":
+        # the greedy walks read the rows of their accepted paths only: the root and each accepted node
+        ab["accept"] = float((W["oc"][:, 2].double() + 1).sum().item()) * a.vocab * 2
     dom, dom_bytes, dom_us = (("tree_attn_kernel", ab["attention"], attn) if attn >= acc
                               else ("acceptance", ab["accept"], acc))
     return {"workload": workload_name(b), "value": steps / (el / 1e3), "unit": UNIT, "steps": steps,
             "ms_per_step": el / steps,
-            "kernels_us": {"tree_attn": attn, "accept_with_compaction" if mode == "traversal" else
-                           "accept_then_compact": acc},
+            "kernels_us": {"tree_attn": attn, "accept_with_compaction": acc},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": dom_bytes / (dom_us * 1e-6) / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": dom_bytes / (dom_us * 1e-6) / 1e9 / peak,
                          "accept_frac": ab["accept"] / (acc * 1e-6) / 1e9 / peak},
@@ -569,6 +567,10 @@ def run_b200(a):
     e2e["value"] = over_ranks([e2e["value"]], "min", device)[0] * world   # the slowest rank's rate, N times
 
     ab = algorithmic_bytes(a)
+    if a.mode == "greedy":
+        # the greedy walks read the rows of their accepted paths only: the root and each accepted node
+        ab["accept"] = float((W["oc"][:, 2].double() + 1).sum().item()) * a.vocab * 2
+        ab["step"] = ab["kv_read"] + ab["q_o"] + ab["append"] + ab["accept"] + ab["compact"]
     peak, peak_kind = measured_peaks()
     tpeak, tpeak_kind = measured_tensor_peak()
     k_attn = statistics.mean(attn_ms) * 1e-3

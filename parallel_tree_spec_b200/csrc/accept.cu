@@ -109,6 +109,13 @@ struct AcceptParams {
   // next pass cleared
   int32_t* order_out;
   unsigned* order_done;
+  // greedy path chain (greedy_chain_kernel): the walk posts each row it needs
+  // to its request's slot in req_ctr ((sequence << 16) | node); no other row
+  // is reduced.  step_form: set by the compacting entry points (a
+  // verification step, whose row statistics only feed its walks), which lets
+  // accept_launch choose the chain for greedy batches
+  int chain;
+  int step_form;
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -454,6 +461,16 @@ __device__ __forceinline__ int match_child(const WalkSmem& w, const NodeRec& r, 
   return -1;
 }
 
+// Path chain: request b's next row is node `node` of its tree (sequence
+// number seq, counting from 1); 0xffff as the sequence ends the request.
+constexpr unsigned kChainDone = 0xffffu;
+__device__ __forceinline__ void chain_post(const AcceptParams& p, int b, unsigned seq, int node) {
+  if ((threadIdx.x & 31) == 0)
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.req_ctr + b), "r"((seq << 16) | (unsigned)node)
+                 : "memory");
+  __syncwarp();
+}
+
 // Greedy walk (verify_tree_exact, verification.py:185-268), by one warp.
 __device__ void walk_greedy_warp(const AcceptParams& p, int b, int lo, const WalkSmem& w) {
   const int lane = threadIdx.x & 31;
@@ -461,9 +478,11 @@ __device__ void walk_greedy_warp(const AcceptParams& p, int b, int lo, const Wal
   int32_t* oh = p.out_hidden + (int64_t)b * p.out_stride;
   int cur = 0, total = 0, acc = 0, n_out = 0;
   int bonus = -1, last_tok = -1;
+  unsigned seq = 1;                                                   // path chain: requests posted so far
   NodeRec r = w.rec[0];
   while (r.child_cnt > 0) {                                           // :232
     total++;
+    if (p.chain) chain_post(p, b, seq++, cur);
     if (!wait_rows_warp(p, lo + cur)) {
       if (lane == 0) write_counts(p, b, -3, 0, 0, 0);
       return;
@@ -490,6 +509,7 @@ __device__ void walk_greedy_warp(const AcceptParams& p, int b, int lo, const Wal
   }
   if (n_out == 0 || p.eos < 0 || (int64_t)last_tok != p.eos) {        // :257
     if (bonus < 0) {
+      if (p.chain) chain_post(p, b, seq++, cur);
       if (!wait_rows_warp(p, lo + cur)) {
         if (lane == 0) write_counts(p, b, -3, 0, 0, 0);
         return;
@@ -1910,6 +1930,177 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   }
 }
 
+// ---- greedy path chain ------------------------------------------------------
+// A greedy walk reads the statistics of the rows on its accepted path only
+// (the root's, then each accepted node's: at most the tree's depth + 1 rows,
+// verification.py:232-262), so the compacting greedy step reduces exactly
+// those rows, each as soon as its walk asks for it, instead of every row.
+// Request b belongs to group b % groups of gs CTAs; member 0's walker warp
+// runs the unchanged greedy walk (walk_request / walk_greedy_warp with
+// p.chain set: it posts each row it waits for), and the group's 16 reducer
+// warps per CTA split that row's 32 KB chunks over the members: chunk k of
+// the row on member k % gs.  A chunk is reduced with the streaming kernel's
+// consumer arithmetic (the same lanes and values per thread, the same warp
+// reduction and warp-order merge) and published as a partial of a split
+// row; the chunk that arrives last merges the row's partials in chunk order
+// and derives the row statistics (finish_row_warp), so a row's statistics
+// are the ones the streaming kernel gives a split row.  Every wait is
+// bounded: a group that gives up leaves its walk to report -3.
+constexpr int kChainWarps = kSConsumerWarps + 1;   // 16 reducer warps + the walker
+constexpr int kChainThreads = kChainWarps * 32;
+
+// Chunk `k` of row `row` by the 16 reducer warps of the CTA (threads
+// 0..511): the chunk's partial into part_ws; the last chunk of the row to
+// arrive merges the row and publishes its statistics.
+__device__ void chain_reduce_chunk(const AcceptParams& p, int row, int k, int nchunks, Part* wparts) {
+  const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5;
+  const int base = k * kSChunk;
+  const int n_el = min(kSChunk, p.vocab - base);
+  const uint16_t* src = p.logits + (int64_t)row * p.row_stride + base;
+  uint32_t v[kSVec * 4];
+#pragma unroll
+  for (int q = 0; q < kSVec; ++q) {
+    const int vi = q * kSConsumers + ct;
+    uint4 x = make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);   // -inf padding
+    if (vi * 8 < n_el) x = ld_stream(src + (size_t)vi * 8);
+    v[4 * q + 0] = x.x;
+    v[4 * q + 1] = x.y;
+    v[4 * q + 2] = x.z;
+    v[4 * q + 3] = x.w;
+  }
+  if (p.use_temp) {
+#pragma unroll
+    for (int i = 0; i < kSVec * 4; ++i) v[i] = scale_pair(v[i], p.inv_temp);
+  }
+  uint32_t m2 = v[0];
+#pragma unroll
+  for (int i = 1; i < kSVec * 4; ++i) m2 = bf16x2_max(m2, v[i]);
+  const float mt = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u));
+  // this thread's partial of the chunk, as the streaming consumer folds its
+  // first chunk of a segment into an empty partial
+  float m_t = -INFINITY;
+  double s_t = 0.0;
+  if (mt > -INFINITY) {
+    const float mlog = mt * kLog2e;
+    const uint64_t sc2 = f2(kLog2e, kLog2e), nm2 = f2(-mlog, -mlog);
+    uint64_t acc_a = f2(0.0f, 0.0f), acc_b = f2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < kSVec * 4; ++i) {
+      float a, b;
+      f2_split(ffma2(f2(__uint_as_float(v[i] << 16), __uint_as_float(v[i] & 0xffff0000u)), sc2, nm2), a, b);
+      const uint64_t e = f2(ex2_approx(a), ex2_approx(b));
+      if (i & 1) acc_b = fadd2(acc_b, e);
+      else acc_a = fadd2(acc_a, e);
+    }
+    float s0, s1, s2, s3;
+    f2_split(acc_a, s0, s1);
+    f2_split(acc_b, s2, s3);
+    const double st = (double)((s0 + s1) + (s2 + s3));
+    s_t = s_t * (double)ex2_approx((m_t - mt) * kLog2e) + st;
+    m_t = mt;
+  }
+  // the warp's partial: its max, the first index holding it, the sum relative to it
+  const float wmax = key_float(__reduce_max_sync(0xffffffffu, float_key(m_t)));
+  int fi = INT_MAX;
+#pragma unroll
+  for (int q = kSVec - 1; q >= 0; --q) {
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      const int e = base + (q * kSConsumers + ct) * 8 + 2 * j;
+      const uint32_t u = v[4 * q + j];
+      fi = (__uint_as_float(u & 0xffff0000u) == wmax) ? e + 1 : fi;
+      fi = (__uint_as_float(u << 16) == wmax) ? e : fi;
+    }
+  }
+  const int w_idx = (int)__reduce_min_sync(0xffffffffu, (unsigned)fi);
+  double ws = (m_t == -INFINITY) ? 0.0 : s_t * (double)ex2_approx((m_t - wmax) * kLog2e);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+  if (lane == 0) wparts[warp] = (wmax == -INFINITY) ? Part{0.0, -INFINITY, INT_MAX} : Part{ws, wmax, w_idx};
+  named_barrier(2, kSConsumers);
+  if (warp == 0) {
+    // the 16 warp partials, merged pairwise in warp order; the chunk's partial
+    // published; the row's last chunk merges the row
+    Part x = lane < kSConsumerWarps ? wparts[lane] : Part{0.0, -INFINITY, INT_MAX};
+#pragma unroll
+    for (int o = 1; o < kSConsumerWarps; o <<= 1) {
+      const Part y = shfl_part(x, o);
+      x = (lane & o) ? merge(y, x) : merge(x, y);
+    }
+    unsigned prev = 0;
+    if (lane == 0) {
+      p.part_ws[(int64_t)row * nchunks + k] = x;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.row_ctr[row]) : "memory");
+    }
+    if (__shfl_sync(0xffffffffu, prev, 0) == (unsigned)(nchunks - 1)) {
+      if (lane == 0) {
+        const Part* pp = p.part_ws + (int64_t)row * nchunks;
+        x = Part{__ldcg(&pp[0].s), __ldcg(&pp[0].m), __ldcg(&pp[0].idx)};
+        for (int i = 1; i < nchunks; ++i) x = merge(x, Part{__ldcg(&pp[i].s), __ldcg(&pp[i].m), __ldcg(&pp[i].idx)});
+      }
+      finish_row_warp(p, row, x);
+    }
+  }
+  named_barrier(2, kSConsumers);                       // wparts free again
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) greedy_chain_kernel(const AcceptParams p, int gs, int groups) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ Part wparts[kSConsumerWarps];
+  __shared__ int s_cmd[2];
+  pdl_trigger();
+  pdl_wait();                           // launched as a programmatic dependent: nothing is read before this
+  const int c = blockIdx.x, warp = threadIdx.x >> 5;
+  if (c >= groups * gs) return;
+  const int gi = c / gs, m = c % gs;
+  const int nchunks = (p.vocab + kSChunk - 1) / kSChunk;
+  if (warp == kSConsumerWarps) {
+    // ------------------------------------------------------------ walker (member 0)
+    if (m != 0) return;
+    const WalkSmem w = walk_smem(sm, p.max_nodes);
+    for (int b = gi; b < p.batch; b += groups) {
+      const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
+      if (n > 0) chain_post(p, b, 1, 0);               // the root's row: reduced while the tree loads
+      walk_request<false>(p, b, lo, n, w, WarpGroup{}, nullptr);
+      chain_post(p, b, kChainDone, 0);
+    }
+    return;
+  }
+  // -------------------------------------------------------------- reducers
+  int phase = 0;
+  for (int b = gi; b < p.batch; b += groups) {
+    const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
+    unsigned seq = 1;
+    for (;;) {
+      if (threadIdx.x == 0) {
+        // the next request of this walk: sequence seq or later, or the end
+        int cmd = -1;
+        const long long t0 = clock64();
+        for (;;) {
+          unsigned v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.req_ctr + b) : "memory");
+          const unsigned sq = v >> 16;
+          if (sq == kChainDone) break;
+          if (sq >= seq) {
+            seq = sq;
+            cmd = (int)(v & 0xffffu);
+            break;
+          }
+          if (clock64() - t0 > kRowWaitLimit) break;   // the walk reports the rows it does not get
+          __nanosleep(32);
+        }
+        s_cmd[phase] = cmd;
+      }
+      named_barrier(1, kSConsumers);
+      const int cmd = s_cmd[phase];
+      phase ^= 1;
+      if (cmd < 0 || cmd >= n) break;
+      for (int k = m; k < nchunks; k += gs) chain_reduce_chunk(p, lo + cmd, k, nchunks, wparts);
+      ++seq;
+    }
+  }
+}
+
 int stream_sm_count() {
   static int count[256] = {};
   int dev = 0;
@@ -1983,6 +2174,23 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
   int dev = 0;
   PTS_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 256) return set_error(PTS_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  if (p.vec_ok && p.vocab % 8 == 0 && sms > 0 && p.step_form && !p.traversal && !p.parts_out && !p.no_walk &&
+      !p.order_out && p.max_nodes <= 0xffff) {
+    // greedy step: the rows on the accepted paths only, each reduced when its
+    // walk asks for it (greedy_chain_kernel); gs CTAs per request, at most one
+    // per chunk of a row
+    const int gs = max(1, min(nchunks, sms / p.batch));
+    const int groups = min(p.batch, max(1, sms / gs));
+    const size_t smem = walk_smem_bytes(p.max_nodes);
+    if (smem <= kMaxDynSmem - 8 * 1024) {
+      p.chain = 1;
+      if (int rc = ensure_smem_attr((const void*)greedy_chain_kernel, smem)) return rc;
+      PTS_CUDA_TRY(launch_pdl(greedy_chain_kernel, dim3(groups * gs), dim3(kChainThreads), smem, stream, p, gs,
+                              groups));
+      if (streamed) *streamed = true;
+      return launch_status("greedy_chain_kernel");
+    }
+  }
   if (p.vec_ok && p.vocab % 8 == 0 && sms > 0) {
     StreamPlan plan;
     // small traversal batches: one CTA per walk that streams nothing, so the
@@ -2784,6 +2992,10 @@ extern "C" int pts_accept_greedy_compact(const uint16_t* logits, int64_t row_str
   p.out_tokens = out_tokens;
   p.out_hidden = out_hidden;
   p.out_counts = out_counts;
+  // with a compaction the call is a verification step: the greedy walks'
+  // rows are reduced on demand (pts_accept_export_row_stats then covers the
+  // rows the walks read)
+  p.step_form = compact != nullptr;
   return finish_compact(accept_launch(p, 0, 1.0f, workspace, workspace_bytes, (cudaStream_t)stream), p, compact,
                         (cudaStream_t)stream);
 }

@@ -228,3 +228,60 @@ def test_accept_with_compaction_matches_separate_launch(method, B, max_nodes):
     assert torch.equal(nl_a, nl_b) and torch.equal(lp_a, lp_b)
     assert torch.equal(pool_a.view(torch.int16), pool_b.view(torch.int16))
     assert int((oc_a[:, 0] > 1).sum()) > 0          # some paths really move rows
+
+
+@pytest.mark.parametrize("shapes,V,eos_at", [
+    ([(8, 8)] * 16, 128256, None),                  # the benchmark shape
+    ([(8, 8)] * 16, 16384, 3),                      # EOS on an accepted path
+    ([(8, 8)] * 40, 16384, None),                   # 40 requests: fewer CTAs per request
+    ([(1, 24)] * 3, 40000, None),                   # chains (24 rows each), three requests
+    ([(16, 8), (1, 30), (4, 3), (0, 0), (8, 8), (2, 12)] * 3, 50000, None),   # ragged, root-only trees
+    ([(4, 4)] * 200, 8192, None),                   # more requests than SMs
+])
+def test_greedy_step_reduces_path_rows_on_demand(shapes, V, eos_at):
+    """The compacting greedy call reduces only the rows on each accepted path
+    (the path chain).  Tokens, hidden indices, counts, new lengths and pool
+    bytes must equal the greedy call without compaction (every row streamed)
+    followed by pts_kv_compact, and the oracle's greedy walk."""
+    rng = np.random.default_rng(len(shapes) * 7 + V)
+    trees = [wl.make_tree(rng, w, d, V) for w, d in shapes]
+    logits = [wl.make_logits(rng, t, V, plant=0.9) for t in trees]
+    B = len(trees)
+    indptr, par, tok, dp = wl.stack_trees(trees)
+    eos = int(tok[int(indptr[eos_at]) + 2]) if eos_at is not None else None
+    x = bf16(np.concatenate(logits, 0)).to(DEV)
+    mn = max(t.size for t in trees)
+    args = (x, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV), torch.from_numpy(tok).to(DEV))
+    L, Hkv, D, pl = 2, 2, 64, 16
+    prefix = rng.integers(0, 40, size=B)
+    kv_len = prefix + np.array([t.size for t in trees])
+    npages = (kv_len + pl - 1) // pl
+    P = int(npages.sum()) + 3
+    perm = rng.permutation(P)[:int(npages.sum())].astype(np.int32)
+    pind = torch.from_numpy(np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)).to(DEV)
+    pidx = torch.from_numpy(perm).to(DEV)
+    offs = torch.from_numpy(prefix.astype(np.int32)).to(DEV)
+    pool0 = torch.randint(-2 ** 15, 2 ** 15, (L, P, 2, pl, Hkv, D), dtype=torch.int16,
+                          generator=torch.Generator().manual_seed(B)).view(torch.bfloat16).to(DEV)
+    for rep in range(2):                           # twice: the request slots and counters start clean each call
+        pool_a, pool_b = pool0.clone(), pool0.clone()
+        nl_a, lp_a, nl_b, lp_b = (torch.zeros(B, dtype=torch.int32, device=DEV) for _ in range(4))
+        ot_a, oh_a, oc_a = K.accept_greedy(*args, eos_token_id=eos, max_nodes=mn)
+        K.kv_compact(pool_a, pind, pidx, oh_a, oc_a, offs, nl_a, lp_a)
+        ca = K.kv_compact_args(pool_b, pind, pidx, offs, nl_b, lp_b)
+        ot_b, oh_b, oc_b = K.accept_greedy(*args, eos_token_id=eos, max_nodes=mn, compact=ca)
+        torch.cuda.synchronize()
+        assert torch.equal(oc_a, oc_b)
+        for b in range(B):
+            n = int(oc_a[b, 0])
+            assert torch.equal(ot_a[b, :n], ot_b[b, :n]) and torch.equal(oh_a[b, :n], oh_b[b, :n]), b
+        assert torch.equal(nl_a, nl_b) and torch.equal(lp_a, lp_b)
+        assert torch.equal(pool_a.view(torch.int16), pool_b.view(torch.int16))
+    ot_b, oh_b, oc_b = ot_b.cpu().numpy(), oh_b.cpu().numpy(), oc_b.cpu().numpy()
+    for b in (0, B // 2, B - 1):
+        t = trees[b]
+        am, _ = acc.row_stats(logits[b], 1.0)
+        s, h, tl, al = acc.greedy_walk(t.parents, t.tokens, am, eos)
+        n = int(oc_b[b, 0])
+        assert list(ot_b[b, :n]) == s and list(oh_b[b, :n]) == h and (int(oc_b[b, 1]), int(oc_b[b, 2])) == (tl, al)
+    assert int(oc_b[:, 2].sum()) > 0                      # some paths accepted
