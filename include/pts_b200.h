@@ -118,7 +118,12 @@ typedef struct pts_kv_compact_args {
 } pts_kv_compact_args;
 
 /* pts_accept_greedy / pts_accept_traversal followed, in the same launch, by
- * the KV compaction described by *compact (NULL: none). */
+ * the KV compaction described by *compact (NULL: none).  With a compaction
+ * (a verification step) and bf16 rows that start 16-byte aligned with a
+ * vocabulary that is a multiple of 8, the greedy form reduces only the rows
+ * its walks read (each request's root and accepted nodes, verification.py:
+ * 232-262), each when its walk reaches it: the same outputs, and
+ * pts_accept_export_row_stats afterwards covers those rows only. */
 int pts_accept_greedy_compact(const uint16_t* logits, int64_t row_stride, const int32_t* row_indptr,
                               const int32_t* parents, const int32_t* tokens, int batch, int num_rows,
                               int vocab, int max_nodes, int64_t eos_token_id, int32_t* out_tokens,
@@ -141,7 +146,9 @@ int pts_accept_traversal_compact(const uint16_t* logits, int64_t row_stride, con
  * arithmetic the walks use.  The same logits, trees and temperature as that
  * call.  These are _sample_probs(...).argmax() (verification.py:46-77) and
  * probs[parent, token] (verification.py:310-349) as this library computes
- * them, exported for diagnostics and parity measurements. */
+ * them, exported for diagnostics and parity measurements.  After a greedy
+ * call with a compaction, only the rows that call's walks read have
+ * statistics (see pts_accept_greedy_compact). */
 int pts_accept_export_row_stats(const void* workspace, size_t workspace_bytes, const uint16_t* logits,
                                 int64_t row_stride, const int32_t* row_indptr, const int32_t* parents,
                                 const int32_t* tokens, int batch, int num_rows, int vocab,
