@@ -203,6 +203,13 @@ def over_ranks(values, op, device):
     return [float(v) for v in t.tolist()]
 
 
+def attn_workspace(device):
+    """The attention workspace at its full size, so every record may take the
+    balanced schedule when it pays (a smaller one forces one CTA per unit)."""
+    from parallel_tree_spec_b200 import _lib, kernels as K
+    return K.workspace(device, "attn", max(256, _lib.lib().pts_tree_attn_workspace_size(0, 0, 0, 0, 0)))
+
+
 def build_workload(a, device, seed):
     import torch
     from parallel_tree_spec_b200 import kernels as K
@@ -720,7 +727,7 @@ def tp_record(a, world, rank, dev, steps):
     bi = torch.empty(T, dtype=torch.int32, device=dev)
     pos = torch.empty(T, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
-    attn_ws = K.workspace(dev, "attn", 256)
+    attn_ws = attn_workspace(dev)
     s = torch.cuda.current_stream(dev).cuda_stream
     pool = layer.view(1, *layer.shape)
 
@@ -829,7 +836,7 @@ def config3_record(a, dev, steps, peak):
     bi = torch.empty(T, dtype=torch.int32, device=dev)
     pos = torch.empty(T, dtype=torch.int32, device=dev)
     out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
-    attn_ws = K.workspace(dev, "attn", 256)
+    attn_ws = attn_workspace(dev)
     acc_ws = K.workspace(dev, "accept", lib.pts_accept_workspace_size(T, V))
     ot = torch.empty(B, n, dtype=torch.int32, device=dev)
     oh = torch.empty(B, n, dtype=torch.int32, device=dev)
@@ -1159,7 +1166,7 @@ def sparse_record(a, dev, steps, peak):
     bi = torch.empty(T, dtype=torch.int32, device=dev)
     pos = torch.empty(T, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
-    attn_ws = K.workspace(dev, "attn", 256)
+    attn_ws = attn_workspace(dev)
     acc_ws = K.workspace(dev, "accept", L.pts_accept_workspace_size(T, V))
     ot = torch.empty(B, n, dtype=torch.int32, device=dev)
     oh = torch.empty(B, n, dtype=torch.int32, device=dev)

@@ -463,11 +463,15 @@ __device__ __forceinline__ int match_child(const WalkSmem& w, const NodeRec& r, 
 
 // Path chain: request b's next row is node `node` of its tree (sequence
 // number seq, counting from 1); 0xffff as the sequence ends the request.
+// Posts only raise the slot (atomic max), so a late post of a step that was
+// already posted changes nothing.
 constexpr unsigned kChainDone = 0xffffu;
+__device__ __forceinline__ void chain_post_lane(const AcceptParams& p, int b, unsigned seq, int node) {
+  asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(p.req_ctr + b), "r"((seq << 16) | (unsigned)node)
+               : "memory");
+}
 __device__ __forceinline__ void chain_post(const AcceptParams& p, int b, unsigned seq, int node) {
-  if ((threadIdx.x & 31) == 0)
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.req_ctr + b), "r"((seq << 16) | (unsigned)node)
-                 : "memory");
+  if ((threadIdx.x & 31) == 0) chain_post_lane(p, b, seq, node);
   __syncwarp();
 }
 
@@ -1952,7 +1956,9 @@ constexpr int kChainThreads = kChainWarps * 32;
 // Chunk `k` of row `row` by the 16 reducer warps of the CTA (threads
 // 0..511): the chunk's partial into part_ws; the last chunk of the row to
 // arrive merges the row and publishes its statistics.
-__device__ void chain_reduce_chunk(const AcceptParams& p, int row, int k, int nchunks, Part* wparts) {
+__device__ void chain_reduce_chunk(const AcceptParams& p, int b, int lo, int n, int cur, unsigned seq, int k,
+                                   int nchunks, Part* wparts) {
+  const int row = lo + cur;
   const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5;
   const int base = k * kSChunk;
   const int n_el = min(kSChunk, p.vocab - base);
@@ -2039,6 +2045,22 @@ __device__ void chain_reduce_chunk(const AcceptParams& p, int row, int k, int nc
         for (int i = 1; i < nchunks; ++i) x = merge(x, Part{__ldcg(&pp[i].s), __ldcg(&pp[i].m), __ldcg(&pp[i].idx)});
       }
       finish_row_warp(p, row, x);
+      // the walk's next row, posted here instead of after the walker has
+      // read this one: the first child of `cur` (index order, as the walk's
+      // child runs) whose token is the row's argmax, unless that token ends
+      // the path (EOS); no child matches: the walk needs no further row
+      const int tok = __ldcg(&p.row_ws[row].argmax);
+      int match = INT_MAX;
+      if (!(p.eos >= 0 && (int64_t)tok == p.eos)) {
+        for (int i0 = cur + 1; i0 < n && match == INT_MAX; i0 += 32) {
+          const int i = i0 + lane;
+          const bool hit = i < n && __ldg(p.parents + lo + i) == cur && __ldg(p.tokens + lo + i) == tok;
+          const unsigned bal = __ballot_sync(0xffffffffu, hit);
+          if (bal) match = i0 + __ffs(bal) - 1;
+        }
+      }
+      if (lane == 0 && match != INT_MAX) chain_post_lane(p, b, seq + 1, match);
+      __syncwarp();
     }
   }
   named_barrier(2, kSConsumers);                       // wparts free again
@@ -2095,7 +2117,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) greedy_chain_kernel(const Ac
       const int cmd = s_cmd[phase];
       phase ^= 1;
       if (cmd < 0 || cmd >= n) break;
-      for (int k = m; k < nchunks; k += gs) chain_reduce_chunk(p, lo + cmd, k, nchunks, wparts);
+      for (int k = m; k < nchunks; k += gs) chain_reduce_chunk(p, b, lo, n, cmd, seq, k, nchunks, wparts);
       ++seq;
     }
   }

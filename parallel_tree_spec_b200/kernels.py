@@ -686,7 +686,9 @@ def tree_attention_head_pages(q: torch.Tensor, kv_layer: torch.Tensor, qo_indptr
     if out is None:
         out = torch.empty_like(q)
     scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(D)
-    ws = workspace(dev, "attn", 256)
+    # the same workspace as tree_attention, so the two choose their schedule alike
+    wsz = _lib.lib().pts_tree_attn_workspace_size(B, T, Hq, D, int(max_kv_len))
+    ws = workspace(dev, "attn", max(wsz, 256))
     _lib.call("pts_tree_attn_run_head_pages", q.data_ptr(), kv_layer.data_ptr(), _i32(qo_indptr, "qo").data_ptr(),
               _i32(head_indptr, "hi").data_ptr(), _i32(head_indices, "hx").data_ptr(),
               _i32(head_last, "hl").data_ptr(), mask_bits.data_ptr() if mask_bits is not None else None,
