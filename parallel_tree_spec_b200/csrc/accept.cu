@@ -116,6 +116,11 @@ struct AcceptParams {
   // accept_launch choose the chain for greedy batches
   int chain;
   int step_form;
+  // top-p without a sampled bonus: the nucleus of a leaf row is never read
+  // (a node's target probability comes from its parent's row, the bonus is
+  // the row's argmax), so the statistics pass marks leaf rows' nucleus flags
+  // done and the nucleus pass skips them
+  int topp_skip_leaves;
 };
 
 constexpr long long kRowWaitLimit = 4000000000ll;   // clock cycles, about 2 s
@@ -1658,17 +1663,20 @@ __global__ void __launch_bounds__(kSThreads, 1) accept_stream_kernel(const Accep
   __syncthreads();
   if (p.order_out && streams) {
     // the order for the next pass (every position once over the CTAs), and
-    // its per-row flags cleared
+    // its per-row flags cleared (leaf rows' set, when the next pass skips them)
+    auto flag0 = [&](int r) -> unsigned {
+      return (p.topp_skip_leaves && !((imask[r >> 5] >> (r & 31)) & 1u)) ? 1u : 0u;
+    };
     for (int k = tid; k < plan.whole_rows(c); k += kSThreads) {
       const int r = mine[k];
       p.order_out[c + k * plan.G] = r;
-      p.order_done[r] = 0u;
+      p.order_done[r] = flag0(r);
     }
     if (c == 0)
       for (int i = tid; i < plan.num_rows - plan.split_first_row; i += kSThreads) {
         const int r = split[i];
         p.order_out[plan.split_first_row + i] = r;
-        p.order_done[r] = 0u;
+        p.order_done[r] = flag0(r);
       }
   }
 
@@ -2573,6 +2581,7 @@ __global__ void __launch_bounds__(kToppThreads, 2) topp_walk_kernel(const Accept
   }
   const int k = blockIdx.x - walkers;
   const int row = order ? order[k] : k;
+  if (order && __ldcg(done + row)) return;     // a leaf row whose nucleus nothing reads (topp_skip_leaves)
   topp_row(p, top_p, thresh, mass, row);
   if (threadIdx.x == 0) {
     __threadfence();
@@ -2838,6 +2847,7 @@ int accept_traversal_extended(AcceptParams p, float temperature, float top_p, in
     // the streaming pass lists its row order and clears the nucleus flags
     stats.order_out = order;
     stats.order_done = done;
+    stats.topp_skip_leaves = do_sample ? 0 : 1;
   }
   bool streamed = false;
   int rc = accept_launch(stats, 1, temperature, workspace, ws_bytes, stream, &streamed);
