@@ -293,7 +293,11 @@ class Step:
             B, B * n, a.hq, 128, W["kv_len"])))
         self.philox_seed = philox_seed
         self.step_index = 0
-        self.launches_per_step = 3
+        # this library's launches per step: tree preparation with the append, attention (one
+        # launch at the benchmark shapes, where one CTA per unit is the schedule chosen), the
+        # acceptance's workspace zeroing and the acceptance itself (top-p: statistics, then the
+        # nucleus pass with the walks)
+        self.launches_per_step = 4 + (1 if (a.mode == "traversal" and a.top_p < 1.0) else 0)
         pool, lay, P, x = W["pool"], W["layer"], W["page_indptr"], W["logits"]
         self.compact = _lib.KvCompactArgs(pool.data_ptr(), 1, lay.shape[0], 16, a.hkv, 128, 2, P.data_ptr(),
                                           W["page_indices"].data_ptr(), W["offsets"].data_ptr(), None, None)
