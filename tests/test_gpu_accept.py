@@ -248,7 +248,12 @@ def test_greedy_step_reduces_path_rows_on_demand(shapes, V, eos_at):
     logits = [wl.make_logits(rng, t, V, plant=0.9) for t in trees]
     B = len(trees)
     indptr, par, tok, dp = wl.stack_trees(trees)
-    eos = int(tok[int(indptr[eos_at]) + 2]) if eos_at is not None else None
+    eos = None
+    if eos_at is not None:
+        # the token request eos_at's walk accepts first (its root row's argmax, planted on a child):
+        # that walk stops on EOS after one node, with no bonus row
+        am0, _ = acc.row_stats(logits[eos_at], 1.0)
+        eos = int(am0[0])
     x = bf16(np.concatenate(logits, 0)).to(DEV)
     mn = max(t.size for t in trees)
     args = (x, torch.from_numpy(indptr).to(DEV), torch.from_numpy(par).to(DEV), torch.from_numpy(tok).to(DEV))
@@ -285,3 +290,9 @@ def test_greedy_step_reduces_path_rows_on_demand(shapes, V, eos_at):
         n = int(oc_b[b, 0])
         assert list(ot_b[b, :n]) == s and list(oh_b[b, :n]) == h and (int(oc_b[b, 1]), int(oc_b[b, 2])) == (tl, al)
     assert int(oc_b[:, 2].sum()) > 0                      # some paths accepted
+    if eos_at is not None:
+        s, h, tl, al = acc.greedy_walk(trees[eos_at].parents, trees[eos_at].tokens,
+                                       acc.row_stats(logits[eos_at], 1.0)[0], eos)
+        assert int(oc_b[eos_at, 0]) == len(s) and list(ot_b[eos_at, :len(s)]) == s
+        if al == 1:
+            assert s[-1] == eos and len(s) == 1           # stopped on EOS: no bonus token
