@@ -1418,7 +1418,7 @@ __device__ __forceinline__ bool s_mbar_wait(uint64_t* bar, uint32_t parity, uint
 // Row statistics from the row's merged partial `r` (valid in lane 0), by one
 // warp (the warp rescans the row when a value below the max can round to the
 // same probability), stored and published in the workspace.
-__device__ void finish_row_warp(const AcceptParams& p, int row, Part r) {
+__device__ int finish_row_warp(const AcceptParams& p, int row, Part r) {
   const int lane = threadIdx.x & 31;
   float m = 0.0f, sf = 0.0f, qmax = 0.0f;
   int arg = 0, tie = 0;
@@ -1456,6 +1456,7 @@ __device__ void finish_row_warp(const AcceptParams& p, int row, Part r) {
     publish_row(p, row);
   }
   __syncwarp();
+  return arg;                                          // the same in every lane
 }
 
 __device__ __forceinline__ Part shfl_part(const Part& x, int src_lane_xor) {
@@ -1965,7 +1966,7 @@ constexpr int kChainThreads = kChainWarps * 32;
 // 0..511): the chunk's partial into part_ws; the last chunk of the row to
 // arrive merges the row and publishes its statistics.
 __device__ void chain_reduce_chunk(const AcceptParams& p, int b, int lo, int n, int cur, unsigned seq, int k,
-                                   int nchunks, Part* wparts) {
+                                   int nchunks, Part* wparts, const int* tpar, const int* ttok) {
   const int row = lo + cur;
   const int ct = threadIdx.x, lane = ct & 31, warp = ct >> 5;
   const int base = k * kSChunk;
@@ -2052,17 +2053,16 @@ __device__ void chain_reduce_chunk(const AcceptParams& p, int b, int lo, int n, 
         x = Part{__ldcg(&pp[0].s), __ldcg(&pp[0].m), __ldcg(&pp[0].idx)};
         for (int i = 1; i < nchunks; ++i) x = merge(x, Part{__ldcg(&pp[i].s), __ldcg(&pp[i].m), __ldcg(&pp[i].idx)});
       }
-      finish_row_warp(p, row, x);
+      const int tok = finish_row_warp(p, row, x);
       // the walk's next row, posted here instead of after the walker has
       // read this one: the first child of `cur` (index order, as the walk's
       // child runs) whose token is the row's argmax, unless that token ends
       // the path (EOS); no child matches: the walk needs no further row
-      const int tok = __ldcg(&p.row_ws[row].argmax);
       int match = INT_MAX;
       if (!(p.eos >= 0 && (int64_t)tok == p.eos)) {
         for (int i0 = cur + 1; i0 < n && match == INT_MAX; i0 += 32) {
           const int i = i0 + lane;
-          const bool hit = i < n && __ldg(p.parents + lo + i) == cur && __ldg(p.tokens + lo + i) == tok;
+          const bool hit = i < n && tpar[i] == cur && ttok[i] == tok;
           const unsigned bal = __ballot_sync(0xffffffffu, hit);
           if (bal) match = i0 + __ffs(bal) - 1;
         }
@@ -2084,6 +2084,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) greedy_chain_kernel(const Ac
   if (c >= groups * gs) return;
   const int gi = c / gs, m = c % gs;
   const int nchunks = (p.vocab + kSChunk - 1) / kSChunk;
+  // the reducers' copy of the current request's parents and tokens (after the walker's state)
+  int* tpar = reinterpret_cast<int*>(sm + ((walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15));
+  int* ttok = tpar + p.max_nodes;
   if (warp == kSConsumerWarps) {
     // ------------------------------------------------------------ walker (member 0)
     if (m != 0) return;
@@ -2100,6 +2103,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) greedy_chain_kernel(const Ac
   int phase = 0;
   for (int b = gi; b < p.batch; b += groups) {
     const int lo = p.row_indptr[b], n = p.row_indptr[b + 1] - lo;
+    // (every reducer of the previous request is past its last barrier: its
+    // merges are done; the first barrier below publishes these copies)
+    for (int i = threadIdx.x; i < min(n, p.max_nodes); i += kSConsumers) {
+      tpar[i] = __ldg(p.parents + lo + i);
+      ttok[i] = __ldg(p.tokens + lo + i);
+    }
     unsigned seq = 1;
     for (;;) {
       if (threadIdx.x == 0) {
@@ -2124,8 +2133,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) greedy_chain_kernel(const Ac
       named_barrier(1, kSConsumers);
       const int cmd = s_cmd[phase];
       phase ^= 1;
-      if (cmd < 0 || cmd >= n) break;
-      for (int k = m; k < nchunks; k += gs) chain_reduce_chunk(p, b, lo, n, cmd, seq, k, nchunks, wparts);
+      if (cmd < 0 || cmd >= n || n > p.max_nodes) break;
+      for (int k = m; k < nchunks; k += gs) chain_reduce_chunk(p, b, lo, n, cmd, seq, k, nchunks, wparts, tpar, ttok);
       ++seq;
     }
   }
@@ -2211,7 +2220,7 @@ int accept_launch(AcceptParams p, int traversal, float temperature, void* worksp
     // per chunk of a row
     const int gs = max(1, min(nchunks, sms / p.batch));
     const int groups = min(p.batch, max(1, sms / gs));
-    const size_t smem = walk_smem_bytes(p.max_nodes);
+    const size_t smem = ((walk_smem_bytes(p.max_nodes) + 15) & ~(size_t)15) + (size_t)p.max_nodes * 8;
     if (smem <= kMaxDynSmem - 8 * 1024) {
       p.chain = 1;
       if (int rc = ensure_smem_attr((const void*)greedy_chain_kernel, smem)) return rc;
