@@ -671,11 +671,14 @@ def run_e2e(a, W, step, device):
     h2d = hin.numel() * 4
     d2h = hres.numel() * 4
 
+    stream = torch.cuda.current_stream(device)
+    tree_in, res = W["tree_in"], W["res"]
+
     def one():
-        W["tree_in"].copy_(hin, non_blocking=True)
+        tree_in.copy_(hin, non_blocking=True)
         step.run()
-        hres.copy_(W["res"], non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
+        hres.copy_(res, non_blocking=True)
+        stream.synchronize()
 
     for _ in range(3):
         one()
